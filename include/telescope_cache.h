@@ -1,0 +1,310 @@
+/*
+ * telescope_cache.h -- C ABI of the B200 (sm_100a) telescoping-attention
+ * library (libtelescope_b200.so).
+ *
+ * Every entry point takes plain pointers, sizes and a cudaStream_t (passed as
+ * void*), and returns an int status (TC_OK on success).  Device tensors are
+ * dense row-major ("BSHD") buffers:
+ *
+ *   q          [B, N, Hq, Dk]        out   [B, N, Hq, Dv]     lse [B, N, Hq] f32
+ *   packed k   [B, total, Hkv, Dk]   packed v [B, total, Hkv, Dv]
+ *   packed w   [B, total, Hkv]       (total = sum of level lengths N >> l)
+ *
+ * GQA maps query head hq to KV head hq / (Hq / Hkv).  The schedule (fmap,
+ * cache_size, N) is described by tc_schedule, built by tc_schedule_init.
+ *
+ * Each function names the reference interface it replaces (paths inside the
+ * Knarf04/telescope_cache project).
+ */
+#ifndef TELESCOPE_CACHE_H
+#define TELESCOPE_CACHE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TC_MAX_LEVELS 16
+
+/* status codes */
+#define TC_OK 0
+#define TC_ERR_ARG 1          /* invalid argument (shape, schedule, pointer) */
+#define TC_ERR_UNSUPPORTED 2  /* valid, but not supported by this build     */
+#define TC_ERR_CUDA 3         /* a CUDA runtime call or launch failed        */
+#define TC_ERR_SCHEDULE 4     /* fmap not dyadically aligned / not 1..L     */
+
+/* element types */
+#define TC_F32 0
+#define TC_BF16 1
+#define TC_F16 2
+
+/* positional modes (reference.py:675-768) */
+#define TC_POS_NONE 0
+#define TC_POS_ROPE 1
+#define TC_POS_RELATIVE 2
+
+/* device status word bits, OR-ed by kernels into a caller-owned int32 */
+#define TC_DEV_WAIT_TIMEOUT 1  /* a bounded mbarrier wait gave up           */
+#define TC_DEV_BAD_INDEX 2     /* a bounds check rejected an index          */
+
+typedef struct tc_schedule {
+  int32_t num_levels;                  /* L + 1                              */
+  int32_t cache_size;
+  int32_t seq_len;                     /* N                                  */
+  int32_t coarsest_span;               /* range_spec.coarsest_lifetime_span  */
+  int32_t act[TC_MAX_LEVELS];          /* activation times a[0..L]           */
+  int32_t level_len[TC_MAX_LEVELS];    /* N >> l                             */
+  int64_t offsets[TC_MAX_LEVELS + 1];  /* packed level offsets               */
+} tc_schedule;
+
+/* ------------------------------------------------------------------------ */
+/* library                                                                   */
+/* ------------------------------------------------------------------------ */
+
+/* Library version, for the Python loader's sanity check. */
+int tc_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* schedule (host side; pure integer)                                        */
+/* ------------------------------------------------------------------------ */
+
+/* fmap values fmap[1..L] (fmap_vals[i] = fmap[i+1]) -> activation times,
+ * level lengths, packed offsets and the coarsest lifetime span.
+ * Replaces RangeSpec.from_fmap + activation_times_from_fmap +
+ * coarsest_lifetime_span (telescoping_attn/range_spec.py:26-126, :287-317).
+ * Returns TC_ERR_SCHEDULE on keys/alignment errors, TC_ERR_ARG on sizes. */
+int tc_schedule_init(const int32_t* fmap_vals, int32_t num_summary_levels,
+                     int32_t cache_size, int32_t seq_len, tc_schedule* out);
+
+/* Same, from explicit activation times (RangeSpec(activation_times, ...),
+ * range_spec.py:57-76). */
+int tc_schedule_from_times(const int32_t* act, int32_t num_levels, int32_t cache_size,
+                           int32_t seq_len, tc_schedule* out);
+
+/* Visible-set statistics over every query q in [0, N):
+ * out[0] = min_q |A(q)|, out[1] = max_q |A(q)|, out[2] = sum_q |A(q)|.
+ * Lets the host raise the reference's RuntimeError for an empty row
+ * (reference.py:1060-1064) and ValueError for a relative table that is too
+ * small (reference.py:441-452) before any launch. */
+int tc_schedule_stats(const tc_schedule* s, int64_t* out3);
+
+/* Per-level decode ring capacities (reference.py:1739-1772). caps_out has
+ * num_levels entries. Returns TC_ERR_ARG if the fine levels exceed the cache. */
+int tc_decode_caps(const int32_t* act, int32_t num_levels, int32_t cache_size,
+                   int32_t* caps_out);
+
+/* Per-query level bounds [lo, hi) (EMPTY = 0,0) from the branch-free closed
+ * forms, evaluated on the HOST: out[(i * num_levels + l) * 2 + {0,1}].
+ * range_spec.level_row_bounds / range_bounds (range_spec.py:142-171, :324-336). */
+int tc_range_bounds_host(const tc_schedule* s, const int32_t* qs, int32_t n, int32_t* out);
+
+/* Hulls on the HOST: kind 0 = fwd_bounds over query blocks [lo[i], hi[i]),
+ * kind 1 = bwd_bounds over node tiles [lo[i], hi[i]) at `level`.
+ * out[i*2 + {0,1}] (range_spec.py:187-202, :256-281, :360-402). */
+int tc_hulls_host(const tc_schedule* s, int32_t kind, int32_t level, const int32_t* lo,
+                  const int32_t* hi, int32_t n, int32_t* out);
+
+/* ------------------------------------------------------------------------ */
+/* device debug                                                              */
+/* ------------------------------------------------------------------------ */
+
+/* The same per-query bounds, computed by a CUDA kernel (the closed forms the
+ * attention kernels use).  qs/out are DEVICE pointers, layout as above. */
+int tc_range_bounds_device(const tc_schedule* s, const int32_t* qs, int32_t n, int32_t* out,
+                           void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Phase 1: dyadic summary tree                                              */
+/* ------------------------------------------------------------------------ */
+
+typedef struct tc_tree_args {
+  int32_t B, N, Hq, Hkv, Dk, Dv;
+  int32_t num_summary_levels;  /* L (tree has L + 1 levels)                 */
+  int32_t dtype;               /* q/k/v/packed element type                 */
+  int32_t w_dtype;             /* packed w element type                     */
+  const void* q;               /* [B, N, Hq, Dk]  (qk weight mode)          */
+  const void* k;               /* [B, N, Hkv, Dk] pre-conv keys             */
+  const void* v;               /* [B, N, Hkv, Dv]                           */
+  const void* w0;              /* [B, N, Hkv] precomputed level-0 weights
+                                  (linear mode), or NULL for qk mode        */
+  const void* k_conv_w;        /* [Hkv*Dk, K] or NULL                       */
+  const void* v_conv_w;        /* [Hkv*Dv, K] or NULL                       */
+  int32_t conv_dtype;          /* element type of the conv weights          */
+  int32_t conv_k;              /* conv width K (0 = no conv)                */
+  void* k_packed;              /* [B, total, Hkv, Dk] out                   */
+  void* v_packed;              /* [B, total, Hkv, Dv] out                   */
+  void* w_packed;              /* [B, total, Hkv]     out                   */
+  int64_t total;               /* sum_l (N >> l)                            */
+} tc_tree_args;
+
+/* Fused short conv + merge weights + all-level softmax pair merges + packing
+ * into the level-major buffer.  Replaces short_conv, compute_summary_weights,
+ * build_dyadic_summaries and pack_levels (reference.py:117-211, :465-640). */
+int tc_build_tree(const tc_tree_args* a, void* stream);
+
+/* w[b, t, h] = x[b, t, :] . w_proj[h, :] (compute_linear_weights,
+ * reference.py:148-164).  x [rows, E], w_proj [H, E], out [rows, H]. */
+int tc_linear_weights(int64_t rows, int32_t E, int32_t H, int32_t x_dtype, const void* x,
+                      int32_t p_dtype, const void* w_proj, int32_t out_dtype, void* out,
+                      void* stream);
+
+/* w[b, t, hkv] = logsumexp_e(q[b, t, hkv*E + e] . k[b, t, hkv] / sqrt(Dk)),
+ * q [B, N, Hq, Dk], k [B, N, Hkv, Dk], out [B, N, Hkv] (compute_summary_weights,
+ * reference.py:117-145). */
+int tc_qk_weights(int32_t B, int32_t N, int32_t Hq, int32_t Hkv, int32_t Dk, int32_t dtype,
+                  const void* q, const void* k, int32_t out_dtype, void* out, void* stream);
+
+/* Causal depthwise short conv with fp32 taps and fp32 residual, one cast:
+ * y[b, t, c] = x[b, t, c] + sum_j w[c, j] x[b, t - K + 1 + j, c]
+ * (short_conv, reference.py:167-211).  x, y [B, N, C]; w [C, K]. */
+int tc_short_conv(int32_t B, int32_t N, int32_t C, int32_t dtype, const void* x, int32_t K,
+                  int32_t w_dtype, const void* w, void* y, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* positional helpers                                                        */
+/* ------------------------------------------------------------------------ */
+
+/* Rotate-half RoPE of the rows of x [B, S, H, D] into y (same dtype), in
+ * fp32, rounded once to the element type (apply_rope, reference.py:267-302).
+ * pos_kind 0: position of row s is s (query rows);
+ * pos_kind 1: rows are a packed level-major buffer of schedule `sched`,
+ *             position of (level l, node j) is (j + 1) 2^l - 1
+ *             (summary_token_position, reference.py:219-237).
+ * pos_kind 2: positions[B * S * H] (int32, device) give every row's position.
+ * inverse != 0 rotates by -theta. */
+int tc_rope_apply(int32_t B, int64_t S, int32_t H, int32_t D, int32_t dtype, const void* x,
+                  void* y, const float* cos_t, const float* sin_t, int32_t n_pos,
+                  int32_t pos_kind, const tc_schedule* sched, const int32_t* positions,
+                  int32_t inverse, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Phase 2 attention                                                         */
+/* ------------------------------------------------------------------------ */
+
+typedef struct tc_attn_args {
+  int32_t B, N, Hq, Hkv, Dk, Dv;
+  int32_t dtype;            /* q, packed k/v, out, dq, dk, dv element type    */
+  int32_t has_softcap;
+  float softcap;
+  int32_t position_mode;    /* TC_POS_*                                      */
+  const void* q;            /* [B, N, Hq, Dk]   (already rotated for rope)   */
+  const void* k;            /* [B, total, Hkv, Dk] (already rotated)         */
+  const void* v;            /* [B, total, Hkv, Dv]                           */
+  const void* rel_states;   /* [B, N, Hq, d_rel] (relative)                  */
+  const void* rel_proj;     /* [d_rel, rel_bins]                             */
+  int32_t rel_dtype;        /* element type of rel_states and rel_proj       */
+  int32_t d_rel, rel_bins;
+  const float* rope_cos;    /* [n_pos, Dk/2] backward only: the kernels      */
+  const float* rope_sin;    /* rotate dq/dk back by R(-p) in fp32 (rope)     */
+  int32_t rope_npos;
+  void* out;                /* [B, N, Hq, Dv]                                */
+  float* lse;               /* [B, N, Hq]                                    */
+  /* backward only */
+  const void* o;            /* forward out [B, N, Hq, Dv]                    */
+  const void* dout;         /* [B, N, Hq, Dv]                                */
+  const float* dlse;        /* [B, N, Hq] or NULL                            */
+  float* delta;             /* scratch [B, N, Hq] f32                        */
+  void* dq;                 /* [B, N, Hq, Dk]                                */
+  void* dk;                 /* [B, total, Hkv, Dk]                           */
+  void* dv;                 /* [B, total, Hkv, Dv]                           */
+  float* drel;              /* [B, N, Hq, rel_bins] f32, zero-filled by the
+                               caller, or NULL                               */
+  int32_t* dev_status;      /* device status word (TC_DEV_*), or NULL        */
+  int32_t impl;             /* 0 auto, 1 SIMT (any shape, any dtype),
+                               2 tensor core (bf16/f16, Dk = Dv = 128)       */
+} tc_attn_args;
+
+/* Phase-2 forward: (out, lse) over the packed level-major K/V
+ * (multilevel_attention_forward, reference.py:771-1071). */
+int tc_attn_fwd(const tc_attn_args* a, const tc_schedule* s, void* stream);
+
+/* Phase-2 backward: dq, dk_packed, dv_packed and (relative) drel_logits, with
+ * the sink dlse seed folded into Delta (multilevel_attention_backward,
+ * reference.py:1249-1672).  For rope, q and k are passed already rotated
+ * and dq/dk are rotated back by R(-p) in fp32 before the single cast. */
+int tc_attn_bwd(const tc_attn_args* a, const tc_schedule* s, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* post-ops                                                                  */
+/* ------------------------------------------------------------------------ */
+
+/* out_sink = out * (sigmoid(lse - sinks[h]) rounded to out's type)
+ * (apply_attention_sink, reference.py:1082-1122).  rows = B*N. */
+int tc_sink_fwd(int64_t rows, int32_t Hq, int32_t Dv, int32_t dtype, const void* out,
+                const float* lse, int32_t sink_dtype, const void* sinks, void* y,
+                void* stream);
+
+/* (dout_pre, dlse, dsinks) (attention_sink_backward, reference.py:1125-1184).
+ * dsinks_f32 is [Hq] f32 and is overwritten. */
+int tc_sink_bwd(int64_t rows, int32_t Hq, int32_t Dv, int32_t dtype, const void* out,
+                const float* lse, int32_t sink_dtype, const void* sinks, const void* dout,
+                void* dout_pre, float* dlse, float* dsinks_f32, void* stream);
+
+/* y = SiLU(g) * out, g = x @ W_g^T precomputed (apply_output_gate,
+ * reference.py:1187-1219).  n = number of elements. */
+int tc_gate_apply(int64_t n, int32_t dtype, const void* out, int32_t g_dtype, const void* g,
+                  int32_t y_dtype, void* y, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* incremental decode                                                        */
+/* ------------------------------------------------------------------------ */
+
+/* decode step modes */
+#define TC_DECODE_FULL 0     /* advance the state, then attend (decode_step)  */
+#define TC_DECODE_ADVANCE 1  /* advance only (advance_decode_state)           */
+#define TC_DECODE_ATTEND 2   /* attend only, state untouched
+                                (multilevel_attention_decode)                 */
+
+typedef struct tc_decode_args {
+  int32_t mode;              /* TC_DECODE_*                                  */
+  int32_t B, Hq, Hkv, Dk, Dv;
+  int32_t dtype;             /* ring / token element type                   */
+  int32_t w_dtype;           /* ring w element type                         */
+  int32_t t;                 /* token consumed (FULL/ADVANCE) or attended (ATTEND) */
+  int32_t num_levels, cache_size;
+  int32_t act[TC_MAX_LEVELS];
+  int32_t caps[TC_MAX_LEVELS];
+  int32_t ring_off[TC_MAX_LEVELS + 1];
+  void* ring_k;              /* [B, sum(caps), Hkv, Dk]   (in place)        */
+  void* ring_v;              /* [B, sum(caps), Hkv, Dv]                     */
+  void* ring_w;              /* [B, sum(caps), Hkv]                         */
+  void* conv_k;              /* [B, K-1, Hkv*Dk] or NULL  (in place)        */
+  void* conv_v;              /* [B, K-1, Hkv*Dv] or NULL                    */
+  const void* k_conv_w;      /* [Hkv*Dk, K] or NULL                         */
+  const void* v_conv_w;      /* [Hkv*Dv, K] or NULL                         */
+  int32_t conv_dtype, conv_k_width;
+  const void* q_t;           /* [B, Hq, Dk]                                 */
+  const void* k_t;           /* [B, Hkv, Dk] raw (pre-conv)                 */
+  const void* v_t;           /* [B, Hkv, Dv]                                */
+  const void* w_t;           /* [B, Hkv] precomputed linear weights or NULL */
+  int32_t has_softcap;
+  float softcap;
+  int32_t position_mode;
+  const float* rope_cos;     /* [n_pos, Dk/2] */
+  const float* rope_sin;
+  const void* rel_states;    /* [B, Hq, d_rel] */
+  const void* rel_proj;      /* [d_rel, rel_bins] */
+  int32_t rel_dtype, d_rel, rel_bins;
+  const void* sinks;         /* [Hq] or NULL */
+  int32_t sink_dtype;
+  const void* gate_pre;      /* [B, Hq*Dv] = x_t @ W_g^T, or NULL */
+  int32_t gate_dtype;
+  void* out;                 /* [B, Hq, Dv] post-sink/gate, element type = dtype */
+  float* lse;                /* [B, Hq] pre-sink                           */
+  void* k_new;               /* [B, Hkv, Dk] post-conv key as stored, or NULL */
+  void* v_new;               /* [B, Hkv, Dv] */
+} tc_decode_args;
+
+/* One fused decode step for token t: short_conv_step, merge weight, the
+ * single ruler-tick merge into the per-level ring, the level-0 write, the
+ * multilevel attention read of query t, sink and gate
+ * (decode_step = advance_decode_state + multilevel_attention_decode +
+ *  apply_attention_sink + apply_output_gate, reference.py:1948-2317). */
+int tc_decode_step(const tc_decode_args* a, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TELESCOPE_CACHE_H */

@@ -1,0 +1,225 @@
+// Elementwise helpers around the attention boundary: RoPE application,
+// attention sink forward/backward and the SiLU output gate.  Each mirrors the
+// reference's mixed-precision graph: fp32 math, casts where it casts.
+#include "common.cuh"
+
+using namespace tc;
+
+namespace {
+
+template <typename T>
+__global__ void rope_kernel(int64_t rows, int H, int D, const T* x, T* y, const float* cos_t,
+                            const float* sin_t, int kind, Sched s, int64_t S, const int32_t* positions,
+                            int inverse) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t n = rows * H * D;
+  if (i >= n) return;
+  const int d = (int)(i % D);
+  const int64_t rowh = i / D;           // (b, s, h)
+  const int64_t srow = (rowh / H) % S;  // sequence row
+  int pos;
+  if (kind == 0) {
+    pos = (int)srow;
+  } else if (kind == 2) {
+    pos = positions[rowh];
+  } else {
+    int l = 0;
+    while (l + 1 < s.nl && srow >= s.off[l + 1]) ++l;
+    pos = (((int)(srow - s.off[l]) + 1) << l) - 1;
+  }
+  const int h = D / 2;
+  const int ii = d < h ? d : d - h;
+  const float c = cos_t[(int64_t)pos * h + ii];
+  const float sn = inverse ? -sin_t[(int64_t)pos * h + ii] : sin_t[(int64_t)pos * h + ii];
+  const T* xr = x + rowh * D;
+  const float x1 = to_f(xr[ii]), x2 = to_f(xr[ii + h]);
+  const float out = d < h ? x1 * c - x2 * sn : x2 * c + x1 * sn;
+  y[i] = from_f<T>(out);
+}
+
+template <typename T>
+__global__ void sink_fwd_kernel(int64_t rows, int Hq, int Dv, const T* out, const float* lse, int sdt,
+                                const void* sinks, T* y) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * Hq * Dv) return;
+  const int64_t rh = i / Dv;
+  const int h = (int)(rh % Hq);
+  const float r = 1.f / (1.f + expf(-(lse[rh] - load_any(sinks, h, sdt))));
+  y[i] = from_f<T>(to_f(out[i]) * round_to<T>(r));
+}
+
+template <typename T>
+__global__ void sink_bwd_kernel(int64_t rows, int Hq, int Dv, const T* out, const float* lse, int sdt,
+                                const void* sinks, const T* g, T* gpre, float* dlse) {
+  // one warp per (row, head)
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= rows * Hq) return;
+  const int h = (int)(w % Hq);
+  const float r = 1.f / (1.f + expf(-(lse[w] - load_any(sinks, h, sdt))));
+  const float rt = round_to<T>(r);
+  float dot = 0.f;
+  for (int d = lane; d < Dv; d += 32) {
+    const int64_t i = w * Dv + d;
+    const float gv = to_f(g[i]);
+    gpre[i] = from_f<T>(gv * rt);
+    dot += gv * to_f(out[i]);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+  if (lane == 0) dlse[w] = round_to<T>(dot) * r * (1.f - r);
+}
+
+// dsinks[h] = -sum over rows of dlse[row, h]: one block per head, fixed order.
+__global__ void sink_reduce_kernel(int64_t rows, int Hq, const float* dlse, float* dsinks) {
+  __shared__ float part[256];
+  const int h = blockIdx.x;
+  float s = 0.f;
+  for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) s += dlse[r * Hq + h];
+  part[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o; o >>= 1) {
+    if ((int)threadIdx.x < o) part[threadIdx.x] += part[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) dsinks[h] = -part[0];
+}
+
+__global__ void gate_kernel(int64_t n, int dt, const void* out, int gdt, const void* g, int ydt, void* y) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float gv = load_any(g, i, gdt);
+  const float silu = round_any(gv / (1.f + expf(-gv)), gdt);
+  store_any(y, i, ydt, silu * load_any(out, i, dt));
+}
+
+inline unsigned blocks_for(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
+
+// one warp per (b, t, hkv): logsumexp over the group's query heads
+template <typename T>
+__global__ void qk_weights_kernel(int64_t rows, int Hq, int Hkv, int Dk, const T* q, const T* k, int odt,
+                                  void* out) {
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= rows * Hkv) return;
+  const int64_t bt = w / Hkv;
+  const int h = (int)(w % Hkv);
+  const int E = Hq / Hkv;
+  const float scale = 1.f / sqrtf((float)Dk);
+  float m = -INFINITY, s = 0.f;
+  for (int e = 0; e < E; ++e) {
+    float dot = 0.f;
+    for (int d = lane; d < Dk; d += 32)
+      dot += to_f(q[(bt * Hq + h * E + e) * Dk + d]) * to_f(k[(bt * Hkv + h) * Dk + d]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    dot *= scale;
+    const float mn = fmaxf(m, dot);
+    s = s * expf(m - mn) + expf(dot - mn);
+    m = mn;
+  }
+  if (lane == 0) store_any(out, w, odt, m + logf(s));
+}
+
+template <typename T>
+__global__ void short_conv_kernel(int B, int N, int C, const T* x, int K, int wdt, const void* w, T* y) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)B * N * C) return;
+  const int c = (int)(i % C);
+  const int64_t bt = i / C;
+  const int t = (int)(bt % N);
+  float acc = 0.f;
+  for (int j = 0; j < K; ++j) {
+    const int tt = t - K + 1 + j;
+    if (tt >= 0) acc += load_any(w, (int64_t)c * K + j, wdt) * to_f(x[i + (int64_t)(tt - t) * C]);
+  }
+  y[i] = from_f<T>(to_f(x[i]) + acc);
+}
+
+}  // namespace
+
+extern "C" int tc_qk_weights(int32_t B, int32_t N, int32_t Hq, int32_t Hkv, int32_t Dk, int32_t dtype,
+                             const void* q, const void* k, int32_t out_dtype, void* out, void* stream) {
+  if (B <= 0 || N < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Dk <= 0 || !q || !k || !out) return TC_ERR_ARG;
+  const int64_t rows = (int64_t)B * N;
+  if (rows == 0) return TC_OK;
+  TC_DISPATCH(dtype, T, {
+    qk_weights_kernel<T><<<blocks_for(rows * Hkv * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+        rows, Hq, Hkv, Dk, static_cast<const T*>(q), static_cast<const T*>(k), out_dtype, out);
+  });
+  return launch_status();
+}
+
+extern "C" int tc_short_conv(int32_t B, int32_t N, int32_t C, int32_t dtype, const void* x, int32_t K,
+                             int32_t w_dtype, const void* w, void* y, void* stream) {
+  if (B <= 0 || N < 0 || C <= 0 || K <= 0 || !x || !w || !y) return TC_ERR_ARG;
+  const int64_t n = (int64_t)B * N * C;
+  if (n == 0) return TC_OK;
+  TC_DISPATCH(dtype, T, {
+    short_conv_kernel<T><<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
+        B, N, C, static_cast<const T*>(x), K, w_dtype, w, static_cast<T*>(y));
+  });
+  return launch_status();
+}
+
+extern "C" int tc_rope_apply(int32_t B, int64_t S, int32_t H, int32_t D, int32_t dtype, const void* x,
+                             void* y, const float* cos_t, const float* sin_t, int32_t n_pos,
+                             int32_t pos_kind, const tc_schedule* sched, const int32_t* positions,
+                             int32_t inverse, void* stream) {
+  if (B <= 0 || S <= 0 || H <= 0 || D <= 0 || D % 2 || !x || !y || !cos_t || !sin_t || n_pos <= 0)
+    return TC_ERR_ARG;
+  if (pos_kind < 0 || pos_kind > 2 || (pos_kind == 2 && !positions)) return TC_ERR_ARG;
+  if (pos_kind == 0 && S > n_pos) return TC_ERR_ARG;
+  Sched s{};
+  if (pos_kind == 1) {
+    if (!sched || sched->offsets[sched->num_levels] != S || sched->seq_len > n_pos) return TC_ERR_ARG;
+    s = make_sched(*sched);
+  }
+  const int64_t rows = (int64_t)B * S;
+  const int64_t n = rows * H * D;
+  TC_DISPATCH(dtype, T, {
+    rope_kernel<T><<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
+        rows, H, D, static_cast<const T*>(x), static_cast<T*>(y), cos_t, sin_t, pos_kind, s, S, positions,
+        inverse);
+  });
+  return launch_status();
+}
+
+extern "C" int tc_sink_fwd(int64_t rows, int32_t Hq, int32_t Dv, int32_t dtype, const void* out,
+                           const float* lse, int32_t sink_dtype, const void* sinks, void* y, void* stream) {
+  if (rows < 0 || Hq <= 0 || Dv <= 0 || !out || !lse || !sinks || !y) return TC_ERR_ARG;
+  const int64_t n = rows * Hq * Dv;
+  if (n == 0) return TC_OK;
+  TC_DISPATCH(dtype, T, {
+    sink_fwd_kernel<T><<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
+        rows, Hq, Dv, static_cast<const T*>(out), lse, sink_dtype, sinks, static_cast<T*>(y));
+  });
+  return launch_status();
+}
+
+extern "C" int tc_sink_bwd(int64_t rows, int32_t Hq, int32_t Dv, int32_t dtype, const void* out,
+                           const float* lse, int32_t sink_dtype, const void* sinks, const void* dout,
+                           void* dout_pre, float* dlse, float* dsinks_f32, void* stream) {
+  if (rows < 0 || Hq <= 0 || Dv <= 0 || !out || !lse || !sinks || !dout || !dout_pre || !dlse || !dsinks_f32)
+    return TC_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t warps = rows * Hq;
+  if (warps > 0) {
+    TC_DISPATCH(dtype, T, {
+      sink_bwd_kernel<T><<<blocks_for(warps * 32, 256), 256, 0, st>>>(
+          rows, Hq, Dv, static_cast<const T*>(out), lse, sink_dtype, sinks, static_cast<const T*>(dout),
+          static_cast<T*>(dout_pre), dlse);
+    });
+    if (int rc = launch_status()) return rc;
+  }
+  sink_reduce_kernel<<<Hq, 256, 0, st>>>(rows, Hq, dlse, dsinks_f32);
+  return launch_status();
+}
+
+extern "C" int tc_gate_apply(int64_t n, int32_t dtype, const void* out, int32_t g_dtype, const void* g,
+                             int32_t y_dtype, void* y, void* stream) {
+  if (n < 0 || !out || !g || !y) return TC_ERR_ARG;
+  if (n == 0) return TC_OK;
+  gate_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(n, dtype, out, g_dtype, g, y_dtype, y);
+  return launch_status();
+}

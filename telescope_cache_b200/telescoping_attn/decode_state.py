@@ -1,0 +1,325 @@
+"""Incremental decode: per-level modular rings driven by the schedule
+(reference ``telescoping_attn/decode_state.py`` / ``reference.py:1675-2317``).
+
+Node j of level l lives at ring slot ring_offsets[l] + j % caps[l]; the
+schedule's ranges alone say which nodes are live.  A decode step (conv step,
+merge weight, the single ruler-tick merge, the level-0 write, the attention
+read of the new query, sink and gate) is one CUDA launch
+(``tc_decode_step``); the gate and linear-weight projections of the token's
+hidden state run first as one GEMM / GEMV each.
+"""
+
+import ctypes
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+from .. import _lib
+from ..range_spec import RangeSpec, activation_times_from_fmap, range_bounds
+from .position import compute_relative_states, positional_args, check_relative_bins
+from .summaries import _check_conv_weight, compute_linear_weights, short_conv
+
+
+@dataclass
+class DecodeState:
+    """One layer's decode cache (reference.py:1703-1736):
+    k [B, sum(caps), Hkv, Dk] unrotated post-conv keys, v [B, sum(caps), Hkv, Dv],
+    w [B, sum(caps), Hkv, 1] merge log-weights, conv_k/conv_v [B, K-1, Hkv*D]
+    (last K-1 pre-conv rows, newest last) or None, t = tokens consumed."""
+
+    k: torch.Tensor
+    v: torch.Tensor
+    w: torch.Tensor
+    conv_k: Optional[torch.Tensor]
+    conv_v: Optional[torch.Tensor]
+    t: int
+    activation_times: Tuple[int, ...]
+    cache_size: int
+    caps: Tuple[int, ...]
+    ring_offsets: Tuple[int, ...]
+
+    @property
+    def num_levels(self) -> int:
+        return len(self.activation_times)
+
+    def spec(self, seq_len: int) -> RangeSpec:
+        return RangeSpec(self.activation_times, self.cache_size, seq_len)
+
+
+_CAPS: Dict[Tuple, Tuple[int, ...]] = {}
+
+
+def decode_capacities(activation_times: Tuple[int, ...], cache_size: int) -> Tuple[int, ...]:
+    """Ring capacity per level: the peak live count of each fine level and
+    the most the coarsest can be left over two schedule periods
+    (reference.py:1739-1772); one scan in the C library, memoised."""
+    a = tuple(activation_times)
+    if not a or a[0] != 0:
+        raise ValueError("activation_times must start with a[0] = 0")
+    if cache_size <= 0:
+        raise ValueError("cache_size must be positive")
+    key = (a, cache_size)
+    hit = _CAPS.get(key)
+    if hit is None:
+        if len(a) > _lib.MAX_LEVELS:
+            raise NotImplementedError(f"at most {_lib.MAX_LEVELS} levels are supported")
+        act = (ctypes.c_int32 * len(a))(*a)
+        caps = (ctypes.c_int32 * len(a))()
+        rc = _lib.lib().tc_decode_caps(ctypes.cast(act, ctypes.c_void_p), len(a), cache_size,
+                                       ctypes.cast(caps, ctypes.c_void_p))
+        if rc == _lib.TC_ERR_ARG:
+            raise ValueError(f"fine levels need more slots than cache_size={cache_size}")
+        _lib.check(rc, "tc_decode_caps")
+        hit = tuple(int(c) for c in caps)
+        _CAPS[key] = hit
+    return hit
+
+
+def ring_slot(state: DecodeState, level: int, j: int) -> int:
+    """Physical slot of node j at `level` (reference.py:1775-1784)."""
+    if not 0 <= level < state.num_levels:
+        raise ValueError(f"level {level} out of range [0, {state.num_levels - 1}]")
+    if j < 0:
+        raise ValueError(f"node index must be nonnegative, got {j}")
+    return state.ring_offsets[level] + j % state.caps[level]
+
+
+def _ring_slots(state: DecodeState, level: int, indices: torch.Tensor) -> torch.Tensor:
+    return state.ring_offsets[level] + torch.remainder(indices, state.caps[level])
+
+
+def _conv_history(x_pre: torch.Tensor, kernel_size: int) -> torch.Tensor:
+    """Last K-1 rows of x_pre [B, N, C], zero-padded on the left when N < K-1
+    (reference.py:1796-1807)."""
+    hist = kernel_size - 1
+    if hist == 0:
+        return x_pre[:, :0].clone()
+    pad = max(hist - x_pre.shape[1], 0)
+    return torch.nn.functional.pad(x_pre, (0, 0, pad, 0))[:, -hist:].contiguous()
+
+
+def short_conv_step(x: torch.Tensor, state: torch.Tensor, weight: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """One-token short conv: full = [state, x], y = x + sum_j w[:, j] full[j]
+    with fp32 taps and residual (reference.py:1810-1845).  Returns
+    (y [B, 1, C], new_state = full[:, 1:])."""
+    if x.dim() != 3 or x.shape[1] != 1:
+        raise ValueError(f"x must be [B, 1, C], got {tuple(x.shape)}")
+    B, _, C = x.shape
+    _check_conv_weight(weight, C)
+    K = weight.shape[1]
+    if tuple(state.shape) != (B, K - 1, C):
+        raise ValueError(f"conv state shape {tuple(state.shape)} != {(B, K - 1, C)}")
+    full = torch.cat([state, x], dim=1)
+    # the causal conv at the last of K rows sees exactly the K taps
+    y = short_conv(full, weight)[:, -1:]
+    return y, full[:, 1:]
+
+
+def init_decode_state(
+    k_levels: List[torch.Tensor],
+    v_levels: List[torch.Tensor],
+    w_levels: List[torch.Tensor],
+    fmap: Dict[int, int],
+    cache_size: int,
+    *,
+    k_pre_conv: Optional[torch.Tensor] = None,
+    v_pre_conv: Optional[torch.Tensor] = None,
+    conv_kernel_size: Optional[int] = None,
+) -> DecodeState:
+    """Prefill hand-off: the nodes live at query N-1 go to their ring slots and
+    t = N; the last K-1 pre-conv rows seed the conv history
+    (reference.py:1848-1945)."""
+    if (k_pre_conv is None) != (v_pre_conv is None):
+        raise ValueError("k_pre_conv and v_pre_conv must both be provided or both be None")
+    if (k_pre_conv is None) != (conv_kernel_size is None):
+        raise ValueError("conv_kernel_size must accompany the pre-conv rows (and vice versa)")
+    a = activation_times_from_fmap(fmap)
+    L = len(a) - 1
+    if min(len(k_levels), len(v_levels), len(w_levels)) < L + 1:
+        raise ValueError(
+            f"need {L + 1} levels, got {len(k_levels)}/{len(v_levels)}/{len(w_levels)}")
+    B, N, Hkv, Dk = k_levels[0].shape
+    Dv = v_levels[0].shape[-1]
+    if N < 1:
+        raise ValueError("prefill must contain at least one token")
+    if tuple(w_levels[0].shape) != (B, N, Hkv, 1):
+        raise ValueError(f"w_levels[0] shape {tuple(w_levels[0].shape)} != {(B, N, Hkv, 1)}")
+    caps = decode_capacities(a, cache_size)
+    offs = [0]
+    for c in caps:
+        offs.append(offs[-1] + c)
+    total = offs[-1]
+    dev = k_levels[0].device
+    state = DecodeState(
+        k=torch.zeros(B, total, Hkv, Dk, device=dev, dtype=k_levels[0].dtype),
+        v=torch.zeros(B, total, Hkv, Dv, device=dev, dtype=v_levels[0].dtype),
+        w=torch.zeros(B, total, Hkv, 1, device=dev, dtype=w_levels[0].dtype),
+        conv_k=None, conv_v=None, t=N, activation_times=a, cache_size=cache_size, caps=caps,
+        ring_offsets=tuple(offs))
+    spec = RangeSpec(a, cache_size, N)
+    for level in range(L + 1):
+        lo, hi = range_bounds(spec, N - 1, level)
+        if lo == hi:
+            continue
+        if hi > k_levels[level].shape[1] or hi > v_levels[level].shape[1] or hi > w_levels[level].shape[1]:
+            raise ValueError(f"level {level}: live range [{lo},{hi}) exceeds the given level tensors")
+        slots = _ring_slots(state, level, torch.arange(lo, hi, device=dev, dtype=torch.long))
+        state.k[:, slots] = k_levels[level][:, lo:hi]
+        state.v[:, slots] = v_levels[level][:, lo:hi]
+        state.w[:, slots] = w_levels[level][:, lo:hi]
+    if k_pre_conv is not None:
+        if conv_kernel_size <= 0:
+            raise ValueError(f"conv kernel size must be positive, got {conv_kernel_size}")
+        if k_pre_conv.shape[:2] != (B, N) or v_pre_conv.shape[:2] != (B, N):
+            raise ValueError(
+                f"pre-conv rows must be [B={B}, N={N}, ...], got {tuple(k_pre_conv.shape)} / "
+                f"{tuple(v_pre_conv.shape)}")
+        state.conv_k = _conv_history(k_pre_conv.reshape(B, N, -1), conv_kernel_size)
+        state.conv_v = _conv_history(v_pre_conv.reshape(B, N, -1), conv_kernel_size)
+    return state
+
+
+def _check_tick(state: DecodeState, t: int):
+    """The schedule invariants the reference asserts at every step
+    (reference.py:2036-2082): at most one level fires, its children are live
+    at t-1, and no level exceeds its ring capacity at t."""
+    a = state.activation_times
+    fired = None
+    for level in range(1, len(a)):
+        if t >= a[level] and (t - a[level]) % (1 << level) == 0:
+            if fired is not None:
+                raise AssertionError(
+                    f"levels {fired} and {level} both activate at t={t}; the schedule is not "
+                    f"dyadically aligned")
+            fired = level
+            j = (t - a[level]) >> level
+            lo_c, hi_c = range_bounds(state.spec(t), t - 1, level - 1)
+            if not (lo_c <= 2 * j and 2 * j + 1 < hi_c):
+                raise AssertionError(
+                    f"children of node ({level}, {j}) not live at t-1={t - 1}: level-{level - 1} "
+                    f"range [{lo_c},{hi_c})")
+    spec_next = state.spec(t + 1)
+    for level in range(len(a)):
+        lo, hi = range_bounds(spec_next, t, level)
+        if hi - lo > state.caps[level]:
+            raise AssertionError(
+                f"level {level} needs {hi - lo} live slots > cap {state.caps[level]} at t={t}")
+
+
+def _decode_launch(state: DecodeState, mode, q_t, k_t=None, v_t=None, w_t=None, kcw=None, vcw=None,
+                   softcap=None, position_mode="none", cos=None, sin=None, rel_states=None,
+                   rel_proj=None, sinks=None, gate_pre=None, t=None, want_kv=False):
+    B, _, Hq, Dk = q_t.shape
+    Hkv = state.k.shape[2]
+    Dv = state.v.shape[-1]
+    dtype = state.k.dtype
+    _lib.require_cuda(q_t, state.k, state.v, state.w)
+    for name, ring in (("k", state.k), ("v", state.v), ("w", state.w)):
+        if not ring.is_contiguous():
+            raise ValueError(f"decode ring {name} must be contiguous (it is updated in place)")
+    qc = q_t.to(dtype).contiguous()
+    kc = None if k_t is None else k_t.to(dtype).contiguous()
+    vc = None if v_t is None else v_t.to(dtype).contiguous()
+    out = torch.empty(B, 1, Hq, Dv, device=q_t.device, dtype=dtype)
+    lse = torch.empty(B, 1, Hq, device=q_t.device, dtype=torch.float32)
+    k_new = torch.empty(B, 1, Hkv, Dk, device=q_t.device, dtype=dtype) if want_kv else None
+    v_new = torch.empty(B, 1, Hkv, Dv, device=q_t.device, dtype=dtype) if want_kv else None
+    L1 = state.num_levels
+    conv_w = 0 if kcw is None else kcw.shape[1]
+    if kcw is not None:
+        kcw = kcw.contiguous()
+        vcw = vcw.to(kcw.dtype).contiguous()
+        for name, cs in (("conv_k", state.conv_k), ("conv_v", state.conv_v)):
+            if not cs.is_contiguous() or cs.dtype != dtype:
+                setattr(state, name, cs.to(dtype).contiguous())
+    keep = []
+
+    def p(t_):
+        if t_ is None:
+            return None
+        keep.append(t_)
+        return t_.data_ptr()
+
+    args = _lib.DecodeArgs(
+        mode=mode, B=B, Hq=Hq, Hkv=Hkv, Dk=Dk, Dv=Dv, dtype=_lib.dtype_code(dtype),
+        w_dtype=_lib.dtype_code(state.w.dtype), t=state.t if t is None else t, num_levels=L1,
+        cache_size=state.cache_size,
+        act=(ctypes.c_int32 * _lib.MAX_LEVELS)(*state.activation_times),
+        caps=(ctypes.c_int32 * _lib.MAX_LEVELS)(*state.caps),
+        ring_off=(ctypes.c_int32 * (_lib.MAX_LEVELS + 1))(*state.ring_offsets),
+        ring_k=state.k.data_ptr(), ring_v=state.v.data_ptr(), ring_w=state.w.data_ptr(),
+        conv_k=p(state.conv_k) if conv_w else None, conv_v=p(state.conv_v) if conv_w else None,
+        k_conv_w=p(kcw), v_conv_w=p(vcw), conv_dtype=_lib.dtype_code(kcw.dtype) if conv_w else 0,
+        conv_k_width=conv_w, q_t=p(qc), k_t=p(kc), v_t=p(vc), w_t=p(w_t),
+        has_softcap=0 if softcap is None else 1, softcap=0.0 if softcap is None else float(softcap),
+        position_mode=_lib.POS[position_mode], rope_cos=p(cos), rope_sin=p(sin),
+        rel_states=p(rel_states), rel_proj=p(rel_proj),
+        rel_dtype=_lib.dtype_code(rel_states.dtype) if rel_states is not None else 0,
+        d_rel=0 if rel_states is None else rel_states.shape[-1],
+        rel_bins=0 if rel_proj is None else rel_proj.shape[1], sinks=p(sinks),
+        sink_dtype=_lib.dtype_code(sinks.dtype) if sinks is not None else 0, gate_pre=p(gate_pre),
+        gate_dtype=_lib.dtype_code(gate_pre.dtype) if gate_pre is not None else 0,
+        out=out.data_ptr(), lse=lse.data_ptr(), k_new=p(k_new), v_new=p(v_new))
+    _lib.check(_lib.lib().tc_decode_step(ctypes.byref(args), _lib.stream_of(q_t)), "tc_decode_step")
+    del keep
+    return out, lse, k_new, v_new
+
+
+def _validate_advance(state, q_t, k_t, v_t, x_t, w_proj, k_conv_weight, v_conv_weight):
+    B, _, Hkv, Dk = state.k.shape
+    Dv = state.v.shape[-1]
+    if q_t.dim() != 4 or q_t.shape[0] != B or q_t.shape[1] != 1 or q_t.shape[-1] != Dk \
+            or q_t.shape[2] % Hkv != 0:
+        raise ValueError(
+            f"q_t shape {tuple(q_t.shape)} incompatible with [B={B}, 1, Hq (multiple of {Hkv}), "
+            f"Dk={Dk}]")
+    if tuple(k_t.shape) != (B, 1, Hkv, Dk):
+        raise ValueError(f"k_t shape {tuple(k_t.shape)} != {(B, 1, Hkv, Dk)}")
+    if tuple(v_t.shape) != (B, 1, Hkv, Dv):
+        raise ValueError(f"v_t shape {tuple(v_t.shape)} != {(B, 1, Hkv, Dv)}")
+    if (k_conv_weight is None) != (v_conv_weight is None):
+        raise ValueError("k_conv_weight and v_conv_weight must both be provided or both be None")
+    if k_conv_weight is not None:
+        if state.conv_k is None or state.conv_v is None:
+            raise ValueError(
+                "conv weights given but the state was initialised without pre-conv rows "
+                "(init_decode_state k_pre_conv/v_pre_conv)")
+        _check_conv_weight(k_conv_weight, Hkv * Dk)
+        _check_conv_weight(v_conv_weight, Hkv * Dv)
+        K = k_conv_weight.shape[1]
+        if v_conv_weight.shape[1] != K:
+            raise NotImplementedError("K and V conv widths must match")
+        if tuple(state.conv_k.shape) != (B, K - 1, Hkv * Dk):
+            raise ValueError(f"conv state shape {tuple(state.conv_k.shape)} != {(B, K - 1, Hkv * Dk)}")
+    elif state.conv_k is not None:
+        raise ValueError("the state carries a conv state but no conv weights were given")
+    if (x_t is None) != (w_proj is None):
+        raise ValueError(
+            "x_t and w_proj must both be provided (linear weight mode) or both be None (QK weight mode)")
+    w_t = None
+    if x_t is not None:
+        w_t = compute_linear_weights(x_t, w_proj)
+        if tuple(w_t.shape) != (B, 1, Hkv, 1):
+            raise ValueError(f"linear weights shape {tuple(w_t.shape)} != {(B, 1, Hkv, 1)}")
+        w_t = w_t.to(state.w.dtype).contiguous()
+    return w_t
+
+
+def advance_decode_state(state: DecodeState, q_t: torch.Tensor, k_t: torch.Tensor, v_t: torch.Tensor,
+                         *, x_t: Optional[torch.Tensor] = None, w_proj: Optional[torch.Tensor] = None,
+                         k_conv_weight: Optional[torch.Tensor] = None,
+                         v_conv_weight: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Consume token t = state.t in place: conv step, merge weight, the ruler-
+    tick merge, then the level-0 write; state.t becomes t + 1
+    (reference.py:1948-2090).  Returns (k_t, v_t) as stored (post-conv)."""
+    w_t = _validate_advance(state, q_t, k_t, v_t, x_t, w_proj, k_conv_weight, v_conv_weight)
+    _check_tick(state, state.t)
+    _, _, k_new, v_new = _decode_launch(state, _lib.DECODE_ADVANCE, q_t, k_t, v_t, w_t=w_t,
+                                        kcw=k_conv_weight, vcw=v_conv_weight, want_kv=True)
+    state.t += 1
+    return k_new, v_new
+
+
+__all__ = ["DecodeState", "decode_capacities", "ring_slot", "short_conv_step", "init_decode_state",
+           "advance_decode_state"]

@@ -1,0 +1,173 @@
+"""Positional helpers: post-summary RoPE and the summary-bin relative bias
+(reference ``telescoping_attn/position.py`` / ``reference.py:214-462``), plus
+the positional-argument validation shared by forward, backward and decode
+(``reference.py:675-768``)."""
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from .. import _lib
+from ..range_spec import RangeSpec, elem_mask, range_bounds, visible_stats
+
+
+def summary_token_position(level: int, local_index: int) -> int:
+    """RoPE anchor of node (level, j): the right endpoint (j + 1) 2^level - 1
+    of the tokens it summarises (reference.py:219-237)."""
+    if level < 0 or local_index < 0:
+        raise ValueError(
+            f"level and local_index must be nonnegative, got ({level}, {local_index})")
+    return ((local_index + 1) << level) - 1
+
+
+def rope_tables(n_pos: int, dim: int, base: float = 10000.0, device=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin [n_pos, dim // 2] float32, theta_i = base^(-2i/dim), GPT-NeoX
+    rotate-half convention (reference.py:240-264)."""
+    if dim <= 0 or dim % 2 != 0:
+        raise ValueError(f"dim must be positive and even, got {dim}")
+    if n_pos <= 0:
+        raise ValueError(f"n_pos must be positive, got {n_pos}")
+    freqs = base ** (-torch.arange(0, dim, 2, device=device, dtype=torch.float32) / dim)
+    ang = torch.arange(n_pos, device=device, dtype=torch.float32)[:, None] * freqs[None, :]
+    return torch.cos(ang), torch.sin(ang)
+
+
+def _rope_into(x, y, cos, sin, kind, sched=None, positions=None, inverse=False):
+    """tc_rope_apply over x viewed as [B, S, H, D]."""
+    B, S, H, D = x.shape
+    cos = cos if cos.dtype == torch.float32 and cos.is_contiguous() else cos.float().contiguous()
+    sin = sin if sin.dtype == torch.float32 and sin.is_contiguous() else sin.float().contiguous()
+    _lib.check(_lib.lib().tc_rope_apply(
+        B, S, H, D, _lib.dtype_code(x.dtype), _lib.ptr(x), _lib.ptr(y), _lib.ptr(cos), _lib.ptr(sin),
+        cos.shape[0], kind, None if sched is None else ctypes.byref(sched),
+        _lib.ptr(positions), 1 if inverse else 0, _lib.stream_of(x)), "tc_rope_apply")
+    return y
+
+
+def apply_rope(x: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+               inverse: bool = False) -> torch.Tensor:
+    """Rotate-half RoPE of x [..., D] at integer `positions` (broadcastable to
+    x.shape[:-1]) in fp32, cast back; inverse=True applies R(-p)
+    (reference.py:267-302)."""
+    if cos.shape != sin.shape:
+        raise ValueError(f"cos shape {tuple(cos.shape)} != sin shape {tuple(sin.shape)}")
+    D = x.shape[-1]
+    if 2 * cos.shape[-1] != D:
+        raise ValueError(f"rope tables cover dim {2 * cos.shape[-1]}, x has dim {D}")
+    _lib.require_cuda(x, cos, sin)
+    if not torch.is_tensor(positions):
+        positions = torch.tensor(positions, device=x.device)
+    pos = positions.to(device=x.device).expand(x.shape[:-1]).to(torch.int32).contiguous()
+    if pos.numel() and (int(pos.min()) < 0 or int(pos.max()) >= cos.shape[0]):
+        raise IndexError("rope position outside the tables")
+    xc = x.contiguous()
+    y = torch.empty_like(xc)
+    if xc.numel():
+        _rope_into(xc.reshape(1, 1, -1, D), y.reshape(1, 1, -1, D), cos, sin, 2,
+                   positions=pos.reshape(-1), inverse=inverse)
+    return y
+
+
+def validate_summary_causality(spec: RangeSpec) -> None:
+    """Positional modes need a[l] >= 2^l - 1: a summary becomes visible only
+    after its newest token (reference.py:305-324)."""
+    for level in range(1, spec.num_levels):
+        if spec.activation_times[level] < (1 << level) - 1:
+            raise ValueError(
+                f"schedule makes a level-{level} summary visible before its interval completes "
+                f"(a[{level}]={spec.activation_times[level]} < {(1 << level) - 1}); positional "
+                f"semantics undefined")
+
+
+def relative_bin_distance(spec: RangeSpec, q: int, level: int, k_local: int) -> int:
+    """0-based chronological bin distance of visible entry (level, k_local)
+    from query q: the number of visible entries whose interval starts later
+    (reference.py:327-371).  Raises ValueError if it is not visible."""
+    if not elem_mask(spec, q, k_local, level):
+        raise ValueError(f"entry (level={level}, k_local={k_local}) is not visible to query {q}")
+    start = k_local << level
+    total = older = 0
+    for lv in range(spec.num_levels):
+        lo, hi = range_bounds(spec, q, lv)
+        total += hi - lo
+        first_not_older = (start + (1 << lv) - 1) >> lv
+        older += min(max(first_not_older, lo), hi) - lo
+    return total - 1 - older
+
+
+def compute_relative_states(x: torch.Tensor, relative_weight: torch.Tensor, Hq: int) -> torch.Tensor:
+    """relative_states [B, N, Hq, d_rel] = x @ relative_weight^T, reshaped
+    (reference.py:374-395).  A plain GEMM (cuBLAS through torch.matmul)."""
+    B, N, E = x.shape
+    rows, Ew = relative_weight.shape
+    if Ew != E or rows % Hq != 0:
+        raise ValueError(
+            f"relative_weight shape {tuple(relative_weight.shape)} incompatible with "
+            f"emb_dim={E}, Hq={Hq}")
+    return x.matmul(relative_weight.t()).reshape(B, N, Hq, rows // Hq)
+
+
+def positional_args(position_mode, rope_cos, rope_sin, relative_states, relative_proj, *,
+                    B, N, Hq, Dk, spec, rope_positions):
+    """Validate the positional arguments exactly like the reference
+    (reference.py:675-768).  Returns max_relative_bins (0 unless relative).
+    Unlike the reference, rel_logits are never materialised: the kernels
+    form each bias from relative_states and relative_proj on the fly."""
+    if position_mode not in ("none", "rope", "relative"):
+        raise ValueError(
+            f"position_mode must be 'none', 'rope' or 'relative', got {position_mode!r}")
+    bins = 0
+    if position_mode == "none":
+        if any(t is not None for t in (rope_cos, rope_sin, relative_states, relative_proj)):
+            raise ValueError("positional arguments provided with position_mode='none'")
+    elif position_mode == "rope":
+        if rope_cos is None or rope_sin is None:
+            raise ValueError("position_mode='rope' requires rope_cos and rope_sin")
+        if relative_states is not None or relative_proj is not None:
+            raise ValueError("relative_* arguments provided with position_mode='rope'")
+        if Dk % 2 != 0:
+            raise ValueError(f"RoPE requires an even Dk, got {Dk}")
+        if rope_cos.shape != rope_sin.shape:
+            raise ValueError(
+                f"rope_cos shape {tuple(rope_cos.shape)} != rope_sin shape {tuple(rope_sin.shape)}")
+        if rope_cos.dim() != 2 or rope_cos.shape[-1] * 2 != Dk:
+            raise ValueError(f"rope tables must be [n_pos, {Dk // 2}], got {tuple(rope_cos.shape)}")
+        if rope_cos.shape[0] < rope_positions:
+            raise ValueError(
+                f"rope tables cover {rope_cos.shape[0]} positions; summary positions reach "
+                f"N-1={rope_positions - 1}")
+        validate_summary_causality(spec)
+    else:
+        if relative_states is None or relative_proj is None:
+            raise ValueError(
+                "position_mode='relative' requires relative_states and relative_proj")
+        if rope_cos is not None or rope_sin is not None:
+            raise ValueError("rope_* arguments provided with position_mode='relative'")
+        if relative_states.dim() != 4 or tuple(relative_states.shape[:3]) != (B, N, Hq):
+            raise ValueError(
+                f"relative_states shape {tuple(relative_states.shape)} != [{B}, {N}, {Hq}, d_rel]")
+        if relative_proj.dim() != 2 or relative_proj.shape[0] != relative_states.shape[-1]:
+            raise ValueError(
+                f"relative_proj shape {tuple(relative_proj.shape)} incompatible with "
+                f"d_rel={relative_states.shape[-1]}")
+        bins = relative_proj.shape[1]
+        if bins < 1:
+            raise ValueError("relative_proj must have >= 1 bins")
+        validate_summary_causality(spec)
+    return bins
+
+
+def check_relative_bins(spec: RangeSpec, bins: int, max_visible: Optional[int] = None):
+    """The reference raises when a visible entry's distance reaches the table
+    size (reference.py:441-452); distances run to |A(q)| - 1, so the check is
+    max_q |A(q)| > bins, decided once per schedule."""
+    mx = visible_stats(spec)[1] if max_visible is None else max_visible
+    if mx - 1 >= bins:
+        raise ValueError(
+            f"relative bin distance {mx - 1} exceeds max_relative_bins={bins}; no silent "
+            f"clamping -- a table with >= cache_size={spec.cache_size} bins always suffices")
+
+
+__all__ = ["summary_token_position", "rope_tables", "apply_rope", "validate_summary_causality",
+           "relative_bin_distance", "compute_relative_states"]

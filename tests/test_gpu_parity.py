@@ -1,0 +1,87 @@
+"""CUDA path vs the reference (golden fixtures) and the CPU oracle, on every
+golden case: builder, forward (none / rope / relative, softcap on/off, sink,
+gate, GQA, odd lengths, eviction), backward at the packed boundary with the
+sink dlse seam, and incremental decode.
+
+Tolerances: fp32 cases use the reference suite's own (1e-5 forward, 1e-4
+gradients, test_reference.py:118-119); bf16 cases must be within 2e-2
+relative of the fp32 reference: |got - want| <= 2e-2 * (|want| + max|want|).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import cases as C
+from oracle_runner import load_golden, oracle_case
+
+pytestmark = pytest.mark.gpu
+
+GRAD_KEYS = {"dq", "dk_packed", "dv_packed", "dpos", "dsinks", "dlse", "dout_pre"}
+BF16_REL = 2e-2
+
+
+def compare(name, key, got, want, dtype):
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    assert got.shape == want.shape, (name, key, got.shape, want.shape)
+    if dtype == "bf16":
+        scale = np.abs(want).max() if want.size else 0.0
+        err = np.abs(got - want)
+        bound = BF16_REL * (np.abs(want) + scale)
+        bad = err > bound
+        assert not bad.any(), (f"{name}:{key} bf16 max err {err.max():.3e} vs scale {scale:.3e}; "
+                               f"{int(bad.sum())} elements out of bound")
+    else:
+        tol = 1e-4 if key in GRAD_KEYS else 1e-5
+        np.testing.assert_allclose(got, want, rtol=tol, atol=tol, err_msg=f"{name}:{key}")
+
+
+def check_against(name, c, got, want, live=None):
+    for key, w in want.items():
+        if key in ("case", "ring_live", "caps", "offsets"):
+            continue
+        gv = got[key]
+        if key.startswith("ring_"):
+            gv, w = gv[:, live], w[:, live]
+        compare(name, key, gv, w, c["dtype"])
+    if "caps" in want:
+        assert tuple(got["caps"]) == tuple(want["caps"])
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch.device("cuda")
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in C.CASES])
+def test_cuda_matches_reference_golden(cuda, name):
+    from product_runner import product_case
+    c = C.CASE_BY_NAME[name]
+    gold = load_golden(name)
+    got = product_case(c)
+    check_against(name, c, got, gold, gold.get("ring_live"))
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in C.CASES if c["kind"] in ("fwd", "bwd")])
+def test_cuda_matches_oracle(cuda, name):
+    from product_runner import product_case
+    c = C.CASE_BY_NAME[name]
+    got = product_case(c)
+    want = oracle_case(c)
+    check_against(name, c, got, want)
+
+
+@pytest.mark.parametrize("name", ["fwd_plain_d64", "fwd_rope_d128_bf16", "fwd_rel_d128_bf16",
+                                  "bwd_rel_sink_d128_bf16"])
+def test_simt_and_default_paths_agree(cuda, name):
+    """The tensor-core and SIMT kernels compute the same function."""
+    from product_runner import product_case
+    c = C.CASE_BY_NAME[name]
+    a = product_case(c, impl="simt")
+    b = product_case(c)
+    for key in a:
+        if key == "offsets":
+            continue
+        compare(name, key, b[key], a[key], "bf16" if c["dtype"] == "bf16" else "fp32")
