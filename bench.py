@@ -1,0 +1,398 @@
+"""Benchmark of the telescoping-attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c3|c5|c2]
+
+A step is one training-layer pass of the hot path over one batch of seeded
+synthetic inputs (the reference publishes no dataset): build the dyadic tree
+(fused conv / merge weights / merges / packing), Phase-2 forward, attention
+sink, sink backward and the Phase-2 backward with the dlse seam.  The default
+workload is BASELINE config 3 (B=4, T=16384, H=16, D=128, bf16, qk weights,
+relative bias, 8 levels x 512, softcap 50, sink).  Multi-GPU runs shard
+(batch x head) units across ranks with no data-path collective: each rank
+processes its own config-3 batch (weak scaling).
+
+The metric is visible-entry TFLOP/s: per visible (query, entry) pair and query
+head, 4 D FLOPs forward (QK^T and PV) + 10 D backward (five GEMMs); hull
+padding, softcap, bias and RoPE are not counted.
+
+``--impl reference`` times the CPU oracle (a numpy restatement of the
+reference's reference.py; the reference itself is Python and cannot run on
+the GPU box) on a bounded sample of the same workload, on all host threads.
+"""
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: (B, T, H, D, levels, window, weights, position, softcap, sink, conv, d_rel)
+    "c3": dict(B=4, T=16384, H=16, D=128, levels=8, W=512, weights="qk", position="relative",
+               softcap=50.0, sink=True, conv=0, d_rel=16,
+               desc="BASELINE config 3: training-layer fwd+bwd, relative bias, sink"),
+    "c5": dict(B=1, T=131072, H=32, D=128, levels=10, W=1024, weights="linear", position="rope",
+               softcap=50.0, sink=True, conv=0, d_rel=0,
+               desc="BASELINE config 5: long-context fwd+bwd, rope, linear weights, sink"),
+    "c2": dict(B=2, T=8192, H=16, D=128, levels=6, W=256, weights="linear", position="rope",
+               softcap=30.0, sink=True, conv=4, d_rel=0,
+               desc="BASELINE config 2 shape (attention fwd+bwd)"),
+}
+EMB = 2048
+
+
+def schedule(wl):
+    fmap = {l: l * wl["W"] for l in range(1, wl["levels"])}
+    return fmap, wl["levels"] * wl["W"]
+
+
+def flops_per_step(wl, total_visible):
+    return (4 + 10) * wl["D"] * total_visible * wl["B"] * wl["H"]
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p.get("bf16_tflops", 1590.0), p.get("bf16_tflops_sustained", 1400.0), \
+            p.get("hbm_gbs", 6650.0), "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clocks / throttle reasons during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        mhz.sort()
+        med = mhz[len(mhz) // 2] if mhz else None
+        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+def make_inputs(wl, device, seed, rank):
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + 7919 * rank)
+    B, T, H, D = wl["B"], wl["T"], wl["H"], wl["D"]
+    bf = torch.bfloat16
+    inp = dict(
+        q=torch.randn(B, T, H, D, generator=g, device=device, dtype=bf),
+        k=torch.randn(B, T, H, D, generator=g, device=device, dtype=bf),
+        v=torch.randn(B, T, H, D, generator=g, device=device, dtype=bf),
+        dout=torch.randn(B, T, H, D, generator=g, device=device, dtype=bf),
+    )
+    fmap, cache = schedule(wl)
+    if wl["sink"]:
+        inp["sinks"] = torch.randn(H, generator=g, device=device, dtype=torch.float32)
+    if wl["position"] == "relative":
+        inp["states"] = (0.02 * torch.randn(B, T, H, wl["d_rel"], generator=g, device=device)).to(bf)
+        inp["proj"] = (0.02 * torch.randn(wl["d_rel"], cache, generator=g, device=device)).to(bf)
+    if wl["weights"] == "linear":
+        inp["x"] = torch.randn(B, T, EMB, generator=g, device=device, dtype=bf)
+        inp["w_proj"] = (0.02 * torch.randn(H, EMB, generator=g, device=device)).to(bf)
+    if wl["conv"]:
+        inp["kcw"] = torch.randn(H * D, wl["conv"], generator=g, device=device) / math.sqrt(wl["conv"])
+        inp["vcw"] = torch.randn(H * D, wl["conv"], generator=g, device=device) / math.sqrt(wl["conv"])
+    return inp
+
+
+def run_step(T, wl, inp, fmap, cache, tables, timers=None):
+    """One pass of the hot path.  timers: dict of (start, end) CUDA events."""
+    import torch
+    kw = {}
+    if wl["weights"] == "linear":
+        kw.update(x=inp["x"], w_proj=inp["w_proj"])
+    if wl["conv"]:
+        kw.update(k_conv_weight=inp["kcw"], v_conv_weight=inp["vcw"])
+    kl, vl, _ = T.build_dyadic_summaries(inp["q"], inp["k"], inp["v"], wl["levels"] - 1, **kw)
+    packed = T.pack_levels(kl, vl)
+    pos = {}
+    if wl["position"] == "relative":
+        pos = dict(position_mode="relative", relative_states=inp["states"], relative_proj=inp["proj"])
+    elif wl["position"] == "rope":
+        pos = dict(position_mode="rope", rope_cos=tables[0], rope_sin=tables[1])
+    if timers:
+        timers["fwd"][0].record()
+    out, lse = T.multilevel_attention_forward(inp["q"], packed, fmap, cache, softcap=wl["softcap"],
+                                              **pos)
+    if timers:
+        timers["fwd"][1].record()
+    dout, dlse = inp["dout"], None
+    if wl["sink"]:
+        _ = T.apply_attention_sink(out, lse, inp["sinks"])
+        dout, dlse, _ = T.attention_sink_backward(out, lse, inp["sinks"], inp["dout"])
+    if timers:
+        timers["bwd"][0].record()
+    dq, dk, dv, dpos, _ = T.multilevel_attention_backward(
+        inp["q"], packed, out, lse, dout, fmap, cache, softcap=wl["softcap"], dlse=dlse, **pos)
+    if timers:
+        timers["bwd"][1].record()
+    return dq, dk, dv, dpos, out
+
+
+def cpu_reference_sample(wl, seconds_budget=20.0):
+    """Time the CPU oracle (fwd + bwd) on a bounded sample of the workload:
+    consecutive query rows of one (batch, head) slice, in the steady state
+    where every level is live, for about `seconds_budget` seconds.  Returns
+    (TFLOP/s on visible-entry FLOPs, description)."""
+    import numpy as np
+
+    from oracle import numerics as O
+    from oracle import schedule as S
+
+    fmap, cache = schedule(wl)
+    a = S.activation_times(fmap)
+    D, T_ = wl["D"], wl["T"]
+    r = np.random.Generator(np.random.PCG64(5))
+    q = r.standard_normal((1, T_, 1, D)).astype(np.float32)
+    k = r.standard_normal((1, T_, 1, D)).astype(np.float32)
+    v = r.standard_normal((1, T_, 1, D)).astype(np.float32)
+    kl, vl, _ = O.build_tree(k, v, O.qk_weights(q, k), wl["levels"] - 1)
+    pos = O.Positional()
+    if wl["position"] == "relative":
+        st = (0.02 * r.standard_normal((1, T_, 1, wl["d_rel"]))).astype(np.float32)
+        pj = (0.02 * r.standard_normal((wl["d_rel"], cache))).astype(np.float32)
+        pos = O.Positional("relative", states=st, proj=pj)
+    elif wl["position"] == "rope":
+        cos, sin = O.rope_tables(T_, D)
+        pos = O.Positional("rope", cos=cos, sin=sin)
+    dout = r.standard_normal((1, T_, 1, D)).astype(np.float32)
+    start = T_ - 1
+    pairs = 0
+    t0 = time.perf_counter()
+    chunk = 16
+    while time.perf_counter() - t0 < seconds_budget and start - chunk >= 0:
+        rows = range(start - chunk, start)
+        out, lse = O.forward(q, kl, vl, fmap, cache, wl["softcap"], pos, rows=rows)
+        O.backward(q, kl, vl, out, lse, dout, fmap, cache, wl["softcap"], pos, rows=rows)
+        pairs += sum(len(S.visible_entries(qi, a, cache)) for qi in rows)
+        start -= chunk
+    el = time.perf_counter() - t0
+    n = T_ - 1 - start
+    return (4 + 10) * D * pairs / el / 1e12, (
+        f"{n} query rows (the last of T={T_}) of one (batch, head) slice, fwd+bwd in float64 "
+        f"numpy, {el:.1f} s; throughput scales linearly with the slice count")
+
+
+def reference_arm(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    times = []
+    sample = ""
+    for i in range(args.warmup + args.steps):
+        tf, sample = cpu_reference_sample(wl, seconds_budget=max(5.0, 60.0 / (args.steps + args.warmup)))
+        if i >= args.warmup:
+            times.append(tf)
+    val = sorted(times)[len(times) // 2]
+    fmap, cache = schedule(wl)
+    line = {
+        "impl": "reference", "metric": "multilevel attn fwd+bwd TFLOP/s (visible-entry FLOPs)",
+        "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "desc": wl["desc"], "fmap": fmap, "cache_size": cache},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return reference_arm(args, wl)
+
+    import torch
+    import torch.distributed as dist
+
+    import telescope_cache_b200 as T
+    from telescope_cache_b200 import _lib
+    from telescope_cache_b200 import range_spec as R
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    fmap, cache = schedule(wl)
+    spec = R.RangeSpec.from_fmap(fmap, cache, wl["T"])
+    total_visible = R.visible_stats(spec)[2]
+    step_flops = flops_per_step(wl, total_visible)
+    inp = make_inputs(wl, dev, 1234, rank)
+    tables = T.rope_tables(wl["T"], wl["D"], device=dev) if wl["position"] == "rope" else None
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > L2 (126 MB)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        run_step(T, wl, inp, fmap, cache, tables)
+    barrier()
+    st = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    kt = [{"fwd": (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)),
+           "bwd": (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))}
+          for _ in range(args.steps)]
+    launches_before = _lib.launch_count()
+    with ClockSampler(local) as clocks:
+        barrier()
+        step_ms = []
+        for i in range(args.steps):
+            flush.zero_()  # L2 flush between timed iterations
+            ev[i][0].record(st)
+            run_step(T, wl, inp, fmap, cache, tables, timers=kt[i])
+            ev[i][1].record(st)
+        barrier()
+    launches_timed = _lib.launch_count() - launches_before
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    fwd_ms = [t["fwd"][0].elapsed_time(t["fwd"][1]) for t in kt]
+    bwd_ms = [t["bwd"][0].elapsed_time(t["bwd"][1]) for t in kt]
+    ms = sum(step_ms) / len(step_ms)
+    if world > 1:
+        tm = torch.tensor([ms], device=dev)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms = float(tm.item())
+    value = step_flops * world / (ms * 1e-3) / 1e12
+
+    # end-to-end through the public API from pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        host = {k: v.cpu().pin_memory() for k, v in inp.items()}
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        dq_host = torch.empty(inp["q"].shape, dtype=inp["q"].dtype, pin_memory=True)
+        d2h = dq_host.numel() * dq_host.element_size()
+        e_ms = []
+        for i in range(args.warmup + args.steps):
+            barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            dinp = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
+            dq, *_ = run_step(T, wl, dinp, fmap, cache, tables)
+            dq_host.copy_(dq, non_blocking=True)
+            b.record(st)
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                e_ms.append(a.elapsed_time(b))
+        em = sum(e_ms) / len(e_ms)
+        if world > 1:
+            tm = torch.tensor([em], device=dev)
+            dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+            em = float(tm.item())
+        e2e = {"value": step_flops * world / (em * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "ms_per_step": em, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+    burst, sustained, hbm, src = peaks()
+    fwd_flops = 4 * wl["D"] * total_visible * wl["B"] * wl["H"]
+    bwd_flops = 10 * wl["D"] * total_visible * wl["B"] * wl["H"]
+    fms, bms = sum(fwd_ms) / len(fwd_ms), sum(bwd_ms) / len(bwd_ms)
+    dom = ("backward", bwd_flops, bms) if bms >= fms else ("forward", fwd_flops, fms)
+    achieved = dom[1] / (dom[2] * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "kernel": f"attention {dom[0]}", "achieved": achieved,
+                "peak": sustained, "peak_source": f"{src} bf16_tflops_sustained", "unit": "TFLOP/s",
+                "frac": achieved / sustained, "traffic": None,
+                "forward_tflops": fwd_flops / (fms * 1e-3) / 1e12,
+                "backward_tflops": bwd_flops / (bms * 1e-3) / 1e12,
+                "forward_ms": fms, "backward_ms": bms}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tf, sample = cpu_reference_sample(wl, seconds_budget=15.0)
+        cpu = {"value": tf, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": sample}
+    launches = launches_timed
+    if rank == 0:
+        line = {
+            "metric": "multilevel attn fwd+bwd TFLOP/s (visible-entry FLOPs)",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": args.workload, "desc": wl["desc"], "B_per_rank": wl["B"],
+                       "T": wl["T"], "H": wl["H"], "D": wl["D"], "fmap": fmap, "cache_size": cache,
+                       "global_batch": wl["B"] * world, "parallelism": f"dp{world} (batch x head shards)",
+                       "l2": "flushed between timed steps (256 MB write)",
+                       "step_flops": step_flops},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks.summary(),
+            "gpu_launches": launches,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

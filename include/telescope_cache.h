@@ -65,6 +65,9 @@ typedef struct tc_schedule {
 /* Library version, for the Python loader's sanity check. */
 int tc_version(void);
 
+/* Number of CUDA kernels this library has launched since it was loaded. */
+int64_t tc_launch_count(void);
+
 /* ------------------------------------------------------------------------ */
 /* schedule (host side; pure integer)                                        */
 /* ------------------------------------------------------------------------ */

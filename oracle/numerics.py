@@ -191,10 +191,11 @@ def _row_scores(qrow, kent, lv, js, dists, qi, b_rel, pos: Positional, e, scale,
 
 
 def forward(q, k_levels, v_levels, fmap, cache, softcap, pos: Optional[Positional] = None,
-            store=identity):
+            store=identity, rows=None):
     """(out [B,N,Hq,Dv], lse [B,N,Hq]) with S = c tanh(X/c) (or X), X = q.k/sqrt(Dk)
     [+ bias], softmax over exactly the visible set (reference.py:771-1071;
-    minimal_reference.py semantics).  lse is the natural-log pre-sink LSE."""
+    minimal_reference.py semantics).  lse is the natural-log pre-sink LSE.
+    `rows` restricts the computation to those query rows (others stay 0)."""
     pos = pos or Positional()
     a = S.activation_times(fmap)
     q = np.asarray(q, np.float64)
@@ -205,7 +206,7 @@ def forward(q, k_levels, v_levels, fmap, cache, softcap, pos: Optional[Positiona
     scale = 1.0 / math.sqrt(dk)
     out = np.zeros((b, n, hq, dv))
     lse = np.zeros((b, n, hq))
-    for qi in range(n):
+    for qi in (range(n) if rows is None else rows):
         lv, js, dists = _entries(qi, a, cache)
         if len(lv) == 0:
             raise RuntimeError(f"query {qi} has no visible entries")
@@ -222,7 +223,7 @@ def forward(q, k_levels, v_levels, fmap, cache, softcap, pos: Optional[Positiona
 
 
 def backward(q, k_levels, v_levels, out, lse, dout, fmap, cache, softcap,
-             pos: Optional[Positional] = None, dlse=None, store=identity):
+             pos: Optional[Positional] = None, dlse=None, store=identity, rows=None):
     """Explicit float64 VJP at the packed boundary (reference.py:1222-1672):
     P = exp(S - lse_saved), dP = dO.V, Delta = sum(dO*O) - dlse,
     dS = P (dP - Delta), dX = dS (1 - tanh^2), dQ = scale dX K, dK = scale dX^T Q,
@@ -245,7 +246,7 @@ def backward(q, k_levels, v_levels, out, lse, dout, fmap, cache, softcap,
     dkl = [np.zeros(kl.shape) for kl in k_levels]
     dvl = [np.zeros(vl.shape) for vl in v_levels]
     drel = np.zeros(pos.rel.shape) if pos.mode == "relative" else None
-    for qi in range(n):
+    for qi in (range(n) if rows is None else rows):
         lv, js, dists = _entries(qi, a, cache)
         kent = _gather(k_levels, lv, js)
         vent = np.repeat(_gather(v_levels, lv, js), e, axis=2)

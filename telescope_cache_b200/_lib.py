@@ -114,6 +114,8 @@ def lib():
             fn = getattr(handle, name)
             fn.argtypes = args
             fn.restype = ctypes.c_int
+        handle.tc_launch_count.argtypes = []
+        handle.tc_launch_count.restype = ctypes.c_int64
         _LIB = handle
     return _LIB
 
@@ -124,6 +126,11 @@ _ERRORS = {
     TC_ERR_CUDA: RuntimeError,
     TC_ERR_SCHEDULE: ValueError,
 }
+
+
+def launch_count():
+    """CUDA kernels launched by the library so far (tc_launch_count)."""
+    return int(lib().tc_launch_count())
 
 
 def check(rc, what):

@@ -9,6 +9,7 @@ int attn_bwd_simt(const AttnParams& p, int dtype, cudaStream_t st);
 int attn_fwd_tc(const AttnParams& p, int dtype, cudaStream_t st);
 int attn_bwd_tc(const AttnParams& p, int dtype, cudaStream_t st);
 bool tc_supported(const AttnParams& p, int dtype);
+bool tc_bwd_supported(const AttnParams& p, int dtype);
 }  // namespace tc
 
 using namespace tc;
@@ -57,7 +58,7 @@ extern "C" int tc_attn_bwd(const tc_attn_args* a, const tc_schedule* s, void* st
   if (!a->o || !a->dout || !a->lse || !a->delta || !a->dq || !a->dk || !a->dv) return TC_ERR_ARG;
   if (a->position_mode == TC_POS_ROPE && (!a->rope_cos || !a->rope_sin)) return TC_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
-  const bool tc_ok = tc_supported(p, a->dtype);
+  const bool tc_ok = tc_bwd_supported(p, a->dtype);
   if (a->impl == 2 && !tc_ok) return TC_ERR_UNSUPPORTED;
   if (a->impl != 1 && tc_ok) return attn_bwd_tc(p, a->dtype, st);
   return attn_bwd_simt(p, a->dtype, st);

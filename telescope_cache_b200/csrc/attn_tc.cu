@@ -1,12 +1,424 @@
-// Tensor-core (tcgen05 / TMEM / TMA) Phase-2 attention for sm_100a.
-// Placeholder until the kernels land: reports "unsupported" so the dispatcher
-// uses the SIMT kernels.
+// Tensor-core Phase-2 attention for sm_100a: tcgen05 MMAs with fp32
+// accumulators in TMEM, operands staged by TMA (128-byte swizzle, no
+// multicast), warp-specialised pipeline.  bf16/f16, Dk = Dv = 128.
+//
+// Forward CTA = 128 query rows of one query head.  It walks every level's
+// O(1) hull (fwd_hull) in 128-node tiles:
+//   warp 0      TMA producer: Q once, then K/V tiles into a 2-stage ring
+//   warp 1      MMA issuer:   S_j = Q K_j^T into TMEM (double buffered),
+//                             O += P_{j-1} V_{j-1} (P from shared memory)
+//   warps 4..7  softmax:      one thread per query row (= TMEM lane):
+//                             exact per-row level mask, softcap, online
+//                             softmax in log2 units with lazy O rescaling,
+//                             P -> shared memory (bf16), final O / l, lse.
+// Every mbarrier wait is bounded (see tc_ptx.cuh); a timeout sets
+// TC_DEV_WAIT_TIMEOUT in the device status word and the CTA drains.
+#include <cudaTypedefs.h>
+
+#include <type_traits>
+
 #include "attn_common.cuh"
+#include "tc_ptx.cuh"
 
 namespace tc {
+namespace {
 
-bool tc_supported(const AttnParams&, int) { return false; }
-int attn_fwd_tc(const AttnParams&, int, cudaStream_t) { return TC_ERR_UNSUPPORTED; }
+using namespace ptx;
+
+constexpr int BQ = 128, BK = 128, HD = 128, NS = 2;
+constexpr int TILE = 128 * 128 * 2;      // one 128 x 128 16-bit tile
+constexpr int KBLK = 128 * 128;          // one 64-column K-block of a tile
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescale = 8.f;          // lazy rescale threshold, log2 units
+constexpr int kFwdSmem = TILE * (1 + 2 * NS + 1) + 1024 + 256;
+
+struct TcParams {
+  int N, Hq, Hkv, E;
+  float scale, cap;
+  int has_cap;
+  void* out;
+  float* lse;
+  int32_t* status;
+  Sched s;
+};
+
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float exp2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// The sequence of (level, first node) KV tiles a query block visits: every
+// level's hull [lo(q0), hi(q1 - 1)) cut into 128-node tiles.  All roles walk
+// the identical sequence.
+struct TileWalk {
+  int lev, k0, hi, q0, q1;
+  __device__ bool next_level(const Sched& s) {
+    while (++lev < s.nl) {
+      int lo, h;
+      fwd_hull(q0, q1, lev, s, &lo, &h);
+      if (lo < h) {
+        k0 = lo;
+        hi = h;
+        return true;
+      }
+    }
+    return false;
+  }
+  __device__ bool start(const Sched& s) {
+    lev = -1;
+    return next_level(s);
+  }
+  __device__ bool advance(const Sched& s) {
+    k0 += BK;
+    return k0 < hi ? true : next_level(s);
+  }
+};
+
+template <typename T> struct Pack2;
+template <> struct Pack2<__nv_bfloat16> {
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+template <> struct Pack2<__half> {
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256, 1)
+    fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                  const __grid_constant__ CUtensorMap tmv, TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* q_s = sm;
+  uint8_t* k_s = q_s + TILE;
+  uint8_t* v_s = k_s + NS * TILE;
+  uint8_t* p_s = v_s + NS * TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + TILE);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + NS;
+  uint64_t* s_full = kv_empty + NS;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* o_done = p_full + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(o_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * BQ, hq = blockIdx.y, b = blockIdx.z;
+  const int hkv = hq / p.E;
+  const int q1 = min(q0 + BQ, p.N);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmq);
+    prefetch_tmap(&tmk);
+    prefetch_tmap(&tmv);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  int32_t* status = p.status;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      mbar_expect_tx(q_full, TILE);
+      tma_load_4d(q_s, &tmq, 0, hq, q0, b, q_full);
+      tma_load_4d(q_s + KBLK, &tmq, 64, hq, q0, b, q_full);
+      TileWalk it{-1, 0, 0, q0, q1};
+      bool ok = it.start(p.s);
+      for (int j = 0; ok; ++j, ok = it.advance(p.s)) {
+        const int st = j % NS;
+        if (j >= NS && !mbar_wait(&kv_empty[st], ((j / NS) - 1) & 1, abort_flag, status)) break;
+        mbar_expect_tx(&kv_full[st], 2 * TILE);
+        const int row = p.s.off[it.lev] + it.k0;
+        uint8_t* kd = k_s + st * TILE;
+        uint8_t* vd = v_s + st * TILE;
+        tma_load_4d(kd, &tmk, 0, hkv, row, b, &kv_full[st]);
+        tma_load_4d(kd + KBLK, &tmk, 64, hkv, row, b, &kv_full[st]);
+        tma_load_4d(vd, &tmv, 0, hkv, row, b, &kv_full[st]);
+        tma_load_4d(vd + KBLK, &tmv, 64, hkv, row, b, &kv_full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+      constexpr uint32_t kIdQK = idesc_f16(128, 128, fmt, 0, 0);
+      constexpr uint32_t kIdPV = idesc_f16(128, 128, fmt, 0, 1);
+      const uint32_t qa = smem_addr(q_s), pa = smem_addr(p_s);
+      auto issue_pv = [&](int t) {
+        const uint32_t va = smem_addr(v_s + (t % NS) * TILE);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = sdesc_sw128(pa + (kk >> 2) * KBLK + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(va + kk * 2048, KBLK, 1024);
+          mma_f16(tmem + 256, ad, bd, kIdPV, (t > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(o_done);
+        mma_commit(&kv_empty[t % NS]);
+      };
+      bool alive = mbar_wait(q_full, 0, abort_flag, status);
+      tc_fence_after();
+      TileWalk it{-1, 0, 0, q0, q1};
+      bool ok = alive && it.start(p.s);
+      int j = 0;
+      for (; ok; ++j, ok = it.advance(p.s)) {
+        const int st = j % NS, bb = j & 1;
+        if (!mbar_wait(&kv_full[st], (j / NS) & 1, abort_flag, status)) { alive = false; break; }
+        if (j >= 2 && !mbar_wait(&s_free[bb], ((j >> 1) - 1) & 1, abort_flag, status)) { alive = false; break; }
+        tc_fence_after();
+        const uint32_t ka = smem_addr(k_s + st * TILE);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = sdesc_sw128(qa + (kk >> 2) * KBLK + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(ka + (kk >> 2) * KBLK + (kk & 3) * 32, 16, 1024);
+          mma_f16(tmem + bb * 128, ad, bd, kIdQK, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[bb]);
+        if (j >= 1) {
+          if (!mbar_wait(p_full, (j - 1) & 1, abort_flag, status)) { alive = false; break; }
+          tc_fence_after();
+          issue_pv(j - 1);
+        }
+      }
+      if (alive && j >= 1 && mbar_wait(p_full, (j - 1) & 1, abort_flag, status)) {
+        tc_fence_after();
+        issue_pv(j - 1);
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- softmax / epilogue: one query row per thread ----------------
+    const int r = threadIdx.x - 128;
+    const int q = q0 + r;
+    const bool row_ok = q < p.N;
+    const uint32_t lane_base = (uint32_t)((warp - 4) * 32) << 16;
+    const float kq = p.has_cap ? p.scale / p.cap : p.scale * kLog2e;
+    const float kc = p.cap * kLog2e;
+    float m_used = -INFINITY, ell = 0.f;
+    int lo = 0, hi = 0, cur = -1;
+    TileWalk it{-1, 0, 0, q0, q1};
+    bool ok = it.start(p.s);
+    int j = 0;
+    bool alive = true;
+    float sv[128];
+    for (; ok; ++j, ok = it.advance(p.s)) {
+      if (it.lev != cur) {
+        cur = it.lev;
+        lo = hi = 0;
+        if (row_ok) {
+          level_bounds_raw(q, cur, p.s, &lo, &hi);
+          if (lo >= hi) lo = hi = 0;
+        }
+      }
+      const int bb = j & 1;
+      alive = __all_sync(0xffffffffu, mbar_wait(&s_full[bb], (j >> 1) & 1, abort_flag, status));
+      if (!alive) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(tmem + lane_base + bb * 128 + c4 * 32, sv + 32 * c4);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_free[bb]);
+      const int jlo = lo - it.k0, jhi = hi - it.k0;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        float x = sv[c] * kq;
+        if (p.has_cap) x = tanh_fast(x) * kc;
+        x = (c >= jlo && c < jhi) ? x : -INFINITY;
+        sv[c] = x;
+        mx = fmaxf(mx, x);
+      }
+      bool rescale = false;
+      float alpha = 1.f;
+      if (mx > -INFINITY) {
+        if (m_used == -INFINITY) {
+          m_used = mx;
+        } else if (mx > m_used + kRescale) {
+          alpha = exp2_fast(m_used - mx);
+          m_used = mx;
+          rescale = true;
+        }
+      }
+      if (j >= 1) {
+        alive = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, abort_flag, status));
+        if (!alive) break;
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        ell *= alpha;
+        tc_fence_after();
+        float ov[32];
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          tmem_ld32(tmem + lane_base + 256 + c4 * 32, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+          tmem_st32(tmem + lane_base + 256 + c4 * 32, ov);
+        }
+        tmem_wait_st();
+      }
+      float sum = 0.f;
+      const bool live = m_used > -INFINITY;
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {
+        float pv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          pv[i] = live ? exp2_fast(sv[c8 * 8 + i] - m_used) : 0.f;
+          sum += pv[i];
+        }
+        uint4 w;
+        w.x = Pack2<T>::pack(pv[0], pv[1]);
+        w.y = Pack2<T>::pack(pv[2], pv[3]);
+        w.z = Pack2<T>::pack(pv[4], pv[5]);
+        w.w = Pack2<T>::pack(pv[6], pv[7]);
+        *reinterpret_cast<uint4*>(p_s + sw128_offset(r, c8 * 8, 128)) = w;
+      }
+      ell += sum;
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (alive && j >= 1) {
+      alive = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, abort_flag, status));
+    }
+    if (alive && j >= 1) {
+      tc_fence_after();
+      const float inv = ell > 0.f ? 1.f / ell : 0.f;
+      T* out = static_cast<T*>(p.out) + (((int64_t)b * p.N + q) * p.Hq + hq) * HD;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        float ov[32];
+        tmem_ld32(tmem + lane_base + 256 + c4 * 32, ov);
+        tmem_wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 w;
+            w.x = Pack2<T>::pack(ov[i * 8 + 0] * inv, ov[i * 8 + 1] * inv);
+            w.y = Pack2<T>::pack(ov[i * 8 + 2] * inv, ov[i * 8 + 3] * inv);
+            w.z = Pack2<T>::pack(ov[i * 8 + 4] * inv, ov[i * 8 + 5] * inv);
+            w.w = Pack2<T>::pack(ov[i * 8 + 6] * inv, ov[i * 8 + 7] * inv);
+            *reinterpret_cast<uint4*>(out + c4 * 32 + i * 8) = w;
+          }
+        }
+      }
+      if (row_ok) p.lse[((int64_t)b * p.N + q) * p.Hq + hq] = (m_used + log2f(ell)) * kLn2;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side: tensor maps through the driver entry point (no libcuda link)
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// [B, S, H, 128] 16-bit tensor as a 4-D map (d, h, s, b) with 64 x 1 x 128 x 1
+// boxes and the 128-byte swizzle; rows past S read as zeros.
+int make_map(CUtensorMap* m, const void* base, int dt, int64_t B, int64_t S, int64_t H) {
+  auto fn = encode_fn();
+  if (!fn) return TC_ERR_CUDA;
+  const CUtensorMapDataType t = dt == TC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[4] = {(cuuint64_t)HD, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)HD * 2, (cuuint64_t)H * HD * 2, (cuuint64_t)S * H * HD * 2};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, t, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TC_OK : TC_ERR_CUDA;
+}
+
+}  // namespace
+
+bool tc_supported(const AttnParams& p, int dtype) {
+  return (dtype == TC_BF16 || dtype == TC_F16) && p.Dk == HD && p.Dv == HD && p.pos_mode != TC_POS_RELATIVE;
+}
+
+int attn_fwd_tc(const AttnParams& a, int dtype, cudaStream_t st) {
+  CUtensorMap mq, mk, mv;
+  if (int rc = make_map(&mq, a.q, dtype, a.B, a.N, a.Hq)) return rc;
+  if (int rc = make_map(&mk, a.k, dtype, a.B, a.total, a.Hkv)) return rc;
+  if (int rc = make_map(&mv, a.v, dtype, a.B, a.total, a.Hkv)) return rc;
+  TcParams p;
+  p.N = a.N;
+  p.Hq = a.Hq;
+  p.Hkv = a.Hkv;
+  p.E = a.E;
+  p.scale = a.scale;
+  p.cap = a.has_cap ? a.cap : 1.f;
+  p.has_cap = a.has_cap;
+  p.out = a.out;
+  p.lse = a.lse;
+  p.status = a.status;
+  p.s = a.s;
+  dim3 grid((a.N + BQ - 1) / BQ, a.Hq, a.B);
+  if (dtype == TC_BF16) {
+    auto k = fwd_tc_kernel<__nv_bfloat16>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem) != cudaSuccess)
+      return TC_ERR_CUDA;
+    k<<<grid, 256, kFwdSmem, st>>>(mq, mk, mv, p);
+  } else {
+    auto k = fwd_tc_kernel<__half>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem) != cudaSuccess)
+      return TC_ERR_CUDA;
+    k<<<grid, 256, kFwdSmem, st>>>(mq, mk, mv, p);
+  }
+  return launch_status();
+}
+
+bool tc_bwd_supported(const AttnParams&, int) { return false; }
+
 int attn_bwd_tc(const AttnParams&, int, cudaStream_t) { return TC_ERR_UNSUPPORTED; }
 
 }  // namespace tc

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/telescope_cache.h"
 
 #define TC_HD __host__ __device__ __forceinline__
@@ -166,9 +168,18 @@ TC_HD int bin_base(int l, const int* lo, const int* hi) {
 // launch plumbing
 // ---------------------------------------------------------------------------
 
+// Kernels launched by this library since load (tc_launch_count): each
+// launch site reports through launch_status() right after its launch.
+inline std::atomic<long long>& launch_counter() {
+  static std::atomic<long long> n{0};
+  return n;
+}
+
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+  if (e != cudaSuccess) return TC_ERR_CUDA;
+  launch_counter().fetch_add(1, std::memory_order_relaxed);
+  return TC_OK;
 }
 
 inline int dtype_size(int dt) { return dt == TC_F32 ? 4 : 2; }

@@ -58,7 +58,7 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
     const T* src = static_cast<const T*>(isk ? a.k_t : a.v_t);
     const float x = to_f(src[((int64_t)b * a.Hkv + h) * D + dd]);
     float y = x;
-    if (K > 0 && (isk ? a.conv_k : a.conv_v)) {
+    if (K > 0) {
       T* cs = static_cast<T*>(isk ? a.conv_k : a.conv_v);
       const void* w = isk ? a.k_conv_w : a.v_conv_w;
       const int C = a.Hkv * D;
@@ -288,8 +288,13 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
 extern "C" int tc_decode_step(const tc_decode_args* a, void* stream) {
   if (!a || a->B <= 0 || a->Hq <= 0 || a->Hkv <= 0 || a->Hq % a->Hkv || a->Dk <= 0 || a->Dv <= 0 ||
       a->num_levels < 1 || a->num_levels > TC_MAX_LEVELS || a->t < 0 || !a->ring_k || !a->ring_v ||
-      !a->ring_w || !a->q_t || !a->k_t || !a->v_t || !a->out || !a->lse)
+      !a->ring_w || !a->q_t || !a->out || !a->lse || a->mode < 0 || a->mode > 2)
     return TC_ERR_ARG;
+  if (a->mode != TC_DECODE_ATTEND) {
+    if (!a->k_t || !a->v_t) return TC_ERR_ARG;
+    if (a->conv_k_width > 0 && (!a->k_conv_w || !a->v_conv_w)) return TC_ERR_ARG;
+    if (a->conv_k_width > 1 && (!a->conv_k || !a->conv_v)) return TC_ERR_ARG;
+  }
   const int E = a->Hq / a->Hkv;
   if (E > MAXE || a->conv_k_width > 17 || (a->position_mode == TC_POS_RELATIVE && a->d_rel > 32))
     return TC_ERR_UNSUPPORTED;

@@ -9,6 +9,8 @@ using namespace tc;
 
 extern "C" int tc_version(void) { return 1; }
 
+extern "C" int64_t tc_launch_count(void) { return launch_counter().load(); }
+
 static int fill_schedule(const int32_t* act, int nl, int32_t cache, int32_t n, tc_schedule* out) {
   if (nl < 1 || nl > TC_MAX_LEVELS || cache <= 0 || n <= 0 || act[0] != 0) return TC_ERR_ARG;
   memset(out, 0, sizeof(*out));

@@ -24,6 +24,7 @@ def test_library_loads_and_exports_every_declared_symbol():
         assert hasattr(lib, n), n
     assert set(names) == set(_lib.SIGNATURES), set(names) ^ set(_lib.SIGNATURES)
     assert lib.tc_version() == 1
+    assert hasattr(lib, "tc_launch_count") and _lib.launch_count() >= 0
 
 
 def test_struct_sizes_match_header():
