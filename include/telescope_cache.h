@@ -228,6 +228,20 @@ int tc_attn_fwd(const tc_attn_args* a, const tc_schedule* s, void* stream);
  * and dq/dk are rotated back by R(-p) in fp32 before the single cast. */
 int tc_attn_bwd(const tc_attn_args* a, const tc_schedule* s, void* stream);
 
+/* Status of tc_attn_bwd_noalloc when B * N * Hq exceeds its fixed scratch. */
+#define TC_ERR_SCRATCH_LIMIT 5
+
+/* tc_attn_bwd for callers that cannot allocate device memory (a framework or
+ * serving engine whose own pool has reserved the GPU, a host runtime that only
+ * hands out buffers it owns).  No counterpart in the reference: it exists only
+ * for this C ABI.  Same arguments as tc_attn_bwd except that a->delta is
+ * ignored: the Delta scratch lives in a fixed 2^22-float (16 MiB) device array
+ * inside the library, held by every GPU that loads it, so B * N * Hq must be
+ * <= 4194304 (else TC_ERR_SCRATCH_LIMIT).  Nothing is allocated.  The first
+ * call on a device looks up the array's address (call it before any stream
+ * capture); calls that overlap on the GPU share the array and race. */
+int tc_attn_bwd_noalloc(const tc_attn_args* a, const tc_schedule* s, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* post-ops                                                                  */
 /* ------------------------------------------------------------------------ */

@@ -1,6 +1,8 @@
 // C-ABI entry points of the Phase-2 attention: argument checks and the choice
 // between the tensor-core kernels (bf16/f16, Dk = Dv = 128) and the SIMT
 // kernels (every other shape and the fp32 parity mode).
+#include <mutex>
+
 #include "attn_common.cuh"
 
 namespace tc {
@@ -57,6 +59,69 @@ extern "C" int tc_attn_bwd(const tc_attn_args* a, const tc_schedule* s, void* st
   if (int rc = make_params(a, s, &p)) return rc;
   if (!a->o || !a->dout || !a->lse || !a->delta || !a->dq || !a->dk || !a->dv) return TC_ERR_ARG;
   if (a->position_mode == TC_POS_ROPE && (!a->rope_cos || !a->rope_sin)) return TC_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool tc_ok = tc_bwd_supported(p, a->dtype);
+  if (a->impl == 2 && !tc_ok) return TC_ERR_UNSUPPORTED;
+  if (a->impl != 1 && tc_ok) return attn_bwd_tc(p, a->dtype, st);
+  return attn_bwd_simt(p, a->dtype, st);
+}
+
+// ---------------------------------------------------------------------------
+// Backward without any device allocation by the caller or the library.
+//
+// Some callers cannot call cudaMalloc: a serving engine or framework that has
+// reserved the GPU's memory in its own pool up front (a raw cudaMalloc then
+// fails, and cudaFree synchronises the whole device), or a host runtime bound
+// over this C ABI that only hands out buffers it owns.  tc_attn_bwd needs one
+// scratch buffer beyond its inputs and outputs, the per-row Delta
+// (rowsum(dO * O) - dlse, [B, N, Hq] f32).  This variant keeps that scratch in
+// the fixed device array below instead, so the caller passes only inputs and
+// outputs.
+//
+// The array holds kNoAllocMaxRows floats (16 MiB).  It is part of this
+// library's device image, so every GPU that loads the library holds it until
+// the process exits.  Host code cannot use the array's name as a device
+// address; the first call on each device looks the address up with
+// cudaGetSymbolAddress while that device is current, caches it, and passes it
+// to the kernels.  That first call therefore does one-time set-up and should
+// come before any stream capture.  Every call shares the one array: Delta is
+// fully rewritten by each call before it is read, and calls that overlap on
+// the GPU (on different streams) race on it.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t kNoAllocMaxRows = int64_t(1) << 22;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) float g_noalloc_delta[kNoAllocMaxRows];
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_delta_addr[kNoAllocMaxDevices] = {};
+
+int noalloc_delta(float** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return TC_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_delta_addr[dev]) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_noalloc_delta) != cudaSuccess || !addr) return TC_ERR_CUDA;
+    g_noalloc_delta_addr[dev] = static_cast<float*>(addr);
+  }
+  *out = g_noalloc_delta_addr[dev];
+  return TC_OK;
+}
+
+}  // namespace
+
+extern "C" int tc_attn_bwd_noalloc(const tc_attn_args* a, const tc_schedule* s, void* stream) {
+  AttnParams p;
+  if (int rc = make_params(a, s, &p)) return rc;
+  if (!a->o || !a->dout || !a->lse || !a->dq || !a->dk || !a->dv) return TC_ERR_ARG;
+  if (a->position_mode == TC_POS_ROPE && (!a->rope_cos || !a->rope_sin)) return TC_ERR_ARG;
+  if ((int64_t)a->B * a->N * a->Hq > kNoAllocMaxRows) return TC_ERR_SCRATCH_LIMIT;
+  float* delta = nullptr;
+  if (int rc = noalloc_delta(&delta)) return rc;
+  p.delta = delta;
   cudaStream_t st = (cudaStream_t)stream;
   const bool tc_ok = tc_bwd_supported(p, a->dtype);
   if (a->impl == 2 && !tc_ok) return TC_ERR_UNSUPPORTED;
