@@ -579,6 +579,12 @@ int attn_fwd_simt(const AttnParams& p, int dtype, cudaStream_t st) {
   return TC_ERR_ARG;
 }
 
+int delta_launch(const AttnParams& p, int dtype, cudaStream_t st) {
+  const int64_t rows = (int64_t)p.B * p.N * p.Hq;
+  TC_DISPATCH(dtype, T, { delta_kernel<T><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(p, rows); });
+  return launch_status();
+}
+
 int attn_bwd_simt(const AttnParams& p, int dtype, cudaStream_t st) {
   const int dm = simt_dm(p.Dk, p.Dv);
   if (!dm || (p.pos_mode == TC_POS_RELATIVE && p.d_rel > kMaxRel)) return TC_ERR_UNSUPPORTED;

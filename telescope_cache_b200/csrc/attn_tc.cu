@@ -13,23 +13,17 @@
 //                             P -> shared memory (bf16), final O / l, lse.
 // Every mbarrier wait is bounded (see tc_ptx.cuh); a timeout sets
 // TC_DEV_WAIT_TIMEOUT in the device status word and the CTA drains.
-#include <cudaTypedefs.h>
-
-#include <type_traits>
-
-#include "attn_common.cuh"
-#include "tc_ptx.cuh"
+#include "tc_common.cuh"
 
 namespace tc {
 namespace {
 
 using namespace ptx;
+using namespace tcx;
 
-constexpr int BQ = 128, BK = 128, HD = 128, NS = 2;
+constexpr int BQ = 128, BK = 128, NS = 2;
 constexpr int TILE = 128 * 128 * 2;      // one 128 x 128 16-bit tile
 constexpr int KBLK = 128 * 128;          // one 64-column K-block of a tile
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescale = 8.f;          // lazy rescale threshold, log2 units
 constexpr int kFwdSmem = TILE * (1 + 2 * NS + 1) + 1024 + 256;
 
@@ -41,58 +35,6 @@ struct TcParams {
   float* lse;
   int32_t* status;
   Sched s;
-};
-
-__device__ __forceinline__ float tanh_fast(float x) {
-  float y;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-__device__ __forceinline__ float exp2_fast(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// The sequence of (level, first node) KV tiles a query block visits: every
-// level's hull [lo(q0), hi(q1 - 1)) cut into 128-node tiles.  All roles walk
-// the identical sequence.
-struct TileWalk {
-  int lev, k0, hi, q0, q1;
-  __device__ bool next_level(const Sched& s) {
-    while (++lev < s.nl) {
-      int lo, h;
-      fwd_hull(q0, q1, lev, s, &lo, &h);
-      if (lo < h) {
-        k0 = lo;
-        hi = h;
-        return true;
-      }
-    }
-    return false;
-  }
-  __device__ bool start(const Sched& s) {
-    lev = -1;
-    return next_level(s);
-  }
-  __device__ bool advance(const Sched& s) {
-    k0 += BK;
-    return k0 < hi ? true : next_level(s);
-  }
-};
-
-template <typename T> struct Pack2;
-template <> struct Pack2<__nv_bfloat16> {
-  static __device__ __forceinline__ uint32_t pack(float a, float b) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&v);
-  }
-};
-template <> struct Pack2<__half> {
-  static __device__ __forceinline__ uint32_t pack(float a, float b) {
-    __half2 v = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&v);
-  }
 };
 
 template <typename T>
@@ -157,7 +99,7 @@ __global__ void __launch_bounds__(256, 1)
       mbar_expect_tx(q_full, TILE);
       tma_load_4d(q_s, &tmq, 0, hq, q0, b, q_full);
       tma_load_4d(q_s + KBLK, &tmq, 64, hq, q0, b, q_full);
-      TileWalk it{-1, 0, 0, q0, q1};
+      TileWalk it{-1, 0, 0, q0, q1, BK};
       bool ok = it.start(p.s);
       for (int j = 0; ok; ++j, ok = it.advance(p.s)) {
         const int st = j % NS;
@@ -192,7 +134,7 @@ __global__ void __launch_bounds__(256, 1)
       };
       bool alive = mbar_wait(q_full, 0, abort_flag, status);
       tc_fence_after();
-      TileWalk it{-1, 0, 0, q0, q1};
+      TileWalk it{-1, 0, 0, q0, q1, BK};
       bool ok = alive && it.start(p.s);
       int j = 0;
       for (; ok; ++j, ok = it.advance(p.s)) {
@@ -229,7 +171,7 @@ __global__ void __launch_bounds__(256, 1)
     const float kc = p.cap * kLog2e;
     float m_used = -INFINITY, ell = 0.f;
     int lo = 0, hi = 0, cur = -1;
-    TileWalk it{-1, 0, 0, q0, q1};
+    TileWalk it{-1, 0, 0, q0, q1, BK};
     bool ok = it.start(p.s);
     int j = 0;
     bool alive = true;
@@ -349,36 +291,6 @@ __global__ void __launch_bounds__(256, 1)
   }
 }
 
-// ---------------------------------------------------------------------------
-// host side: tensor maps through the driver entry point (no libcuda link)
-// ---------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
-  return fn;
-}
-
-// [B, S, H, 128] 16-bit tensor as a 4-D map (d, h, s, b) with 64 x 1 x 128 x 1
-// boxes and the 128-byte swizzle; rows past S read as zeros.
-int make_map(CUtensorMap* m, const void* base, int dt, int64_t B, int64_t S, int64_t H) {
-  auto fn = encode_fn();
-  if (!fn) return TC_ERR_CUDA;
-  const CUtensorMapDataType t = dt == TC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  cuuint64_t dims[4] = {(cuuint64_t)HD, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
-  cuuint64_t strides[3] = {(cuuint64_t)HD * 2, (cuuint64_t)H * HD * 2, (cuuint64_t)S * H * HD * 2};
-  cuuint32_t box[4] = {64, 1, 128, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(m, t, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? TC_OK : TC_ERR_CUDA;
-}
-
 }  // namespace
 
 bool tc_supported(const AttnParams& p, int dtype) {
@@ -387,9 +299,9 @@ bool tc_supported(const AttnParams& p, int dtype) {
 
 int attn_fwd_tc(const AttnParams& a, int dtype, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
-  if (int rc = make_map(&mq, a.q, dtype, a.B, a.N, a.Hq)) return rc;
-  if (int rc = make_map(&mk, a.k, dtype, a.B, a.total, a.Hkv)) return rc;
-  if (int rc = make_map(&mv, a.v, dtype, a.B, a.total, a.Hkv)) return rc;
+  if (int rc = make_map(&mq, a.q, dtype, a.B, a.N, a.Hq, 128)) return rc;
+  if (int rc = make_map(&mk, a.k, dtype, a.B, a.total, a.Hkv, 128)) return rc;
+  if (int rc = make_map(&mv, a.v, dtype, a.B, a.total, a.Hkv, 128)) return rc;
   TcParams p;
   p.N = a.N;
   p.Hq = a.Hq;
@@ -416,9 +328,5 @@ int attn_fwd_tc(const AttnParams& a, int dtype, cudaStream_t st) {
   }
   return launch_status();
 }
-
-bool tc_bwd_supported(const AttnParams&, int) { return false; }
-
-int attn_bwd_tc(const AttnParams&, int, cudaStream_t) { return TC_ERR_UNSUPPORTED; }
 
 }  // namespace tc

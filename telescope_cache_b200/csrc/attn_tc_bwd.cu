@@ -1,0 +1,612 @@
+// Tensor-core Phase-2 backward for sm_100a (bf16/f16, Dk = Dv = 128): the
+// reference's two passes (reference.py:1494-1664), each recomputing S and dP
+// on tcgen05 with fp32 accumulators in TMEM and operands staged by TMA.
+//
+// Pass A (Q-owned dQ): CTA = 128 query rows of one query head walking every
+//   level's hull in 64-node tiles.  Per tile: S = Q K^T and dP = dO V^T into
+//   double-buffered TMEM; one thread per query row rebuilds P from the saved
+//   lse with the exact level mask, forms dX = P (dP - Delta) softcap' into
+//   shared memory, and the MMA warp accumulates dQ += dX K in TMEM.  The
+//   epilogue scales, rotates back (RoPE) and stores dQ.
+// Pass B (KV-owned dK/dV): CTA = 128 nodes of one level of one KV head walking
+//   the nodes' query hull (bwd_hull) in 64-query steps, every query head of
+//   the GQA group.  Per step: S^T = K Q^T, dP^T = V dO^T; one thread per node
+//   forms P^T and dX^T; dV += P^T dO and dK += dX^T Q accumulate in TMEM.
+// Neither pass needs scratch memory beyond Delta, and neither uses atomics.
+#include "tc_common.cuh"
+
+namespace tc {
+
+int delta_launch(const AttnParams& p, int dtype, cudaStream_t st);
+
+namespace {
+
+using namespace ptx;
+using namespace tcx;
+
+constexpr int T128 = 128 * 128 * 2;  // [128 rows x 128] 16-bit tile, two 64-col blocks
+constexpr int T64 = 64 * 128 * 2;    // [64 rows x 128] tile
+constexpr int B128 = 128 * 128;      // one 64-col block of a 128-row tile
+constexpr int B64 = 64 * 128;        // one 64-col block of a 64-row tile
+constexpr int kSmemA = 2 * T128 + 4 * T64 + 128 * 128 + 1024 + 256;
+constexpr int kSmemB = 2 * T128 + 4 * T64 + 2 * 128 * 128 + 4 * 64 * 4 + 1024 + 256;
+
+struct BwdParams {
+  int N, Hq, Hkv, E;
+  float scale, cap;
+  int has_cap, rope;
+  const float* lse;
+  const float* delta;
+  const float* cos_t;
+  const float* sin_t;
+  void* dq;
+  void* dk;
+  void* dv;
+  int32_t* status;
+  Sched s;
+  int tiles[TC_MAX_LEVELS + 1];  // Pass B: prefix count of 128-node tiles per level
+};
+
+struct BwdScalars {
+  float kq, kc;
+  __device__ BwdScalars(const BwdParams& p)
+      : kq(p.has_cap ? p.scale / p.cap : p.scale * kLog2e), kc(p.cap * kLog2e) {}
+  // x: raw accumulator S; returns the log2-domain logit and the softcap derivative.
+  __device__ __forceinline__ void logit(float s, int has_cap, float* l2, float* g) const {
+    const float x = s * kq;
+    if (has_cap) {
+      const float t = tanh_fast(x);
+      *l2 = t * kc;
+      *g = 1.f - t * t;
+    } else {
+      *l2 = x;
+      *g = 1.f;
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Pass A
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256, 1)
+    bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmg,
+                     const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* q_s = sm;
+  uint8_t* g_s = q_s + T128;
+  uint8_t* k_s = g_s + T128;   // [2] x T64
+  uint8_t* v_s = k_s + 2 * T64;
+  uint8_t* x_s = v_s + 2 * T64;  // dX [128 x 64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(x_s + 128 * 128);
+  uint64_t* qg_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = bars + 3;
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_free = bars + 7;
+  uint64_t* x_full = bars + 9;
+  uint64_t* x_free = bars + 10;
+  uint64_t* dq_done = bars + 11;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * 128, hq = blockIdx.y, b = blockIdx.z;
+  const int hkv = hq / p.E;
+  const int q1 = min(q0 + 128, p.N);
+  int32_t* status = p.status;
+
+  if (threadIdx.x == 0) {
+    mbar_init(qg_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    mbar_init(x_full, 128);
+    mbar_init(x_free, 1);
+    mbar_init(dq_done, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(qg_full, 2 * T128);
+      tma_load_4d(q_s, &tmq, 0, hq, q0, b, qg_full);
+      tma_load_4d(q_s + B128, &tmq, 64, hq, q0, b, qg_full);
+      tma_load_4d(g_s, &tmg, 0, hq, q0, b, qg_full);
+      tma_load_4d(g_s + B128, &tmg, 64, hq, q0, b, qg_full);
+      TileWalk it{-1, 0, 0, q0, q1, 64};
+      bool ok = it.start(p.s);
+      for (int j = 0; ok; ++j, ok = it.advance(p.s)) {
+        const int st = j & 1;
+        if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1, abort_flag, status)) break;
+        mbar_expect_tx(&kv_full[st], 2 * T64);
+        const int row = p.s.off[it.lev] + it.k0;
+        tma_load_4d(k_s + st * T64, &tmk, 0, hkv, row, b, &kv_full[st]);
+        tma_load_4d(k_s + st * T64 + B64, &tmk, 64, hkv, row, b, &kv_full[st]);
+        tma_load_4d(v_s + st * T64, &tmv, 0, hkv, row, b, &kv_full[st]);
+        tma_load_4d(v_s + st * T64 + B64, &tmv, 64, hkv, row, b, &kv_full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t kIdS = idesc_f16(128, 64, Pack2<T>::kFmt, 0, 0);
+      constexpr uint32_t kIdQ = idesc_f16(128, 128, Pack2<T>::kFmt, 0, 1);
+      const uint32_t qa = smem_addr(q_s), ga = smem_addr(g_s), xa = smem_addr(x_s);
+      auto issue_dq = [&](int t) {
+        const uint32_t ka = smem_addr(k_s + (t & 1) * T64);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16(tmem + 256, sdesc_sw128(xa + kk * 32, 16, 1024), sdesc_sw128(ka + kk * 2048, B64, 1024), kIdQ,
+                  (t > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(x_free);
+        mma_commit(&kv_empty[t & 1]);
+      };
+      bool alive = mbar_wait(qg_full, 0, abort_flag, status);
+      tc_fence_after();
+      TileWalk it{-1, 0, 0, q0, q1, 64};
+      bool ok = alive && it.start(p.s);
+      int j = 0;
+      for (; ok; ++j, ok = it.advance(p.s)) {
+        const int st = j & 1, bb = j & 1;
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, abort_flag, status)) { alive = false; break; }
+        if (j >= 2 && !mbar_wait(&s_free[bb], ((j >> 1) - 1) & 1, abort_flag, status)) { alive = false; break; }
+        tc_fence_after();
+        const uint32_t ka = smem_addr(k_s + st * T64), va = smem_addr(v_s + st * T64);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t ao = (kk >> 2) * B128 + (kk & 3) * 32, bo = (kk >> 2) * B64 + (kk & 3) * 32;
+          mma_f16(tmem + bb * 64, sdesc_sw128(qa + ao, 16, 1024), sdesc_sw128(ka + bo, 16, 1024), kIdS,
+                  kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t ao = (kk >> 2) * B128 + (kk & 3) * 32, bo = (kk >> 2) * B64 + (kk & 3) * 32;
+          mma_f16(tmem + 128 + bb * 64, sdesc_sw128(ga + ao, 16, 1024), sdesc_sw128(va + bo, 16, 1024), kIdS,
+                  kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[bb]);
+        if (j >= 1) {
+          if (!mbar_wait(x_full, (j - 1) & 1, abort_flag, status)) { alive = false; break; }
+          tc_fence_after();
+          issue_dq(j - 1);
+        }
+      }
+      if (alive && j >= 1 && mbar_wait(x_full, (j - 1) & 1, abort_flag, status)) {
+        tc_fence_after();
+        issue_dq(j - 1);
+      }
+      mma_commit(dq_done);
+    }
+  } else if (warp >= 4) {
+    const int r = threadIdx.x - 128;
+    const int q = q0 + r;
+    const bool row_ok = q < p.N;
+    const uint32_t lane_base = (uint32_t)((warp - 4) * 32) << 16;
+    const BwdScalars sc(p);
+    const int64_t row = ((int64_t)b * p.N + q) * p.Hq + hq;
+    const float lse2 = row_ok ? p.lse[row] * kLog2e : 0.f;
+    const float dlt = row_ok ? p.delta[row] : 0.f;
+    int lo = 0, hi = 0, cur = -1;
+    TileWalk it{-1, 0, 0, q0, q1, 64};
+    bool ok = it.start(p.s);
+    bool alive = true;
+    int j = 0;
+    for (; ok; ++j, ok = it.advance(p.s)) {
+      if (it.lev != cur) {
+        cur = it.lev;
+        lo = hi = 0;
+        if (row_ok) {
+          level_bounds_raw(q, cur, p.s, &lo, &hi);
+          if (lo >= hi) lo = hi = 0;
+        }
+      }
+      const int bb = j & 1;
+      alive = __all_sync(0xffffffffu, mbar_wait(&s_full[bb], (j >> 1) & 1, abort_flag, status));
+      if (!alive) break;
+      tc_fence_after();
+      float sv[64], dp[64];
+      tmem_ld32(tmem + lane_base + bb * 64, sv);
+      tmem_ld32(tmem + lane_base + bb * 64 + 32, sv + 32);
+      tmem_ld32(tmem + lane_base + 128 + bb * 64, dp);
+      tmem_ld32(tmem + lane_base + 128 + bb * 64 + 32, dp + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_free[bb]);
+      if (j >= 1) {
+        alive = __all_sync(0xffffffffu, mbar_wait(x_free, (j - 1) & 1, abort_flag, status));
+        if (!alive) break;
+      }
+      const int jlo = lo - it.k0, jhi = hi - it.k0;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        float dx[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int c = c8 * 8 + i;
+          float l2, g;
+          sc.logit(sv[c], p.has_cap, &l2, &g);
+          const bool valid = c >= jlo && c < jhi;
+          const float pr = valid ? exp2_fast(l2 - lse2) : 0.f;
+          dx[i] = pr * (dp[c] - dlt) * g;
+        }
+        *reinterpret_cast<uint4*>(x_s + sw128_offset(r, c8 * 8, 128)) = pack8<T>(dx, 1.f);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(x_full);
+    }
+    if (alive && j >= 1) alive = __all_sync(0xffffffffu, mbar_wait(dq_done, 0, abort_flag, status));
+    if (alive) {
+      tc_fence_after();
+      float v[128];
+      if (j >= 1) {
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(tmem + lane_base + 256 + c4 * 32, v + c4 * 32);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 128; ++i) v[i] *= p.scale;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) v[i] = 0.f;
+      }
+      if (row_ok) {
+        if (p.rope) rope_inverse_row(v, p.cos_t, p.sin_t, q);
+        T* out = static_cast<T*>(p.dq) + row * HD;
+#pragma unroll
+        for (int c8 = 0; c8 < 16; ++c8) *reinterpret_cast<uint4*>(out + c8 * 8) = pack8<T>(v + c8 * 8, 1.f);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Pass B
+// ---------------------------------------------------------------------------
+struct QSteps {
+  int qb, e, qhi, E;
+  __device__ bool start(int qlo, int qhi_, int E_) {
+    qhi = qhi_;
+    E = E_;
+    e = 0;
+    qb = (qlo / 64) * 64;
+    return qlo < qhi && qb < qhi;
+  }
+  __device__ bool advance() {
+    if (++e == E) {
+      e = 0;
+      qb += 64;
+    }
+    return qb < qhi;
+  }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256, 1)
+    bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmg,
+                      const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                      BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* k_s = sm;
+  uint8_t* v_s = k_s + T128;
+  uint8_t* q_s = v_s + T128;   // [2] x T64
+  uint8_t* g_s = q_s + 2 * T64;
+  uint8_t* pt_s = g_s + 2 * T64;  // P^T  [128 x 64]
+  uint8_t* xt_s = pt_s + 128 * 128;  // dX^T [128 x 64]
+  float* lse_s = reinterpret_cast<float*>(xt_s + 128 * 128);  // [64]
+  float* dlt_s = lse_s + 64;
+  int* lo_s = reinterpret_cast<int*>(dlt_s + 64);
+  int* hi_s = lo_s + 64;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(hi_s + 64);
+  uint64_t* kv_full = bars;
+  uint64_t* q_full = bars + 1;
+  uint64_t* q_empty = bars + 3;
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_free = bars + 7;
+  uint64_t* x_full = bars + 9;
+  uint64_t* x_free = bars + 10;
+  uint64_t* kv_done = bars + 11;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  int lev = 0;
+  while (lev + 1 < p.s.nl && (int)blockIdx.x >= p.tiles[lev + 1]) ++lev;
+  const int k0 = ((int)blockIdx.x - p.tiles[lev]) * 128;
+  const int hkv = blockIdx.y, b = blockIdx.z;
+  const int nk = min(128, p.s.len[lev] - k0);
+  const int row0 = p.s.off[lev] + k0;
+  int qlo, qhi;
+  bwd_hull(k0, k0 + nk, lev, p.s, &qlo, &qhi);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int32_t* status = p.status;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    mbar_init(x_full, 128);
+    mbar_init(x_free, 1);
+    mbar_init(kv_done, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      QSteps w;
+      bool ok = w.start(qlo, qhi, p.E);
+      if (ok) {
+        mbar_expect_tx(kv_full, 2 * T128);
+        tma_load_4d(k_s, &tmk, 0, hkv, row0, b, kv_full);
+        tma_load_4d(k_s + B128, &tmk, 64, hkv, row0, b, kv_full);
+        tma_load_4d(v_s, &tmv, 0, hkv, row0, b, kv_full);
+        tma_load_4d(v_s + B128, &tmv, 64, hkv, row0, b, kv_full);
+      }
+      for (int i = 0; ok; ++i, ok = w.advance()) {
+        const int st = i & 1;
+        if (i >= 2 && !mbar_wait(&q_empty[st], ((i >> 1) - 1) & 1, abort_flag, status)) break;
+        const int hq = hkv * p.E + w.e;
+        mbar_expect_tx(&q_full[st], 2 * T64);
+        tma_load_4d(q_s + st * T64, &tmq, 0, hq, w.qb, b, &q_full[st]);
+        tma_load_4d(q_s + st * T64 + B64, &tmq, 64, hq, w.qb, b, &q_full[st]);
+        tma_load_4d(g_s + st * T64, &tmg, 0, hq, w.qb, b, &q_full[st]);
+        tma_load_4d(g_s + st * T64 + B64, &tmg, 64, hq, w.qb, b, &q_full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t kIdS = idesc_f16(128, 64, Pack2<T>::kFmt, 0, 0);
+      constexpr uint32_t kIdA = idesc_f16(128, 128, Pack2<T>::kFmt, 0, 1);
+      const uint32_t ka = smem_addr(k_s), va = smem_addr(v_s), pa = smem_addr(pt_s), xa = smem_addr(xt_s);
+      auto issue_acc = [&](int t) {
+        const uint32_t qa = smem_addr(q_s + (t & 1) * T64), ga = smem_addr(g_s + (t & 1) * T64);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+          mma_f16(tmem + 256, sdesc_sw128(pa + kk * 32, 16, 1024), sdesc_sw128(ga + kk * 2048, B64, 1024), kIdA, acc);
+          mma_f16(tmem + 384, sdesc_sw128(xa + kk * 32, 16, 1024), sdesc_sw128(qa + kk * 2048, B64, 1024), kIdA, acc);
+        }
+        mma_commit(x_free);
+        mma_commit(&q_empty[t & 1]);
+      };
+      QSteps w;
+      bool ok = w.start(qlo, qhi, p.E);
+      bool alive = true;
+      int i = 0;
+      if (ok) {
+        alive = mbar_wait(kv_full, 0, abort_flag, status);
+        ok = alive;
+      }
+      for (; ok; ++i, ok = w.advance()) {
+        const int st = i & 1, bb = i & 1;
+        if (!mbar_wait(&q_full[st], (i >> 1) & 1, abort_flag, status)) { alive = false; break; }
+        if (i >= 2 && !mbar_wait(&s_free[bb], ((i >> 1) - 1) & 1, abort_flag, status)) { alive = false; break; }
+        tc_fence_after();
+        const uint32_t qa = smem_addr(q_s + st * T64), ga = smem_addr(g_s + st * T64);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t ao = (kk >> 2) * B128 + (kk & 3) * 32, bo = (kk >> 2) * B64 + (kk & 3) * 32;
+          mma_f16(tmem + bb * 64, sdesc_sw128(ka + ao, 16, 1024), sdesc_sw128(qa + bo, 16, 1024), kIdS,
+                  kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t ao = (kk >> 2) * B128 + (kk & 3) * 32, bo = (kk >> 2) * B64 + (kk & 3) * 32;
+          mma_f16(tmem + 128 + bb * 64, sdesc_sw128(va + ao, 16, 1024), sdesc_sw128(ga + bo, 16, 1024), kIdS,
+                  kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[bb]);
+        if (i >= 1) {
+          if (!mbar_wait(x_full, (i - 1) & 1, abort_flag, status)) { alive = false; break; }
+          tc_fence_after();
+          issue_acc(i - 1);
+        }
+      }
+      if (alive && i >= 1 && mbar_wait(x_full, (i - 1) & 1, abort_flag, status)) {
+        tc_fence_after();
+        issue_acc(i - 1);
+      }
+      mma_commit(kv_done);
+    }
+  } else if (warp >= 4) {
+    const int r = threadIdx.x - 128;     // node row = TMEM lane
+    const int jn = k0 + r;               // level-local node index
+    const bool node_ok = r < nk;
+    const uint32_t lane_base = (uint32_t)((warp - 4) * 32) << 16;
+    const BwdScalars sc(p);
+    QSteps w;
+    bool ok = w.start(qlo, qhi, p.E);
+    bool alive = true;
+    int i = 0;
+    for (; ok; ++i, ok = w.advance()) {
+      const int hq = hkv * p.E + w.e;
+      named_bar(1, 128);  // everyone is done with the previous step's row data
+      if (r < 64) {
+        const int q = w.qb + r;
+        int lo = 0, hi = 0;
+        float l2 = 0.f, dl = 0.f;
+        if (q < p.N) {
+          level_bounds_raw(q, lev, p.s, &lo, &hi);
+          if (lo >= hi) lo = hi = 0;
+          const int64_t row = ((int64_t)b * p.N + q) * p.Hq + hq;
+          l2 = p.lse[row] * kLog2e;
+          dl = p.delta[row];
+        }
+        lo_s[r] = lo;
+        hi_s[r] = hi;
+        lse_s[r] = l2;
+        dlt_s[r] = dl;
+      }
+      named_bar(1, 128);
+      const int bb = i & 1;
+      alive = __all_sync(0xffffffffu, mbar_wait(&s_full[bb], (i >> 1) & 1, abort_flag, status));
+      if (!alive) break;
+      tc_fence_after();
+      float sv[64], dp[64];
+      tmem_ld32(tmem + lane_base + bb * 64, sv);
+      tmem_ld32(tmem + lane_base + bb * 64 + 32, sv + 32);
+      tmem_ld32(tmem + lane_base + 128 + bb * 64, dp);
+      tmem_ld32(tmem + lane_base + 128 + bb * 64 + 32, dp + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_free[bb]);
+      if (i >= 1) {
+        alive = __all_sync(0xffffffffu, mbar_wait(x_free, (i - 1) & 1, abort_flag, status));
+        if (!alive) break;
+      }
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        float pr[8], dx[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int c = c8 * 8 + k;
+          float l2, g;
+          sc.logit(sv[c], p.has_cap, &l2, &g);
+          const bool valid = node_ok && jn >= lo_s[c] && jn < hi_s[c];
+          pr[k] = valid ? exp2_fast(l2 - lse_s[c]) : 0.f;
+          dx[k] = pr[k] * (dp[c] - dlt_s[c]) * g;
+        }
+        const uint32_t off = sw128_offset(r, c8 * 8, 128);
+        *reinterpret_cast<uint4*>(pt_s + off) = pack8<T>(pr, 1.f);
+        *reinterpret_cast<uint4*>(xt_s + off) = pack8<T>(dx, 1.f);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(x_full);
+    }
+    if (alive && i >= 1) alive = __all_sync(0xffffffffu, mbar_wait(kv_done, 0, abort_flag, status));
+    if (alive) {
+      tc_fence_after();
+      const int64_t orow = ((int64_t)b * (p.s.off[p.s.nl]) + row0 + r) * p.Hkv + hkv;
+      float v[128];
+      // dV
+      if (i >= 1) {
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(tmem + lane_base + 256 + c4 * 32, v + c4 * 32);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int k = 0; k < 128; ++k) v[k] = 0.f;
+      }
+      if (node_ok) {
+        T* out = static_cast<T*>(p.dv) + orow * HD;
+#pragma unroll
+        for (int c8 = 0; c8 < 16; ++c8) *reinterpret_cast<uint4*>(out + c8 * 8) = pack8<T>(v + c8 * 8, 1.f);
+      }
+      // dK
+      if (i >= 1) {
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(tmem + lane_base + 384 + c4 * 32, v + c4 * 32);
+        tmem_wait_ld();
+#pragma unroll
+        for (int k = 0; k < 128; ++k) v[k] *= p.scale;
+      }
+      if (node_ok) {
+        if (p.rope && i >= 1) rope_inverse_row(v, p.cos_t, p.sin_t, ((jn + 1) << lev) - 1);
+        T* out = static_cast<T*>(p.dk) + orow * HD;
+#pragma unroll
+        for (int c8 = 0; c8 < 16; ++c8) *reinterpret_cast<uint4*>(out + c8 * 8) = pack8<T>(v + c8 * 8, 1.f);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <typename T>
+int launch_bwd(const AttnParams& a, int dtype, cudaStream_t st) {
+  CUtensorMap mq128, mg128, mk64, mv64, mq64, mg64, mk128, mv128;
+  if (int rc = make_map(&mq128, a.q, dtype, a.B, a.N, a.Hq, 128)) return rc;
+  if (int rc = make_map(&mg128, a.dout, dtype, a.B, a.N, a.Hq, 128)) return rc;
+  if (int rc = make_map(&mk64, a.k, dtype, a.B, a.total, a.Hkv, 64)) return rc;
+  if (int rc = make_map(&mv64, a.v, dtype, a.B, a.total, a.Hkv, 64)) return rc;
+  if (int rc = make_map(&mq64, a.q, dtype, a.B, a.N, a.Hq, 64)) return rc;
+  if (int rc = make_map(&mg64, a.dout, dtype, a.B, a.N, a.Hq, 64)) return rc;
+  if (int rc = make_map(&mk128, a.k, dtype, a.B, a.total, a.Hkv, 128)) return rc;
+  if (int rc = make_map(&mv128, a.v, dtype, a.B, a.total, a.Hkv, 128)) return rc;
+  BwdParams p;
+  p.N = a.N;
+  p.Hq = a.Hq;
+  p.Hkv = a.Hkv;
+  p.E = a.E;
+  p.scale = a.scale;
+  p.cap = a.has_cap ? a.cap : 1.f;
+  p.has_cap = a.has_cap;
+  p.rope = a.pos_mode == TC_POS_ROPE;
+  p.lse = a.lse;
+  p.delta = a.delta;
+  p.cos_t = a.cos_t;
+  p.sin_t = a.sin_t;
+  p.dq = a.dq;
+  p.dk = a.dk;
+  p.dv = a.dv;
+  p.status = a.status;
+  p.s = a.s;
+  p.tiles[0] = 0;
+  for (int l = 0; l < TC_MAX_LEVELS; ++l)
+    p.tiles[l + 1] = p.tiles[l] + (l < a.s.nl ? (a.s.len[l] + 127) / 128 : 0);
+  if (int rc = delta_launch(a, dtype, st)) return rc;
+  auto ka = bwd_dq_tc_kernel<T>;
+  if (cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemA) != cudaSuccess) return TC_ERR_CUDA;
+  ka<<<dim3((a.N + 127) / 128, a.Hq, a.B), 256, kSmemA, st>>>(mq128, mg128, mk64, mv64, p);
+  if (int rc = launch_status()) return rc;
+  const int ntiles = p.tiles[a.s.nl];
+  if (ntiles > 0) {
+    auto kb = bwd_dkv_tc_kernel<T>;
+    if (cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemB) != cudaSuccess)
+      return TC_ERR_CUDA;
+    kb<<<dim3(ntiles, a.Hkv, a.B), 256, kSmemB, st>>>(mq64, mg64, mk128, mv128, p);
+    if (int rc = launch_status()) return rc;
+  }
+  return TC_OK;
+}
+
+}  // namespace
+
+bool tc_bwd_supported(const AttnParams& p, int dtype) {
+  return (dtype == TC_BF16 || dtype == TC_F16) && p.Dk == HD && p.Dv == HD && p.pos_mode != TC_POS_RELATIVE;
+}
+
+int attn_bwd_tc(const AttnParams& a, int dtype, cudaStream_t st) {
+  if (dtype == TC_BF16) return launch_bwd<__nv_bfloat16>(a, dtype, st);
+  return launch_bwd<__half>(a, dtype, st);
+}
+
+}  // namespace tc

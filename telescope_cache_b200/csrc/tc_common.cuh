@@ -1,0 +1,129 @@
+// Pieces shared by the tensor-core attention kernels: constants, fast
+// transcendental instructions, bf16/f16 packing, the forward tile walk and
+// the TMA tensor maps.
+#pragma once
+
+#include <cudaTypedefs.h>
+
+#include <type_traits>
+
+#include "attn_common.cuh"
+#include "tc_ptx.cuh"
+
+namespace tc {
+namespace tcx {
+
+constexpr int HD = 128;                      // head dim of the tensor-core path
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float exp2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T> struct Pack2;
+template <> struct Pack2<__nv_bfloat16> {
+  static constexpr int kFmt = 1;
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+template <> struct Pack2<__half> {
+  static constexpr int kFmt = 0;
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float* v, float mul) {
+  uint4 w;
+  w.x = Pack2<T>::pack(v[0] * mul, v[1] * mul);
+  w.y = Pack2<T>::pack(v[2] * mul, v[3] * mul);
+  w.z = Pack2<T>::pack(v[4] * mul, v[5] * mul);
+  w.w = Pack2<T>::pack(v[6] * mul, v[7] * mul);
+  return w;
+}
+
+// The (level, first node) KV tiles a query block [q0, q1) visits: every
+// level's O(1) hull cut into `step`-node tiles, in level order.  All roles
+// of a CTA walk the identical sequence.
+struct TileWalk {
+  int lev, k0, hi, q0, q1, step;
+  __device__ bool next_level(const Sched& s) {
+    while (++lev < s.nl) {
+      int lo, h;
+      fwd_hull(q0, q1, lev, s, &lo, &h);
+      if (lo < h) {
+        k0 = lo;
+        hi = h;
+        return true;
+      }
+    }
+    return false;
+  }
+  __device__ bool start(const Sched& s) {
+    lev = -1;
+    return next_level(s);
+  }
+  __device__ bool advance(const Sched& s) {
+    k0 += step;
+    return k0 < hi ? true : next_level(s);
+  }
+};
+
+// Inverse RoPE (rotate by R(-p)) of a 128-wide fp32 row held by one thread.
+__device__ __forceinline__ void rope_inverse_row(float* v, const float* cos_t, const float* sin_t, int pos) {
+  const float* c = cos_t + (int64_t)pos * (HD / 2);
+  const float* s = sin_t + (int64_t)pos * (HD / 2);
+#pragma unroll
+  for (int i = 0; i < HD / 2; ++i) {
+    const float x1 = v[i], x2 = v[i + HD / 2];
+    const float cc = __ldg(c + i), ss = __ldg(s + i);
+    v[i] = x1 * cc + x2 * ss;
+    v[i + HD / 2] = x2 * cc - x1 * ss;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host: tensor maps through the driver entry point (no libcuda link)
+// ---------------------------------------------------------------------------
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// [B, S, H, 128] 16-bit tensor as a 4-D map (d, h, s, b) with
+// 64 x 1 x box_rows x 1 boxes and the 128-byte swizzle; rows past S read as
+// zeros.  A box lands in shared memory as box_rows rows of 128 bytes.
+inline int make_map(CUtensorMap* m, const void* base, int dt, int64_t B, int64_t S, int64_t H, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return TC_ERR_CUDA;
+  const CUtensorMapDataType t = dt == TC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[4] = {(cuuint64_t)HD, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)HD * 2, (cuuint64_t)H * HD * 2, (cuuint64_t)S * H * HD * 2};
+  cuuint32_t box[4] = {64, 1, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, t, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TC_OK : TC_ERR_CUDA;
+}
+
+}  // namespace tcx
+}  // namespace tc

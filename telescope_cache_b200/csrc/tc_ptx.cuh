@@ -41,11 +41,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after ~kWaitLimit polls (seconds), sets the CTA's
+// Bounded wait: gives up after kWaitLimit polls (well under a second), sets the CTA's
 // abort flag and the device status word, and returns false.  Once the abort
 // flag is set every later wait returns false immediately, so all roles drain
 // to the kernel's teardown instead of spinning.
-constexpr uint32_t kWaitLimit = 1u << 26;
+constexpr uint32_t kWaitLimit = 1u << 22;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatile int* abort_flag,
                                           int32_t* status) {
   uint32_t n = 0;
@@ -56,7 +56,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatil
       if (status) atomicOr(status, TC_DEV_WAIT_TIMEOUT);
       return false;
     }
-    if (n > 4096) __nanosleep(32);
+    if (n > 1024) __nanosleep(64);
   }
   return true;
 }

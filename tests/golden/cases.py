@@ -93,6 +93,9 @@ CASES = [
     case("bwd_none_gqa3", "bwd", "evict_gqa3", seed=345),
     case("bwd_rel_sink_d128_bf16", "bwd", "d128", dtype="bf16", position="relative",
          sink=True, softcap=50.0, seed=346),
+    case("bwd_rope_sink_d128_bf16", "bwd", "d128", dtype="bf16", position="rope",
+         sink=True, softcap=30.0, seed=347),
+    case("bwd_none_d128_bf16", "bwd", "d128", dtype="bf16", softcap=None, seed=348),
     # incremental decode: prefill N - tail tokens, decode `tail`
     case("dec_plain_tiny", "decode", "tiny", tail=7, seed=500),
     case("dec_plain_evict", "decode", "evict", tail=40, seed=501),

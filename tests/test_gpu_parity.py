@@ -74,7 +74,8 @@ def test_cuda_matches_oracle(cuda, name):
 
 
 @pytest.mark.parametrize("name", ["fwd_plain_d64", "fwd_rope_d128_bf16", "fwd_rel_d128_bf16",
-                                  "bwd_rel_sink_d128_bf16"])
+                                  "bwd_rel_sink_d128_bf16", "bwd_rope_sink_d128_bf16",
+                                  "bwd_none_d128_bf16"])
 def test_simt_and_default_paths_agree(cuda, name):
     """The tensor-core and SIMT kernels compute the same function."""
     from product_runner import product_case

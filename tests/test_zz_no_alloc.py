@@ -88,7 +88,7 @@ def _noalloc_call(c, g, d, packed, pos, out, lse, dout, dlse):
 
 
 @pytest.mark.parametrize("name", ["bwd_rel_sink_tiny", "bwd_rope_sink_tiny", "bwd_none_gqa3",
-                                  "bwd_rel_sink_d128_bf16"])
+                                  "bwd_rel_sink_d128_bf16", "bwd_rope_sink_d128_bf16"])
 def test_noalloc_backward_matches_allocating_entry_point(name):
     c, g, d, packed, pos, out, lse, dout, dlse = _inputs(name)
     want = T.multilevel_attention_backward(d["q"], packed, out, lse, dout, g["fmap"], g["cache"],
