@@ -216,6 +216,17 @@ typedef struct tc_attn_args {
   int32_t* dev_status;      /* device status word (TC_DEV_*), or NULL        */
   int32_t impl;             /* 0 auto, 1 SIMT (any shape, any dtype),
                                2 tensor core (bf16/f16, Dk = Dv = 128)       */
+  /* Relative mode on the tensor-core path: the bias logits
+   * rel_logits[row, pad + d] = relative_states[row] . relative_proj[:, d]
+   * (row = (b * N + q) * Hq + hq, d = bin distance) in the element type,
+   * with `pad` zero columns on each side of the bins a query can reach;
+   * row stride rel_logits_stride elements (a multiple of 8).  NULL: the
+   * relative mode runs on the SIMT kernels, which form the bias from
+   * rel_states / rel_proj directly. */
+  const void* rel_logits;
+  int64_t rel_logits_stride;
+  int32_t rel_logits_pad;
+  int32_t tile_n;           /* forward KV tile width: 0 auto, 64 or 128      */
 } tc_attn_args;
 
 /* Phase-2 forward: (out, lse) over the packed level-major K/V

@@ -50,7 +50,8 @@ class AttnArgs(ctypes.Structure):
         ("rel_bins", _c_i32), ("rope_cos", _c_vp), ("rope_sin", _c_vp), ("rope_npos", _c_i32),
         ("out", _c_vp), ("lse", _c_vp), ("o", _c_vp), ("dout", _c_vp), ("dlse", _c_vp),
         ("delta", _c_vp), ("dq", _c_vp), ("dk", _c_vp), ("dv", _c_vp), ("drel", _c_vp),
-        ("dev_status", _c_vp), ("impl", _c_i32),
+        ("dev_status", _c_vp), ("impl", _c_i32), ("rel_logits", _c_vp),
+        ("rel_logits_stride", _c_i64), ("rel_logits_pad", _c_i32), ("tile_n", _c_i32),
     ]
 
 

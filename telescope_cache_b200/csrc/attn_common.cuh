@@ -32,6 +32,10 @@ struct AttnParams {
   void* dv;
   float* drel;
   int32_t* status;
+  const void* rl;     // relative bias logits band (tensor-core path), or null
+  int64_t rl_stride;
+  int rl_pad;
+  int tile_n;
   Sched s;
 };
 

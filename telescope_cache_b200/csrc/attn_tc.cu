@@ -1,16 +1,16 @@
-// Tensor-core Phase-2 attention for sm_100a: tcgen05 MMAs with fp32
+// Tensor-core Phase-2 forward for sm_100a: tcgen05 MMAs with fp32
 // accumulators in TMEM, operands staged by TMA (128-byte swizzle, no
 // multicast), warp-specialised pipeline.  bf16/f16, Dk = Dv = 128.
 //
-// Forward CTA = 128 query rows of one query head.  It walks every level's
-// O(1) hull (fwd_hull) in 128-node tiles:
-//   warp 0      TMA producer: Q once, then K/V tiles into a 2-stage ring
+// CTA = 128 query rows of one query head.  It walks every level's O(1) hull
+// (fwd_hull) in BK-node tiles (BK = 128, or 64 for the relative bias):
+//   warp 0      TMA producer: Q once, then K/V tiles into an NS-stage ring
 //   warp 1      MMA issuer:   S_j = Q K_j^T into TMEM (double buffered),
 //                             O += P_{j-1} V_{j-1} (P from shared memory)
 //   warps 4..7  softmax:      one thread per query row (= TMEM lane):
-//                             exact per-row level mask, softcap, online
-//                             softmax in log2 units with lazy O rescaling,
-//                             P -> shared memory (bf16), final O / l, lse.
+//                             exact per-row level mask, relative bias,
+//                             softcap, online softmax in log2 units with lazy
+//                             O rescaling, P -> shared memory, final O / l.
 // Every mbarrier wait is bounded (see tc_ptx.cuh); a timeout sets
 // TC_DEV_WAIT_TIMEOUT in the device status word and the CTA drains.
 #include "tc_common.cuh"
@@ -21,11 +21,20 @@ namespace {
 using namespace ptx;
 using namespace tcx;
 
-constexpr int BQ = 128, BK = 128, NS = 2;
-constexpr int TILE = 128 * 128 * 2;      // one 128 x 128 16-bit tile
-constexpr int KBLK = 128 * 128;          // one 64-column K-block of a tile
+constexpr int BQ = 128;
+constexpr int QTILE = 128 * 128 * 2;     // Q tile bytes
+constexpr int QBLK = 128 * 128;          // one 64-column block of a 128-row tile
 constexpr float kRescale = 8.f;          // lazy rescale threshold, log2 units
-constexpr int kFwdSmem = TILE * (1 + 2 * NS + 1) + 1024 + 256;
+
+template <int BK> struct FwdShape {
+  static constexpr int NS = BK == 64 ? 3 : 2;         // K/V stages
+  static constexpr int KVBLK = BK * 128;              // one 64-column block of a K/V tile
+  static constexpr int KVTILE = 2 * KVBLK;            // one K or V tile
+  static constexpr int PTILE = 128 * BK * 2;          // P tile [128 x BK]
+  static constexpr int TMEM_COLS = BK == 64 ? 256 : 512;
+  static constexpr int O_COL = 2 * BK;
+  static constexpr int SMEM = QTILE + 2 * NS * KVTILE + PTILE + 1024 + 256;
+};
 
 struct TcParams {
   int N, Hq, Hkv, E;
@@ -34,20 +43,25 @@ struct TcParams {
   void* out;
   float* lse;
   int32_t* status;
+  const uint16_t* rl;
+  int64_t rl_stride;
+  int rl_pad;
   Sched s;
 };
 
-template <typename T>
+template <typename T, int BK, bool REL>
 __global__ void __launch_bounds__(256, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, TcParams p) {
+  using Sh = FwdShape<BK>;
+  constexpr int NS = Sh::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_s = sm;
-  uint8_t* k_s = q_s + TILE;
-  uint8_t* v_s = k_s + NS * TILE;
-  uint8_t* p_s = v_s + NS * TILE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + TILE);
+  uint8_t* k_s = q_s + QTILE;
+  uint8_t* v_s = k_s + NS * Sh::KVTILE;
+  uint8_t* p_s = v_s + NS * Sh::KVTILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + Sh::PTILE);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + NS;
@@ -79,7 +93,7 @@ __global__ void __launch_bounds__(256, 1)
     mbar_fence_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, 512);
+    tmem_alloc(tmem_holder, Sh::TMEM_COLS);
     tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
@@ -96,38 +110,37 @@ __global__ void __launch_bounds__(256, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
-      mbar_expect_tx(q_full, TILE);
+      mbar_expect_tx(q_full, QTILE);
       tma_load_4d(q_s, &tmq, 0, hq, q0, b, q_full);
-      tma_load_4d(q_s + KBLK, &tmq, 64, hq, q0, b, q_full);
+      tma_load_4d(q_s + QBLK, &tmq, 64, hq, q0, b, q_full);
       TileWalk it{-1, 0, 0, q0, q1, BK};
       bool ok = it.start(p.s);
       for (int j = 0; ok; ++j, ok = it.advance(p.s)) {
         const int st = j % NS;
         if (j >= NS && !mbar_wait(&kv_empty[st], ((j / NS) - 1) & 1, abort_flag, status)) break;
-        mbar_expect_tx(&kv_full[st], 2 * TILE);
+        mbar_expect_tx(&kv_full[st], 2 * Sh::KVTILE);
         const int row = p.s.off[it.lev] + it.k0;
-        uint8_t* kd = k_s + st * TILE;
-        uint8_t* vd = v_s + st * TILE;
+        uint8_t* kd = k_s + st * Sh::KVTILE;
+        uint8_t* vd = v_s + st * Sh::KVTILE;
         tma_load_4d(kd, &tmk, 0, hkv, row, b, &kv_full[st]);
-        tma_load_4d(kd + KBLK, &tmk, 64, hkv, row, b, &kv_full[st]);
+        tma_load_4d(kd + Sh::KVBLK, &tmk, 64, hkv, row, b, &kv_full[st]);
         tma_load_4d(vd, &tmv, 0, hkv, row, b, &kv_full[st]);
-        tma_load_4d(vd + KBLK, &tmv, 64, hkv, row, b, &kv_full[st]);
+        tma_load_4d(vd + Sh::KVBLK, &tmv, 64, hkv, row, b, &kv_full[st]);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
-      constexpr uint32_t kIdQK = idesc_f16(128, 128, fmt, 0, 0);
-      constexpr uint32_t kIdPV = idesc_f16(128, 128, fmt, 0, 1);
+      constexpr uint32_t kIdQK = idesc_f16(128, BK, Pack2<T>::kFmt, 0, 0);
+      constexpr uint32_t kIdPV = idesc_f16(128, 128, Pack2<T>::kFmt, 0, 1);
       const uint32_t qa = smem_addr(q_s), pa = smem_addr(p_s);
       auto issue_pv = [&](int t) {
-        const uint32_t va = smem_addr(v_s + (t % NS) * TILE);
+        const uint32_t va = smem_addr(v_s + (t % NS) * Sh::KVTILE);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = sdesc_sw128(pa + (kk >> 2) * KBLK + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(va + kk * 2048, KBLK, 1024);
-          mma_f16(tmem + 256, ad, bd, kIdPV, (t > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t ad = sdesc_sw128(pa + (kk >> 2) * QBLK + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(va + kk * 2048, Sh::KVBLK, 1024);
+          mma_f16(tmem + Sh::O_COL, ad, bd, kIdPV, (t > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(o_done);
         mma_commit(&kv_empty[t % NS]);
@@ -142,12 +155,12 @@ __global__ void __launch_bounds__(256, 1)
         if (!mbar_wait(&kv_full[st], (j / NS) & 1, abort_flag, status)) { alive = false; break; }
         if (j >= 2 && !mbar_wait(&s_free[bb], ((j >> 1) - 1) & 1, abort_flag, status)) { alive = false; break; }
         tc_fence_after();
-        const uint32_t ka = smem_addr(k_s + st * TILE);
+        const uint32_t ka = smem_addr(k_s + st * Sh::KVTILE);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = sdesc_sw128(qa + (kk >> 2) * KBLK + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(ka + (kk >> 2) * KBLK + (kk & 3) * 32, 16, 1024);
-          mma_f16(tmem + bb * 128, ad, bd, kIdQK, kk > 0 ? 1u : 0u);
+          const uint64_t ad = sdesc_sw128(qa + (kk >> 2) * QBLK + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(ka + (kk >> 2) * Sh::KVBLK + (kk & 3) * 32, 16, 1024);
+          mma_f16(tmem + bb * BK, ad, bd, kIdQK, kk > 0 ? 1u : 0u);
         }
         mma_commit(&s_full[bb]);
         if (j >= 1) {
@@ -167,22 +180,34 @@ __global__ void __launch_bounds__(256, 1)
     const int q = q0 + r;
     const bool row_ok = q < p.N;
     const uint32_t lane_base = (uint32_t)((warp - 4) * 32) << 16;
+    // logit2 = (S * scale + bias) * log2(e), softcapped: cap * tanh(. / cap) * log2(e)
     const float kq = p.has_cap ? p.scale / p.cap : p.scale * kLog2e;
+    const float kb = p.has_cap ? 1.f / p.cap : kLog2e;
     const float kc = p.cap * kLog2e;
+    const uint16_t* rl_row = nullptr;
+    if (REL) rl_row = p.rl + (((int64_t)b * p.N + (row_ok ? q : 0)) * p.Hq + hq) * p.rl_stride;
     float m_used = -INFINITY, ell = 0.f;
-    int lo = 0, hi = 0, cur = -1;
+    int lo = 0, hi = 0, base = 0, cur = -1;
     TileWalk it{-1, 0, 0, q0, q1, BK};
     bool ok = it.start(p.s);
     int j = 0;
     bool alive = true;
-    float sv[128];
+    float sv[BK];
     for (; ok; ++j, ok = it.advance(p.s)) {
       if (it.lev != cur) {
         cur = it.lev;
-        lo = hi = 0;
+        lo = hi = base = 0;
         if (row_ok) {
-          level_bounds_raw(q, cur, p.s, &lo, &hi);
-          if (lo >= hi) lo = hi = 0;
+          if (REL) {
+            int los[TC_MAX_LEVELS], his[TC_MAX_LEVELS];
+            row_bounds(q, p.s, los, his);
+            lo = los[cur];
+            hi = his[cur];
+            base = bin_base(cur, los, his);
+          } else {
+            level_bounds_raw(q, cur, p.s, &lo, &hi);
+            if (lo >= hi) lo = hi = 0;
+          }
         }
       }
       const int bb = j & 1;
@@ -190,19 +215,40 @@ __global__ void __launch_bounds__(256, 1)
       if (!alive) break;
       tc_fence_after();
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(tmem + lane_base + bb * 128 + c4 * 32, sv + 32 * c4);
+      for (int c4 = 0; c4 < BK / 32; ++c4) tmem_ld32(tmem + lane_base + bb * BK + c4 * 32, sv + 32 * c4);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[bb]);
       const int jlo = lo - it.k0, jhi = hi - it.k0;
       float mx = -INFINITY;
+      if constexpr (REL) {
+        static_assert(!REL || BK == 64, "the relative bias path uses 64-node tiles");
+        uint32_t run[32];
+        const bool any = jlo < BK && jhi > 0 && lo < hi;
+        if (any) {
+          // columns c see bin distance base - k0 - c: the run rl[pad + base - k0 - 63 + i]
+          load_run64(rl_row, p.rl_pad + base - it.k0 - (BK - 1), run);
+        } else {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float x = sv[c] * kq;
-        if (p.has_cap) x = tanh_fast(x) * kc;
-        x = (c >= jlo && c < jhi) ? x : -INFINITY;
-        sv[c] = x;
-        mx = fmaxf(mx, x);
+          for (int k = 0; k < 32; ++k) run[k] = 0u;
+        }
+#pragma unroll
+        for (int c = 0; c < BK; ++c) {
+          float x = fmaf(sv[c], kq, run_elem<T>(run, BK - 1 - c) * kb);
+          if (p.has_cap) x = tanh_fast(x) * kc;
+          x = (c >= jlo && c < jhi) ? x : -INFINITY;
+          sv[c] = x;
+          mx = fmaxf(mx, x);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < BK; ++c) {
+          float x = sv[c] * kq;
+          if (p.has_cap) x = tanh_fast(x) * kc;
+          x = (c >= jlo && c < jhi) ? x : -INFINITY;
+          sv[c] = x;
+          mx = fmaxf(mx, x);
+        }
       }
       bool rescale = false;
       float alpha = 1.f;
@@ -225,30 +271,25 @@ __global__ void __launch_bounds__(256, 1)
         float ov[32];
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
-          tmem_ld32(tmem + lane_base + 256 + c4 * 32, ov);
+          tmem_ld32(tmem + lane_base + Sh::O_COL + c4 * 32, ov);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-          tmem_st32(tmem + lane_base + 256 + c4 * 32, ov);
+          tmem_st32(tmem + lane_base + Sh::O_COL + c4 * 32, ov);
         }
         tmem_wait_st();
       }
       float sum = 0.f;
       const bool live = m_used > -INFINITY;
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
+      for (int c8 = 0; c8 < BK / 8; ++c8) {
         float pv[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           pv[i] = live ? exp2_fast(sv[c8 * 8 + i] - m_used) : 0.f;
           sum += pv[i];
         }
-        uint4 w;
-        w.x = Pack2<T>::pack(pv[0], pv[1]);
-        w.y = Pack2<T>::pack(pv[2], pv[3]);
-        w.z = Pack2<T>::pack(pv[4], pv[5]);
-        w.w = Pack2<T>::pack(pv[6], pv[7]);
-        *reinterpret_cast<uint4*>(p_s + sw128_offset(r, c8 * 8, 128)) = w;
+        *reinterpret_cast<uint4*>(p_s + sw128_offset(r, c8 * 8, 128)) = pack8<T>(pv, 1.f);
       }
       ell += sum;
       fence_async_smem();
@@ -265,18 +306,11 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         float ov[32];
-        tmem_ld32(tmem + lane_base + 256 + c4 * 32, ov);
+        tmem_ld32(tmem + lane_base + Sh::O_COL + c4 * 32, ov);
         tmem_wait_ld();
         if (row_ok) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint4 w;
-            w.x = Pack2<T>::pack(ov[i * 8 + 0] * inv, ov[i * 8 + 1] * inv);
-            w.y = Pack2<T>::pack(ov[i * 8 + 2] * inv, ov[i * 8 + 3] * inv);
-            w.z = Pack2<T>::pack(ov[i * 8 + 4] * inv, ov[i * 8 + 5] * inv);
-            w.w = Pack2<T>::pack(ov[i * 8 + 6] * inv, ov[i * 8 + 7] * inv);
-            *reinterpret_cast<uint4*>(out + c4 * 32 + i * 8) = w;
-          }
+          for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(out + c4 * 32 + i * 8) = pack8<T>(ov + i * 8, inv);
         }
       }
       if (row_ok) p.lse[((int64_t)b * p.N + q) * p.Hq + hq] = (m_used + log2f(ell)) * kLn2;
@@ -287,21 +321,16 @@ __global__ void __launch_bounds__(256, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, Sh::TMEM_COLS);
   }
 }
 
-}  // namespace
-
-bool tc_supported(const AttnParams& p, int dtype) {
-  return (dtype == TC_BF16 || dtype == TC_F16) && p.Dk == HD && p.Dv == HD && p.pos_mode != TC_POS_RELATIVE;
-}
-
-int attn_fwd_tc(const AttnParams& a, int dtype, cudaStream_t st) {
+template <typename T, int BK, bool REL>
+int launch_fwd(const AttnParams& a, int dtype, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
   if (int rc = make_map(&mq, a.q, dtype, a.B, a.N, a.Hq, 128)) return rc;
-  if (int rc = make_map(&mk, a.k, dtype, a.B, a.total, a.Hkv, 128)) return rc;
-  if (int rc = make_map(&mv, a.v, dtype, a.B, a.total, a.Hkv, 128)) return rc;
+  if (int rc = make_map(&mk, a.k, dtype, a.B, a.total, a.Hkv, BK)) return rc;
+  if (int rc = make_map(&mv, a.v, dtype, a.B, a.total, a.Hkv, BK)) return rc;
   TcParams p;
   p.N = a.N;
   p.Hq = a.Hq;
@@ -313,20 +342,34 @@ int attn_fwd_tc(const AttnParams& a, int dtype, cudaStream_t st) {
   p.out = a.out;
   p.lse = a.lse;
   p.status = a.status;
+  p.rl = static_cast<const uint16_t*>(a.rl);
+  p.rl_stride = a.rl_stride;
+  p.rl_pad = a.rl_pad;
   p.s = a.s;
-  dim3 grid((a.N + BQ - 1) / BQ, a.Hq, a.B);
-  if (dtype == TC_BF16) {
-    auto k = fwd_tc_kernel<__nv_bfloat16>;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem) != cudaSuccess)
-      return TC_ERR_CUDA;
-    k<<<grid, 256, kFwdSmem, st>>>(mq, mk, mv, p);
-  } else {
-    auto k = fwd_tc_kernel<__half>;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem) != cudaSuccess)
-      return TC_ERR_CUDA;
-    k<<<grid, 256, kFwdSmem, st>>>(mq, mk, mv, p);
-  }
+  constexpr int smem = FwdShape<BK>::SMEM;
+  auto k = fwd_tc_kernel<T, BK, REL>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TC_ERR_CUDA;
+  k<<<dim3((a.N + BQ - 1) / BQ, a.Hq, a.B), 256, smem, st>>>(mq, mk, mv, p);
   return launch_status();
+}
+
+template <typename T>
+int fwd_dispatch(const AttnParams& a, int dtype, cudaStream_t st) {
+  if (a.pos_mode == TC_POS_RELATIVE) return launch_fwd<T, 64, true>(a, dtype, st);
+  if (a.tile_n == 64) return launch_fwd<T, 64, false>(a, dtype, st);
+  return launch_fwd<T, 128, false>(a, dtype, st);
+}
+
+}  // namespace
+
+bool tc_supported(const AttnParams& p, int dtype) {
+  return (dtype == TC_BF16 || dtype == TC_F16) && p.Dk == HD && p.Dv == HD &&
+         (p.pos_mode != TC_POS_RELATIVE || p.rl != nullptr);
+}
+
+int attn_fwd_tc(const AttnParams& a, int dtype, cudaStream_t st) {
+  if (dtype == TC_BF16) return fwd_dispatch<__nv_bfloat16>(a, dtype, st);
+  return fwd_dispatch<__half>(a, dtype, st);
 }
 
 }  // namespace tc

@@ -29,7 +29,7 @@ constexpr int T64 = 64 * 128 * 2;    // [64 rows x 128] tile
 constexpr int B128 = 128 * 128;      // one 64-col block of a 128-row tile
 constexpr int B64 = 64 * 128;        // one 64-col block of a 64-row tile
 constexpr int kSmemA = 2 * T128 + 4 * T64 + 128 * 128 + 1024 + 256;
-constexpr int kSmemB = 2 * T128 + 4 * T64 + 2 * 128 * 128 + 4 * 64 * 4 + 1024 + 256;
+constexpr int kSmemB = 2 * T128 + 4 * T64 + 2 * 128 * 128 + 6 * 64 * 4 + 1024 + 256;
 
 struct BwdParams {
   int N, Hq, Hkv, E;
@@ -42,18 +42,26 @@ struct BwdParams {
   void* dq;
   void* dk;
   void* dv;
+  float* drel;                   // relative: drel_logits [B, N, Hq, bins] f32, or null
+  int bins;
+  const uint16_t* rl;            // relative: bias logits band (see tc_attn_args)
+  int64_t rl_stride;
+  int rl_pad;
   int32_t* status;
   Sched s;
   int tiles[TC_MAX_LEVELS + 1];  // Pass B: prefix count of 128-node tiles per level
 };
 
 struct BwdScalars {
-  float kq, kc;
+  float kq, kb, kc;
   __device__ BwdScalars(const BwdParams& p)
-      : kq(p.has_cap ? p.scale / p.cap : p.scale * kLog2e), kc(p.cap * kLog2e) {}
-  // x: raw accumulator S; returns the log2-domain logit and the softcap derivative.
-  __device__ __forceinline__ void logit(float s, int has_cap, float* l2, float* g) const {
-    const float x = s * kq;
+      : kq(p.has_cap ? p.scale / p.cap : p.scale * kLog2e),
+        kb(p.has_cap ? 1.f / p.cap : kLog2e),
+        kc(p.cap * kLog2e) {}
+  // s: raw accumulator S, bias: relative bias (natural units).  Returns the
+  // log2-domain logit and the softcap derivative 1 - tanh^2 (1 without cap).
+  __device__ __forceinline__ void logit(float s, float bias, int has_cap, float* l2, float* g) const {
+    const float x = fmaf(s, kq, bias * kb);
     if (has_cap) {
       const float t = tanh_fast(x);
       *l2 = t * kc;
@@ -68,7 +76,7 @@ struct BwdScalars {
 // ---------------------------------------------------------------------------
 // Pass A
 // ---------------------------------------------------------------------------
-template <typename T>
+template <typename T, bool REL>
 __global__ void __launch_bounds__(256, 1)
     bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmg,
                      const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, BwdParams p) {
@@ -199,7 +207,9 @@ __global__ void __launch_bounds__(256, 1)
     const int64_t row = ((int64_t)b * p.N + q) * p.Hq + hq;
     const float lse2 = row_ok ? p.lse[row] * kLog2e : 0.f;
     const float dlt = row_ok ? p.delta[row] : 0.f;
-    int lo = 0, hi = 0, cur = -1;
+    const uint16_t* rl_row = REL ? p.rl + (row_ok ? row : 0) * p.rl_stride : nullptr;
+    float* drel_row = (REL && p.drel && row_ok) ? p.drel + row * p.bins : nullptr;
+    int lo = 0, hi = 0, base = 0, cur = -1;
     TileWalk it{-1, 0, 0, q0, q1, 64};
     bool ok = it.start(p.s);
     bool alive = true;
@@ -207,10 +217,18 @@ __global__ void __launch_bounds__(256, 1)
     for (; ok; ++j, ok = it.advance(p.s)) {
       if (it.lev != cur) {
         cur = it.lev;
-        lo = hi = 0;
+        lo = hi = base = 0;
         if (row_ok) {
-          level_bounds_raw(q, cur, p.s, &lo, &hi);
-          if (lo >= hi) lo = hi = 0;
+          if (REL) {
+            int los[TC_MAX_LEVELS], his[TC_MAX_LEVELS];
+            row_bounds(q, p.s, los, his);
+            lo = los[cur];
+            hi = his[cur];
+            base = bin_base(cur, los, his);
+          } else {
+            level_bounds_raw(q, cur, p.s, &lo, &hi);
+            if (lo >= hi) lo = hi = 0;
+          }
         }
       }
       const int bb = j & 1;
@@ -230,6 +248,16 @@ __global__ void __launch_bounds__(256, 1)
         if (!alive) break;
       }
       const int jlo = lo - it.k0, jhi = hi - it.k0;
+      uint32_t run[REL ? 32 : 1];
+      if constexpr (REL) {
+        // column c has bin distance base - k0 - c: the run rl[pad + base - k0 - 63 + i]
+        if (jlo < 64 && jhi > 0 && lo < hi) {
+          load_run64(rl_row, p.rl_pad + base - it.k0 - 63, run);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) run[k] = 0u;
+        }
+      }
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
         float dx[8];
@@ -237,10 +265,12 @@ __global__ void __launch_bounds__(256, 1)
         for (int i = 0; i < 8; ++i) {
           const int c = c8 * 8 + i;
           float l2, g;
-          sc.logit(sv[c], p.has_cap, &l2, &g);
+          sc.logit(sv[c], REL ? run_elem<T>(run, 63 - c) : 0.f, p.has_cap, &l2, &g);
           const bool valid = c >= jlo && c < jhi;
           const float pr = valid ? exp2_fast(l2 - lse2) : 0.f;
-          dx[i] = pr * (dp[c] - dlt) * g;
+          dx[i] = valid ? pr * (dp[c] - dlt) * g : 0.f;
+          // d rel_logits[q, h, dist] = dX: each (row, distance) is written once
+          if (REL && valid && drel_row) drel_row[base - it.k0 - c] = dx[i];
         }
         *reinterpret_cast<uint4*>(x_s + sw128_offset(r, c8 * 8, 128)) = pack8<T>(dx, 1.f);
       }
@@ -300,7 +330,7 @@ struct QSteps {
   }
 };
 
-template <typename T>
+template <typename T, bool REL>
 __global__ void __launch_bounds__(256, 1)
     bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmg,
                       const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
@@ -317,7 +347,8 @@ __global__ void __launch_bounds__(256, 1)
   float* dlt_s = lse_s + 64;
   int* lo_s = reinterpret_cast<int*>(dlt_s + 64);
   int* hi_s = lo_s + 64;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(hi_s + 64);
+  int64_t* rl_s = reinterpret_cast<int64_t*>(hi_s + 64);  // [64] relative: row + pad + base
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rl_s + 64);
   uint64_t* kv_full = bars;
   uint64_t* q_full = bars + 1;
   uint64_t* q_empty = bars + 3;
@@ -457,10 +488,20 @@ __global__ void __launch_bounds__(256, 1)
         const int q = w.qb + r;
         int lo = 0, hi = 0;
         float l2 = 0.f, dl = 0.f;
+        int64_t rlo = 0;
         if (q < p.N) {
-          level_bounds_raw(q, lev, p.s, &lo, &hi);
-          if (lo >= hi) lo = hi = 0;
           const int64_t row = ((int64_t)b * p.N + q) * p.Hq + hq;
+          if (REL) {
+            int los[TC_MAX_LEVELS], his[TC_MAX_LEVELS];
+            row_bounds(q, p.s, los, his);
+            lo = los[lev];
+            hi = his[lev];
+            // bias of node j: rl[row, pad + base - j]
+            rlo = row * p.rl_stride + p.rl_pad + bin_base(lev, los, his);
+          } else {
+            level_bounds_raw(q, lev, p.s, &lo, &hi);
+            if (lo >= hi) lo = hi = 0;
+          }
           l2 = p.lse[row] * kLog2e;
           dl = p.delta[row];
         }
@@ -468,6 +509,7 @@ __global__ void __launch_bounds__(256, 1)
         hi_s[r] = hi;
         lse_s[r] = l2;
         dlt_s[r] = dl;
+        if (REL) rl_s[r] = rlo;
       }
       named_bar(1, 128);
       const int bb = i & 1;
@@ -492,11 +534,16 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const int c = c8 * 8 + k;
-          float l2, g;
-          sc.logit(sv[c], p.has_cap, &l2, &g);
           const bool valid = node_ok && jn >= lo_s[c] && jn < hi_s[c];
+          float bias = 0.f;
+          if (REL && valid) {
+            // lanes hold consecutive nodes: consecutive (descending) addresses
+            bias = bits_to_float<T>(__ldg(p.rl + rl_s[c] - jn));
+          }
+          float l2, g;
+          sc.logit(sv[c], bias, p.has_cap, &l2, &g);
           pr[k] = valid ? exp2_fast(l2 - lse_s[c]) : 0.f;
-          dx[k] = pr[k] * (dp[c] - dlt_s[c]) * g;
+          dx[k] = valid ? pr[k] * (dp[c] - dlt_s[c]) * g : 0.f;
         }
         const uint32_t off = sw128_offset(r, c8 * 8, 128);
         *reinterpret_cast<uint4*>(pt_s + off) = pack8<T>(pr, 1.f);
@@ -550,7 +597,7 @@ __global__ void __launch_bounds__(256, 1)
   }
 }
 
-template <typename T>
+template <typename T, bool REL>
 int launch_bwd(const AttnParams& a, int dtype, cudaStream_t st) {
   CUtensorMap mq128, mg128, mk64, mv64, mq64, mg64, mk128, mv128;
   if (int rc = make_map(&mq128, a.q, dtype, a.B, a.N, a.Hq, 128)) return rc;
@@ -577,19 +624,24 @@ int launch_bwd(const AttnParams& a, int dtype, cudaStream_t st) {
   p.dq = a.dq;
   p.dk = a.dk;
   p.dv = a.dv;
+  p.drel = a.drel;
+  p.bins = a.bins;
+  p.rl = static_cast<const uint16_t*>(a.rl);
+  p.rl_stride = a.rl_stride;
+  p.rl_pad = a.rl_pad;
   p.status = a.status;
   p.s = a.s;
   p.tiles[0] = 0;
   for (int l = 0; l < TC_MAX_LEVELS; ++l)
     p.tiles[l + 1] = p.tiles[l] + (l < a.s.nl ? (a.s.len[l] + 127) / 128 : 0);
   if (int rc = delta_launch(a, dtype, st)) return rc;
-  auto ka = bwd_dq_tc_kernel<T>;
+  auto ka = bwd_dq_tc_kernel<T, REL>;
   if (cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemA) != cudaSuccess) return TC_ERR_CUDA;
   ka<<<dim3((a.N + 127) / 128, a.Hq, a.B), 256, kSmemA, st>>>(mq128, mg128, mk64, mv64, p);
   if (int rc = launch_status()) return rc;
   const int ntiles = p.tiles[a.s.nl];
   if (ntiles > 0) {
-    auto kb = bwd_dkv_tc_kernel<T>;
+    auto kb = bwd_dkv_tc_kernel<T, REL>;
     if (cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemB) != cudaSuccess)
       return TC_ERR_CUDA;
     kb<<<dim3(ntiles, a.Hkv, a.B), 256, kSmemB, st>>>(mq64, mg64, mk128, mv128, p);
@@ -601,12 +653,15 @@ int launch_bwd(const AttnParams& a, int dtype, cudaStream_t st) {
 }  // namespace
 
 bool tc_bwd_supported(const AttnParams& p, int dtype) {
-  return (dtype == TC_BF16 || dtype == TC_F16) && p.Dk == HD && p.Dv == HD && p.pos_mode != TC_POS_RELATIVE;
+  return (dtype == TC_BF16 || dtype == TC_F16) && p.Dk == HD && p.Dv == HD &&
+         (p.pos_mode != TC_POS_RELATIVE || p.rl != nullptr);
 }
 
 int attn_bwd_tc(const AttnParams& a, int dtype, cudaStream_t st) {
-  if (dtype == TC_BF16) return launch_bwd<__nv_bfloat16>(a, dtype, st);
-  return launch_bwd<__half>(a, dtype, st);
+  const bool rel = a.pos_mode == TC_POS_RELATIVE;
+  if (dtype == TC_BF16)
+    return rel ? launch_bwd<__nv_bfloat16, true>(a, dtype, st) : launch_bwd<__nv_bfloat16, false>(a, dtype, st);
+  return rel ? launch_bwd<__half, true>(a, dtype, st) : launch_bwd<__half, false>(a, dtype, st);
 }
 
 }  // namespace tc

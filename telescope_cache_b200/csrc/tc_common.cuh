@@ -81,6 +81,50 @@ struct TileWalk {
   }
 };
 
+// 64 consecutive 16-bit values row[e0 .. e0 + 63] (any alignment of e0) as 32
+// packed words, element 2k in the low half of word k.  Reads the 16-byte
+// aligned superset (9 vector loads) and realigns it with two select stages
+// (whole words) and one funnel shift (half words).
+__device__ __forceinline__ void load_run64(const uint16_t* row, int e0, uint32_t* out) {
+  const int a = e0 & ~7;
+  const int sh = e0 - a;
+  const uint4* src = reinterpret_cast<const uint4*>(row + a);
+  uint32_t w[36];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) {
+    const uint4 v = __ldg(src + i);
+    w[4 * i] = v.x;
+    w[4 * i + 1] = v.y;
+    w[4 * i + 2] = v.z;
+    w[4 * i + 3] = v.w;
+  }
+  const int wo = sh >> 1;
+#pragma unroll
+  for (int i = 0; i < 35; ++i) w[i] = (wo & 1) ? w[i + 1] : w[i];
+#pragma unroll
+  for (int i = 0; i < 33; ++i) w[i] = (wo & 2) ? w[i + 2] : w[i];
+  const bool odd = sh & 1;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) out[k] = odd ? __funnelshift_r(w[k], w[k + 1], 16) : w[k];
+}
+
+// A 16-bit element (bf16 or f16 bits) as float.
+template <typename T>
+__device__ __forceinline__ float bits_to_float(uint16_t h) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return __uint_as_float((uint32_t)h << 16);
+  } else {
+    return __half2float(__ushort_as_half(h));
+  }
+}
+
+// Element i (0..63) of a run loaded by load_run64, as float.
+template <typename T>
+__device__ __forceinline__ float run_elem(const uint32_t* run, int i) {
+  const uint32_t w = run[i >> 1];
+  return bits_to_float<T>((i & 1) ? (uint16_t)(w >> 16) : (uint16_t)(w & 0xffffu));
+}
+
 // Inverse RoPE (rotate by R(-p)) of a 128-wide fp32 row held by one thread.
 __device__ __forceinline__ void rope_inverse_row(float* v, const float* cos_t, const float* sin_t, int pos) {
   const float* c = cos_t + (int64_t)pos * (HD / 2);

@@ -49,8 +49,33 @@ def _impl_code(impl: Optional[str]) -> int:
     return {None: 0, "auto": 0, "simt": 1, "tensor": 2}[impl]
 
 
+REL_PAD = 128  # zero bins on each side of the relative band (>= one 64-node tile + 8)
+
+
+def _relative_band(st, pj, max_visible, dtype):
+    """Bias logits rel[row, REL_PAD + d] = states[row] . proj[:, d] for every
+    distance d a query can reach (< max_visible), in the kernels' element
+    type, with REL_PAD zero columns on both sides -- the operand of the
+    tensor-core relative path.  One plain GEMM (cuBLAS through torch)."""
+    d_rel, bins = pj.shape
+    reach = min(bins, max_visible)
+    width = (reach + 2 * REL_PAD + 7) // 8 * 8
+    proj_pad = torch.zeros(d_rel, width, device=pj.device, dtype=pj.dtype)
+    proj_pad[:, REL_PAD:REL_PAD + reach] = pj[:, :reach]
+    rows = st.reshape(-1, d_rel)
+    if st.dtype == dtype and pj.dtype == dtype:
+        band = rows.matmul(proj_pad)  # exact products, fp32 accumulation
+    else:
+        band = rows.float().matmul(proj_pad.float()).to(dtype)
+    return band.contiguous(), width
+
+
+def _tensor_core_shape(dtype, Dk, Dv):
+    return dtype in (torch.bfloat16, torch.float16) and Dk == 128 and Dv == 128
+
+
 def _prepare(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope_sin,
-             relative_states, relative_proj):
+             relative_states, relative_proj, impl=None):
     """Shared validation + operand preparation of forward and backward."""
     B, N, Hq, Dk = q.shape
     Hkv = packed.k.shape[2]
@@ -98,14 +123,21 @@ def _prepare(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope
         rope_cos=None if cos is None else cos.data_ptr(), rope_sin=None if sin is None else sin.data_ptr(),
         rope_npos=0 if cos is None else cos.shape[0],
         dev_status=device_status(q.device).data_ptr())
-    keep = (qc, kc, vc, cos, sin, st, pj)
+    band = None
+    if position_mode == "relative" and impl != "simt" and _tensor_core_shape(dtype, Dk, Dv):
+        band, width = _relative_band(st, pj, mx, dtype)
+        args.rel_logits = band.data_ptr()
+        args.rel_logits_stride = width
+        args.rel_logits_pad = REL_PAD
+    keep = (qc, kc, vc, cos, sin, st, pj, band)
     return args, sched, spec, keep, (B, N, Hq, Hkv, Dk, Dv, dtype)
 
 
 def _forward(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope_sin,
              relative_states, relative_proj, impl=None):
     args, sched, spec, keep, dims = _prepare(q, packed, fmap, cache_size, softcap, position_mode,
-                                             rope_cos, rope_sin, relative_states, relative_proj)
+                                             rope_cos, rope_sin, relative_states, relative_proj,
+                                             impl)
     B, N, Hq, Hkv, Dk, Dv, dtype = dims
     out = torch.empty(B, N, Hq, Dv, device=q.device, dtype=dtype)
     lse = torch.empty(B, N, Hq, device=q.device, dtype=torch.float32)
@@ -236,7 +268,8 @@ def multilevel_attention_backward(
         if not dlse.dtype.is_floating_point:
             raise ValueError("dlse must have floating dtype")
     args, sched, spec, keep, dims = _prepare(q, packed, fmap, cache_size, softcap, position_mode,
-                                             rope_cos, rope_sin, relative_states, relative_proj)
+                                             rope_cos, rope_sin, relative_states, relative_proj,
+                                             impl)
     dtype = dims[-1]
     _lib.require_cuda(out, lse, dout, dlse)
     oc = out.to(dtype).contiguous()
