@@ -211,8 +211,10 @@ typedef struct tc_attn_args {
   void* dq;                 /* [B, N, Hq, Dk]                                */
   void* dk;                 /* [B, total, Hkv, Dk]                           */
   void* dv;                 /* [B, total, Hkv, Dv]                           */
-  float* drel;              /* [B, N, Hq, rel_bins] f32, zero-filled by the
-                               caller, or NULL                               */
+  float* drel;              /* [B, N, Hq, rel_bins] f32 or NULL.  With
+                               rel_logits the kernels write every element;
+                               without, only visible bins are written and
+                               the caller zero-fills                         */
   int32_t* dev_status;      /* device status word (TC_DEV_*), or NULL        */
   int32_t impl;             /* 0 auto, 1 SIMT (any shape, any dtype),
                                2 tensor core (bf16/f16, Dk = Dv = 128)       */

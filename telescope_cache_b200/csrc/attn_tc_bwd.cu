@@ -29,6 +29,9 @@ constexpr int T64 = 64 * 128 * 2;    // [64 rows x 128] tile
 constexpr int B128 = 128 * 128;      // one 64-col block of a 128-row tile
 constexpr int B64 = 64 * 128;        // one 64-col block of a 64-row tile
 constexpr int kSmemA = 2 * T128 + 4 * T64 + 128 * 128 + 1024 + 256;
+// relative Pass A: + two fp32 dX staging tiles [128 x 65] and per-row run info
+constexpr int kDxfStride = 65;
+constexpr int kSmemArel = kSmemA + 2 * 128 * kDxfStride * 4 + 2 * 128 * 3 * 4 + 128 * 4;
 constexpr int kSmemB = 2 * T128 + 4 * T64 + 2 * 128 * 128 + 6 * 64 * 4 + 1024 + 256;
 
 struct BwdParams {
@@ -98,6 +101,10 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* dq_done = bars + 11;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  // relative only: fp32 dX staging [2][128][65], run info [2][128][3], row totals [128]
+  float* dxf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
+  int* rinfo = reinterpret_cast<int*>(dxf + 2 * 128 * kDxfStride);
+  int* mtot = rinfo + 2 * 128 * 3;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * 128, hq = blockIdx.y, b = blockIdx.z;
@@ -208,7 +215,11 @@ __global__ void __launch_bounds__(256, 1)
     const float lse2 = row_ok ? p.lse[row] * kLog2e : 0.f;
     const float dlt = row_ok ? p.delta[row] : 0.f;
     const uint16_t* rl_row = REL ? p.rl + (row_ok ? row : 0) * p.rl_stride : nullptr;
-    float* drel_row = (REL && p.drel && row_ok) ? p.drel + row * p.bins : nullptr;
+    const bool want_drel = REL && p.drel != nullptr;
+    if (want_drel) {
+      int los[TC_MAX_LEVELS], his[TC_MAX_LEVELS];
+      mtot[r] = row_ok ? row_bounds(q, p.s, los, his) : 0;
+    }
     int lo = 0, hi = 0, base = 0, cur = -1;
     TileWalk it{-1, 0, 0, q0, q1, 64};
     bool ok = it.start(p.s);
@@ -269,14 +280,46 @@ __global__ void __launch_bounds__(256, 1)
           const bool valid = c >= jlo && c < jhi;
           const float pr = valid ? exp2_fast(l2 - lse2) : 0.f;
           dx[i] = valid ? pr * (dp[c] - dlt) * g : 0.f;
-          // d rel_logits[q, h, dist] = dX: each (row, distance) is written once
-          if (REL && valid && drel_row) drel_row[base - it.k0 - c] = dx[i];
+          if (want_drel) dxf[(j & 1) * 128 * kDxfStride + r * kDxfStride + c] = dx[i];
         }
         *reinterpret_cast<uint4*>(x_s + sw128_offset(r, c8 * 8, 128)) = pack8<T>(dx, 1.f);
       }
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(x_full);
+      if (want_drel) {
+        // d rel_logits[q, h, dist] = dX (each (row, distance) once): this row's
+        // valid columns [cs, ce) are distances base - k0 - c, one ascending run
+        // in memory; the warp then writes its 32 rows' runs coalesced.
+        const int cs = max(jlo, 0), ce = min(jhi, 64);
+        int* ri = rinfo + (j & 1) * 128 * 3 + r * 3;
+        ri[0] = base - it.k0 - (ce - 1);
+        ri[1] = (row_ok && lo < hi && ce > cs) ? ce - cs : 0;
+        ri[2] = ce;
+        named_bar(1, 128);
+        const int w4 = warp - 4;
+        const float* src = dxf + (j & 1) * 128 * kDxfStride;
+        const int* inf = rinfo + (j & 1) * 128 * 3;
+        for (int k = 0; k < 32; ++k) {
+          const int rr = w4 * 32 + k;
+          const int n = inf[rr * 3 + 1];
+          if (n == 0) continue;
+          const int dmin = inf[rr * 3], cend = inf[rr * 3 + 2];
+          float* dst = p.drel + (((int64_t)b * p.N + q0 + rr) * p.Hq + hq) * p.bins + dmin;
+          for (int l = lane; l < n; l += 32) dst[l] = src[rr * kDxfStride + (cend - 1 - l)];
+        }
+      }
+    }
+    if (want_drel) {  // all four warps reach this barrier, also after an abort
+      // distances at or beyond a row's visible count are never attended: zero them
+      named_bar(1, 128);
+      const int w4 = warp - 4;
+      for (int k = 0; k < 32; ++k) {
+        const int rr = w4 * 32 + k;
+        if (q0 + rr >= p.N) break;
+        float* dst = p.drel + (((int64_t)b * p.N + q0 + rr) * p.Hq + hq) * p.bins;
+        for (int d = mtot[rr] + lane; d < p.bins; d += 32) dst[d] = 0.f;
+      }
     }
     if (alive && j >= 1) alive = __all_sync(0xffffffffu, mbar_wait(dq_done, 0, abort_flag, status));
     if (alive) {
@@ -636,8 +679,9 @@ int launch_bwd(const AttnParams& a, int dtype, cudaStream_t st) {
     p.tiles[l + 1] = p.tiles[l] + (l < a.s.nl ? (a.s.len[l] + 127) / 128 : 0);
   if (int rc = delta_launch(a, dtype, st)) return rc;
   auto ka = bwd_dq_tc_kernel<T, REL>;
-  if (cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemA) != cudaSuccess) return TC_ERR_CUDA;
-  ka<<<dim3((a.N + 127) / 128, a.Hq, a.B), 256, kSmemA, st>>>(mq128, mg128, mk64, mv64, p);
+  constexpr int smem_a = REL ? kSmemArel : kSmemA;
+  if (cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_a) != cudaSuccess) return TC_ERR_CUDA;
+  ka<<<dim3((a.N + 127) / 128, a.Hq, a.B), 256, smem_a, st>>>(mq128, mg128, mk64, mv64, p);
   if (int rc = launch_status()) return rc;
   const int ntiles = p.tiles[a.s.nl];
   if (ntiles > 0) {

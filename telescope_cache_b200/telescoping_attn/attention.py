@@ -282,7 +282,10 @@ def multilevel_attention_backward(
     dv = torch.empty(packed.v.shape, device=q.device, dtype=dtype)
     drel = None
     if position_mode == "relative":
-        drel = torch.zeros(B, N, Hq, args.rel_bins, device=q.device, dtype=torch.float32)
+        # the tensor-core path writes every element (zeros past each row's
+        # visible count); the SIMT path writes visible bins only
+        alloc = torch.empty if args.rel_logits else torch.zeros
+        drel = alloc(B, N, Hq, args.rel_bins, device=q.device, dtype=torch.float32)
     args.lse = lc.data_ptr()
     args.o = oc.data_ptr()
     args.dout = gc.data_ptr()
