@@ -44,6 +44,13 @@ WORKLOADS = {
     "c2": dict(B=2, T=8192, H=16, D=128, levels=6, W=256, weights="linear", position="rope",
                softcap=30.0, sink=True, conv=4, d_rel=0,
                desc="BASELINE config 2 shape (attention fwd+bwd)"),
+    # reduced shapes of the same kernels for ncu captures (a few GB on the device)
+    "c3_small": dict(B=1, T=16384, H=4, D=128, levels=8, W=512, weights="qk", position="relative",
+                     softcap=50.0, sink=True, conv=0, d_rel=16,
+                     desc="config 3 schedule and features at B=1, H=4 (profiling case)"),
+    "c5_small": dict(B=1, T=32768, H=4, D=128, levels=10, W=1024, weights="linear", position="rope",
+                     softcap=50.0, sink=True, conv=0, d_rel=0,
+                     desc="config 5 schedule and features at T=32768, H=4 (profiling case)"),
 }
 EMB = 2048
 
