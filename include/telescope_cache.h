@@ -221,8 +221,8 @@ typedef struct tc_attn_args {
   /* Relative mode on the tensor-core path: the bias logits
    * rel_logits[row, pad + d] = relative_states[row] . relative_proj[:, d]
    * (row = (b * N + q) * Hq + hq, d = bin distance) in the element type,
-   * with `pad` zero columns on each side of the bins a query can reach;
-   * row stride rel_logits_stride elements (a multiple of 8).  NULL: the
+   * with `pad` (>= 136) zero columns on each side of the bins a query can
+   * reach; row stride rel_logits_stride elements (a multiple of 8).  NULL: the
    * relative mode runs on the SIMT kernels, which form the bias from
    * rel_states / rel_proj directly. */
   const void* rel_logits;

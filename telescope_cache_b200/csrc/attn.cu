@@ -43,7 +43,7 @@ static int make_params(const tc_attn_args* a, const tc_schedule* s, AttnParams* 
   p->rl_stride = a->rel_logits_stride;
   p->rl_pad = a->rel_logits_pad;
   p->tile_n = a->tile_n;
-  if (p->rl && (p->rl_stride % 8 || p->rl_pad < 128 || a->position_mode != TC_POS_RELATIVE)) return TC_ERR_ARG;
+  if (p->rl && (p->rl_stride % 8 || p->rl_pad < 136 || a->position_mode != TC_POS_RELATIVE)) return TC_ERR_ARG;
   if (p->tile_n != 0 && p->tile_n != 64 && p->tile_n != 128) return TC_ERR_ARG;
   p->s = make_sched(*s);
   return TC_OK;

@@ -69,8 +69,11 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
   uint64_t* o_done = p_full + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(o_done + 1);
+  uint64_t* run_full = o_done + 1;   // relative: staged bias runs ready (warps 2-3)
+  uint64_t* run_empty = run_full + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(run_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  uint16_t* run_s = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [2][128][72]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * BQ, hq = blockIdx.y, b = blockIdx.z;
@@ -86,6 +89,8 @@ __global__ void __launch_bounds__(256, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 128);
+      mbar_init(&run_full[i], 64);
+      mbar_init(&run_empty[i], 128);
     }
     mbar_init(p_full, 128);
     mbar_init(o_done, 1);
@@ -174,7 +179,12 @@ __global__ void __launch_bounds__(256, 1)
         issue_pv(j - 1);
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp < 4) {
+    // ---------------- relative bias staging (warps 2, 3) ----------------
+    if constexpr (REL)
+      stage_runs(threadIdx.x - 64, q0, q1, p.N, p.Hq, hq, b, p.s, p.rl, p.rl_stride, p.rl_pad, run_s, run_full,
+                 run_empty, abort_flag, status);
+  } else {
     // ---------------- softmax / epilogue: one query row per thread ----------------
     const int r = threadIdx.x - 128;
     const int q = q0 + r;
@@ -184,10 +194,8 @@ __global__ void __launch_bounds__(256, 1)
     const float kq = p.has_cap ? p.scale / p.cap : p.scale * kLog2e;
     const float kb = p.has_cap ? 1.f / p.cap : kLog2e;
     const float kc = p.cap * kLog2e;
-    const uint16_t* rl_row = nullptr;
-    if (REL) rl_row = p.rl + (((int64_t)b * p.N + (row_ok ? q : 0)) * p.Hq + hq) * p.rl_stride;
     float m_used = -INFINITY, ell = 0.f;
-    int lo = 0, hi = 0, base = 0, cur = -1;
+    int lo = 0, hi = 0, cur = -1;
     TileWalk it{-1, 0, 0, q0, q1, BK};
     bool ok = it.start(p.s);
     int j = 0;
@@ -196,18 +204,10 @@ __global__ void __launch_bounds__(256, 1)
     for (; ok; ++j, ok = it.advance(p.s)) {
       if (it.lev != cur) {
         cur = it.lev;
-        lo = hi = base = 0;
+        lo = hi = 0;
         if (row_ok) {
-          if (REL) {
-            int los[TC_MAX_LEVELS], his[TC_MAX_LEVELS];
-            row_bounds(q, p.s, los, his);
-            lo = los[cur];
-            hi = his[cur];
-            base = bin_base(cur, los, his);
-          } else {
-            level_bounds_raw(q, cur, p.s, &lo, &hi);
-            if (lo >= hi) lo = hi = 0;
-          }
+          level_bounds_raw(q, cur, p.s, &lo, &hi);
+          if (lo >= hi) lo = hi = 0;
         }
       }
       const int bb = j & 1;
@@ -220,36 +220,43 @@ __global__ void __launch_bounds__(256, 1)
       tc_fence_before();
       mbar_arrive(&s_free[bb]);
       const int jlo = lo - it.k0, jhi = hi - it.k0;
-      float mx = -INFINITY;
+      const bool interior = jlo <= 0 && jhi >= BK;  // every column visible: no mask
+      float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if constexpr (REL) {
         static_assert(!REL || BK == 64, "the relative bias path uses 64-node tiles");
-        uint32_t run[32];
-        const bool any = jlo < BK && jhi > 0 && lo < hi;
-        if (any) {
-          // columns c see bin distance base - k0 - c: the run rl[pad + base - k0 - 63 + i]
-          load_run64(rl_row, p.rl_pad + base - it.k0 - (BK - 1), run);
-        } else {
+        // columns c see bin distance base - k0 - c: staged run element 63 - c
+        alive = __all_sync(0xffffffffu, mbar_wait(&run_full[bb], (j >> 1) & 1, abort_flag, status));
+        if (!alive) break;
+        // 8 columns per 16-byte read: columns 8*c8 .. 8*c8+7 use elements
+        // 63-8*c8 .. 56-8*c8, i.e. vector 7-c8 read back to front.
+        const uint4* runp = reinterpret_cast<const uint4*>(run_s + bb * 128 * kRunStride + r * kRunStride);
 #pragma unroll
-          for (int k = 0; k < 32; ++k) run[k] = 0u;
-        }
+        for (int c8 = 0; c8 < BK / 8; ++c8) {
+          const uint4 v = runp[7 - c8];
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int c = 0; c < BK; ++c) {
-          float x = fmaf(sv[c], kq, run_elem<T>(run, BK - 1 - c) * kb);
-          if (p.has_cap) x = tanh_fast(x) * kc;
-          x = (c >= jlo && c < jhi) ? x : -INFINITY;
-          sv[c] = x;
-          mx = fmaxf(mx, x);
+          for (int i = 0; i < 8; ++i) {
+            const int c = c8 * 8 + i, e = 7 - i;
+            const uint16_t h = (e & 1) ? (uint16_t)(w[e >> 1] >> 16) : (uint16_t)(w[e >> 1] & 0xffffu);
+            float x = fmaf(sv[c], kq, bits_to_float<T>(h) * kb);
+            if (p.has_cap) x = tanh_fast(x) * kc;
+            if (!interior) x = (c >= jlo && c < jhi) ? x : -INFINITY;
+            sv[c] = x;
+            mxp[c & 3] = fmaxf(mxp[c & 3], x);
+          }
         }
+        mbar_arrive(&run_empty[bb]);
       } else {
 #pragma unroll
         for (int c = 0; c < BK; ++c) {
           float x = sv[c] * kq;
           if (p.has_cap) x = tanh_fast(x) * kc;
-          x = (c >= jlo && c < jhi) ? x : -INFINITY;
+          if (!interior) x = (c >= jlo && c < jhi) ? x : -INFINITY;
           sv[c] = x;
-          mx = fmaxf(mx, x);
+          mxp[c & 3] = fmaxf(mxp[c & 3], x);
         }
       }
+      const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
       bool rescale = false;
       float alpha = 1.f;
       if (mx > -INFINITY) {
@@ -279,7 +286,7 @@ __global__ void __launch_bounds__(256, 1)
         }
         tmem_wait_st();
       }
-      float sum = 0.f;
+      float sp[4] = {0.f, 0.f, 0.f, 0.f};
       const bool live = m_used > -INFINITY;
 #pragma unroll
       for (int c8 = 0; c8 < BK / 8; ++c8) {
@@ -287,10 +294,11 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           pv[i] = live ? exp2_fast(sv[c8 * 8 + i] - m_used) : 0.f;
-          sum += pv[i];
+          sp[i & 3] += pv[i];
         }
         *reinterpret_cast<uint4*>(p_s + sw128_offset(r, c8 * 8, 128)) = pack8<T>(pv, 1.f);
       }
+      const float sum = (sp[0] + sp[1]) + (sp[2] + sp[3]);
       ell += sum;
       fence_async_smem();
       tc_fence_before();
@@ -346,7 +354,7 @@ int launch_fwd(const AttnParams& a, int dtype, cudaStream_t st) {
   p.rl_stride = a.rl_stride;
   p.rl_pad = a.rl_pad;
   p.s = a.s;
-  constexpr int smem = FwdShape<BK>::SMEM;
+  constexpr int smem = FwdShape<BK>::SMEM + (REL ? 2 * 128 * kRunStride * 2 : 0);
   auto k = fwd_tc_kernel<T, BK, REL>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TC_ERR_CUDA;
   k<<<dim3((a.N + BQ - 1) / BQ, a.Hq, a.B), 256, smem, st>>>(mq, mk, mv, p);

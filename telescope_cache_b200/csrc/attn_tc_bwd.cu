@@ -29,10 +29,15 @@ constexpr int T64 = 64 * 128 * 2;    // [64 rows x 128] tile
 constexpr int B128 = 128 * 128;      // one 64-col block of a 128-row tile
 constexpr int B64 = 64 * 128;        // one 64-col block of a 64-row tile
 constexpr int kSmemA = 2 * T128 + 4 * T64 + 128 * 128 + 1024 + 256;
-// relative Pass A: + two fp32 dX staging tiles [128 x 65] and per-row run info
+// relative Pass A: + an fp32 dX staging tile [128 x 65], per-row run info,
+// row totals and the double-buffered bias runs [2][128][kRunStride]
 constexpr int kDxfStride = 65;
-constexpr int kSmemArel = kSmemA + 2 * 128 * kDxfStride * 4 + 2 * 128 * 3 * 4 + 128 * 4;
-constexpr int kSmemB = 2 * T128 + 4 * T64 + 2 * 128 * 128 + 6 * 64 * 4 + 1024 + 256;
+constexpr int kSmemArel = kSmemA + 128 * kDxfStride * 4 + 128 * 3 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2;
+// Pass B: tiles + per-step query info [2][64] (int4) + bias offsets [2][64]
+// (bytes) + barriers; relative adds the staged bias columns [2][64][kColStride]
+constexpr int kColStride = 136;  // 272 B: the 16-byte aligned superset of a 128-node run
+constexpr int kSmemB = 2 * T128 + 4 * T64 + 2 * 128 * 128 + 2 * 64 * 16 + 2 * 64 + 256 + 1024;
+constexpr int kSmemBrel = kSmemB + 2 * 64 * kColStride * 2;
 
 struct BwdParams {
   int N, Hq, Hkv, E;
@@ -99,12 +104,16 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* x_full = bars + 9;
   uint64_t* x_free = bars + 10;
   uint64_t* dq_done = bars + 11;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* run_full = bars + 12;   // relative: staged bias runs ready (warps 2-3)
+  uint64_t* run_empty = bars + 14;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  // relative only: fp32 dX staging [2][128][65], run info [2][128][3], row totals [128]
+  // relative only: fp32 dX staging [128][65], run info [128][3], row totals
+  // [128], bias runs [2][128][kRunStride]
   float* dxf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
-  int* rinfo = reinterpret_cast<int*>(dxf + 2 * 128 * kDxfStride);
-  int* mtot = rinfo + 2 * 128 * 3;
+  int* rinfo = reinterpret_cast<int*>(dxf + 128 * kDxfStride);
+  int* mtot = rinfo + 128 * 3;
+  uint16_t* run_s = reinterpret_cast<uint16_t*>(mtot + 128);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * 128, hq = blockIdx.y, b = blockIdx.z;
@@ -119,6 +128,8 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 128);
+      mbar_init(&run_full[i], 64);
+      mbar_init(&run_empty[i], 128);
     }
     mbar_init(x_full, 128);
     mbar_init(x_free, 1);
@@ -205,7 +216,12 @@ __global__ void __launch_bounds__(256, 1)
       }
       mma_commit(dq_done);
     }
-  } else if (warp >= 4) {
+  } else if (warp < 4) {
+    // relative bias staging (warps 2, 3)
+    if constexpr (REL)
+      stage_runs(threadIdx.x - 64, q0, q1, p.N, p.Hq, hq, b, p.s, p.rl, p.rl_stride, p.rl_pad, run_s, run_full,
+                 run_empty, abort_flag, status);
+  } else {
     const int r = threadIdx.x - 128;
     const int q = q0 + r;
     const bool row_ok = q < p.N;
@@ -214,12 +230,8 @@ __global__ void __launch_bounds__(256, 1)
     const int64_t row = ((int64_t)b * p.N + q) * p.Hq + hq;
     const float lse2 = row_ok ? p.lse[row] * kLog2e : 0.f;
     const float dlt = row_ok ? p.delta[row] : 0.f;
-    const uint16_t* rl_row = REL ? p.rl + (row_ok ? row : 0) * p.rl_stride : nullptr;
     const bool want_drel = REL && p.drel != nullptr;
-    if (want_drel) {
-      int los[TC_MAX_LEVELS], his[TC_MAX_LEVELS];
-      mtot[r] = row_ok ? row_bounds(q, p.s, los, his) : 0;
-    }
+    if (want_drel) mtot[r] = row_ok ? visible_count(q, p.s) : 0;
     int lo = 0, hi = 0, base = 0, cur = -1;
     TileWalk it{-1, 0, 0, q0, q1, 64};
     bool ok = it.start(p.s);
@@ -231,11 +243,7 @@ __global__ void __launch_bounds__(256, 1)
         lo = hi = base = 0;
         if (row_ok) {
           if (REL) {
-            int los[TC_MAX_LEVELS], his[TC_MAX_LEVELS];
-            row_bounds(q, p.s, los, his);
-            lo = los[cur];
-            hi = his[cur];
-            base = bin_base(cur, los, his);
+            level_info(q, cur, p.s, &lo, &hi, &base);
           } else {
             level_bounds_raw(q, cur, p.s, &lo, &hi);
             if (lo >= hi) lo = hi = 0;
@@ -259,31 +267,41 @@ __global__ void __launch_bounds__(256, 1)
         if (!alive) break;
       }
       const int jlo = lo - it.k0, jhi = hi - it.k0;
-      uint32_t run[REL ? 32 : 1];
+      // column c has bin distance base - k0 - c: staged run element 63 - c
+      // (columns 8*c8 .. 8*c8+7 are vector 7-c8 of the row, back to front)
+      const uint4* runp = nullptr;
       if constexpr (REL) {
-        // column c has bin distance base - k0 - c: the run rl[pad + base - k0 - 63 + i]
-        if (jlo < 64 && jhi > 0 && lo < hi) {
-          load_run64(rl_row, p.rl_pad + base - it.k0 - 63, run);
-        } else {
-#pragma unroll
-          for (int k = 0; k < 32; ++k) run[k] = 0u;
-        }
+        alive = __all_sync(0xffffffffu, mbar_wait(&run_full[bb], (j >> 1) & 1, abort_flag, status));
+        if (!alive) break;
+        runp = reinterpret_cast<const uint4*>(run_s + bb * 128 * kRunStride + r * kRunStride);
       }
+      // the single dX staging tile is free once every warp wrote out the last one
+      if (want_drel && j >= 1) named_bar(1, 128);
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
         float dx[8];
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        if constexpr (REL) {
+          const uint4 v = runp[7 - c8];
+          w[0] = v.x;
+          w[1] = v.y;
+          w[2] = v.z;
+          w[3] = v.w;
+        }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int c = c8 * 8 + i;
+          const int c = c8 * 8 + i, e = 7 - i;
+          const uint16_t h = (e & 1) ? (uint16_t)(w[e >> 1] >> 16) : (uint16_t)(w[e >> 1] & 0xffffu);
           float l2, g;
-          sc.logit(sv[c], REL ? run_elem<T>(run, 63 - c) : 0.f, p.has_cap, &l2, &g);
+          sc.logit(sv[c], REL ? bits_to_float<T>(h) : 0.f, p.has_cap, &l2, &g);
           const bool valid = c >= jlo && c < jhi;
           const float pr = valid ? exp2_fast(l2 - lse2) : 0.f;
           dx[i] = valid ? pr * (dp[c] - dlt) * g : 0.f;
-          if (want_drel) dxf[(j & 1) * 128 * kDxfStride + r * kDxfStride + c] = dx[i];
+          if (want_drel) dxf[r * kDxfStride + c] = dx[i];
         }
         *reinterpret_cast<uint4*>(x_s + sw128_offset(r, c8 * 8, 128)) = pack8<T>(dx, 1.f);
       }
+      if constexpr (REL) mbar_arrive(&run_empty[bb]);
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(x_full);
@@ -292,14 +310,14 @@ __global__ void __launch_bounds__(256, 1)
         // valid columns [cs, ce) are distances base - k0 - c, one ascending run
         // in memory; the warp then writes its 32 rows' runs coalesced.
         const int cs = max(jlo, 0), ce = min(jhi, 64);
-        int* ri = rinfo + (j & 1) * 128 * 3 + r * 3;
+        int* ri = rinfo + r * 3;
         ri[0] = base - it.k0 - (ce - 1);
         ri[1] = (row_ok && lo < hi && ce > cs) ? ce - cs : 0;
         ri[2] = ce;
         named_bar(1, 128);
         const int w4 = warp - 4;
-        const float* src = dxf + (j & 1) * 128 * kDxfStride;
-        const int* inf = rinfo + (j & 1) * 128 * 3;
+        const float* src = dxf;
+        const int* inf = rinfo;
         for (int k = 0; k < 32; ++k) {
           const int rr = w4 * 32 + k;
           const int n = inf[rr * 3 + 1];
@@ -386,12 +404,10 @@ __global__ void __launch_bounds__(256, 1)
   uint8_t* g_s = q_s + 2 * T64;
   uint8_t* pt_s = g_s + 2 * T64;  // P^T  [128 x 64]
   uint8_t* xt_s = pt_s + 128 * 128;  // dX^T [128 x 64]
-  float* lse_s = reinterpret_cast<float*>(xt_s + 128 * 128);  // [64]
-  float* dlt_s = lse_s + 64;
-  int* lo_s = reinterpret_cast<int*>(dlt_s + 64);
-  int* hi_s = lo_s + 64;
-  int64_t* rl_s = reinterpret_cast<int64_t*>(hi_s + 64);  // [64] relative: row + pad + base
-  uint64_t* bars = reinterpret_cast<uint64_t*>(rl_s + 64);
+  // per step (double buffered), per query column: {lo, hi, lse * log2e, Delta}
+  int4* info_s = reinterpret_cast<int4*>(xt_s + 128 * 128);  // [2][64]
+  uint8_t* bo_s = reinterpret_cast<uint8_t*>(info_s + 2 * 64);  // [2][64] relative: run offset - 127
+  uint64_t* bars = reinterpret_cast<uint64_t*>(bo_s + 2 * 64);
   uint64_t* kv_full = bars;
   uint64_t* q_full = bars + 1;
   uint64_t* q_empty = bars + 3;
@@ -400,8 +416,13 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* x_full = bars + 9;
   uint64_t* x_free = bars + 10;
   uint64_t* kv_done = bars + 11;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* info_full = bars + 12;   // warps 2-3: step info (and bias columns) ready
+  uint64_t* info_empty = bars + 14;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  // relative: bias column c of a step holds rl[row_c, pad + base_c - k0 - 127 - o_c ...]
+  // (272 B from the 16-byte boundary below it); node r reads element o_c + 127 - r
+  uint16_t* bias_s = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(bars) + 256);
 
   int lev = 0;
   while (lev + 1 < p.s.nl && (int)blockIdx.x >= p.tiles[lev + 1]) ++lev;
@@ -421,6 +442,8 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 128);
+      mbar_init(&info_full[i], 64);
+      mbar_init(&info_empty[i], 128);
     }
     mbar_init(x_full, 128);
     mbar_init(x_free, 1);
@@ -514,7 +537,52 @@ __global__ void __launch_bounds__(256, 1)
       }
       mma_commit(kv_done);
     }
-  } else if (warp >= 4) {
+  } else if (warp < 4) {
+    // ---------------- step info / bias staging (warps 2, 3): one query column per thread ----------------
+    const int t = threadIdx.x - 64;
+    QSteps w;
+    bool ok = w.start(qlo, qhi, p.E);
+    for (int i = 0; ok; ++i, ok = w.advance()) {
+      const int buf = i & 1;
+      if (i >= 2 && !__all_sync(0xffffffffu, mbar_wait(&info_empty[buf], ((i >> 1) - 1) & 1, abort_flag, status)))
+        break;
+      const int hq = hkv * p.E + w.e;
+      const int q = w.qb + t;
+      const int64_t row = ((int64_t)b * p.N + q) * p.Hq + hq;
+      int lo = 0, hi = 0, base = 0;
+      float l2 = 0.f, dl = 0.f;
+      if (q < p.N) {
+        if (REL) {
+          level_info(q, lev, p.s, &lo, &hi, &base);
+        } else {
+          level_bounds_raw(q, lev, p.s, &lo, &hi);
+          if (lo >= hi) lo = hi = 0;
+        }
+        l2 = p.lse[row] * kLog2e;
+        dl = p.delta[row];
+      }
+      const int ci = buf * 64 + t;
+      info_s[ci] = make_int4(lo, hi, __float_as_int(l2), __float_as_int(dl));
+      if constexpr (REL) {
+        // nodes k0 + r see distance base - k0 - r: one descending run of 128
+        // elements ending at rl[row, pad + base - k0]; some node of the tile
+        // is visible, so base >= k0 and the 16-byte superset stays inside the
+        // row's padding (pad >= 136)
+        if (lo < hi && lo < k0 + nk && hi > k0) {
+          const int64_t e0 = row * p.rl_stride + p.rl_pad + base - k0 - 127;
+          const int64_t a = e0 & ~int64_t(7);
+          bo_s[ci] = (uint8_t)(e0 - a);
+          mbar_expect_tx(&info_full[buf], kColStride * 2);
+          bulk_load(bias_s + ci * kColStride, p.rl + a, kColStride * 2, &info_full[buf]);
+        } else {
+          bo_s[ci] = 0;
+          mbar_arrive(&info_full[buf]);
+        }
+      } else {
+        mbar_arrive(&info_full[buf]);
+      }
+    }
+  } else {
     const int r = threadIdx.x - 128;     // node row = TMEM lane
     const int jn = k0 + r;               // level-local node index
     const bool node_ok = r < nk;
@@ -525,36 +593,6 @@ __global__ void __launch_bounds__(256, 1)
     bool alive = true;
     int i = 0;
     for (; ok; ++i, ok = w.advance()) {
-      const int hq = hkv * p.E + w.e;
-      named_bar(1, 128);  // everyone is done with the previous step's row data
-      if (r < 64) {
-        const int q = w.qb + r;
-        int lo = 0, hi = 0;
-        float l2 = 0.f, dl = 0.f;
-        int64_t rlo = 0;
-        if (q < p.N) {
-          const int64_t row = ((int64_t)b * p.N + q) * p.Hq + hq;
-          if (REL) {
-            int los[TC_MAX_LEVELS], his[TC_MAX_LEVELS];
-            row_bounds(q, p.s, los, his);
-            lo = los[lev];
-            hi = his[lev];
-            // bias of node j: rl[row, pad + base - j]
-            rlo = row * p.rl_stride + p.rl_pad + bin_base(lev, los, his);
-          } else {
-            level_bounds_raw(q, lev, p.s, &lo, &hi);
-            if (lo >= hi) lo = hi = 0;
-          }
-          l2 = p.lse[row] * kLog2e;
-          dl = p.delta[row];
-        }
-        lo_s[r] = lo;
-        hi_s[r] = hi;
-        lse_s[r] = l2;
-        dlt_s[r] = dl;
-        if (REL) rl_s[r] = rlo;
-      }
-      named_bar(1, 128);
       const int bb = i & 1;
       alive = __all_sync(0xffffffffu, mbar_wait(&s_full[bb], (i >> 1) & 1, abort_flag, status));
       if (!alive) break;
@@ -571,27 +609,37 @@ __global__ void __launch_bounds__(256, 1)
         alive = __all_sync(0xffffffffu, mbar_wait(x_free, (i - 1) & 1, abort_flag, status));
         if (!alive) break;
       }
+      alive = __all_sync(0xffffffffu, mbar_wait(&info_full[bb], (i >> 1) & 1, abort_flag, status));
+      if (!alive) break;
+      const int4* inf = info_s + bb * 64;
+      const uint8_t* bo = bo_s + bb * 64;
+      const uint16_t* bcol = bias_s + bb * 64 * kColStride + 127 - r;
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
         float pr[8], dx[8];
+        uint2 bo8 = make_uint2(0u, 0u);
+        if constexpr (REL) bo8 = *reinterpret_cast<const uint2*>(bo + c8 * 8);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const int c = c8 * 8 + k;
-          const bool valid = node_ok && jn >= lo_s[c] && jn < hi_s[c];
+          const int4 ci = inf[c];
+          const bool valid = node_ok && jn >= ci.x && jn < ci.y;
           float bias = 0.f;
-          if (REL && valid) {
-            // lanes hold consecutive nodes: consecutive (descending) addresses
-            bias = bits_to_float<T>(__ldg(p.rl + rl_s[c] - jn));
+          if constexpr (REL) {
+            // lanes hold consecutive nodes: consecutive (descending) halves
+            const uint32_t o = ((k < 4 ? bo8.x : bo8.y) >> (8 * (k & 3))) & 0xffu;
+            bias = bits_to_float<T>(bcol[c * kColStride + o]);
           }
           float l2, g;
           sc.logit(sv[c], bias, p.has_cap, &l2, &g);
-          pr[k] = valid ? exp2_fast(l2 - lse_s[c]) : 0.f;
-          dx[k] = valid ? pr[k] * (dp[c] - dlt_s[c]) * g : 0.f;
+          pr[k] = valid ? exp2_fast(l2 - __int_as_float(ci.z)) : 0.f;
+          dx[k] = valid ? pr[k] * (dp[c] - __int_as_float(ci.w)) * g : 0.f;
         }
         const uint32_t off = sw128_offset(r, c8 * 8, 128);
         *reinterpret_cast<uint4*>(pt_s + off) = pack8<T>(pr, 1.f);
         *reinterpret_cast<uint4*>(xt_s + off) = pack8<T>(dx, 1.f);
       }
+      mbar_arrive(&info_empty[bb]);
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(x_full);
@@ -686,9 +734,10 @@ int launch_bwd(const AttnParams& a, int dtype, cudaStream_t st) {
   const int ntiles = p.tiles[a.s.nl];
   if (ntiles > 0) {
     auto kb = bwd_dkv_tc_kernel<T, REL>;
-    if (cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemB) != cudaSuccess)
+    constexpr int smem_b = REL ? kSmemBrel : kSmemB;
+    if (cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_b) != cudaSuccess)
       return TC_ERR_CUDA;
-    kb<<<dim3(ntiles, a.Hkv, a.B), 256, kSmemB, st>>>(mq64, mg64, mk128, mv128, p);
+    kb<<<dim3(ntiles, a.Hkv, a.B), 256, smem_b, st>>>(mq64, mg64, mk128, mv128, p);
     if (int rc = launch_status()) return rc;
   }
   return TC_OK;

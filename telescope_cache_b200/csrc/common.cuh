@@ -119,11 +119,51 @@ TC_HD void level_bounds_raw(int q, int l, const Sched& s, int* lo, int* hi) {
     *hi = imax(q - s.act[l] + (1 << l), 0) >> l;
     *lo = (imax(q - s.act[l + 1] + (2 << l), 0) >> (l + 1)) * 2;
   } else {
-    int los[TC_MAX_LEVELS], his[TC_MAX_LEVELS];
-    row_bounds_raw(q, s.act, s.nl, s.cache, los, his);
-    *lo = los[top];
-    *hi = his[top];
+    int used = 0;
+    for (int i = 0; i < top; ++i) {
+      const int h = imax(q - s.act[i] + (1 << i), 0) >> i;
+      const int o = (imax(q - s.act[i + 1] + (2 << i), 0) >> (i + 1)) * 2;
+      used += imax(h - o, 0);
+    }
+    const int ht = imax(q - s.act[top] + (1 << top), 0) >> top;
+    *lo = imax(ht - (s.cache - used), 0);
+    *hi = ht;
   }
+}
+
+// Normalised bounds of level l for query q together with its bin base
+// (bin_base below), computed in one pass over the levels with no per-level
+// arrays, so device code keeps everything in registers.
+TC_HD void level_info(int q, int l, const Sched& s, int* lo, int* hi, int* base) {
+  const int top = s.nl - 1;
+  int used = 0, below = 0, ol = 0, hl = 0;
+  for (int i = 0; i < top; ++i) {
+    const int h = imax(q - s.act[i] + (1 << i), 0) >> i;
+    const int o = (imax(q - s.act[i + 1] + (2 << i), 0) >> (i + 1)) * 2;
+    const int c = imax(h - o, 0);
+    if (i < l) below += c;
+    if (i == l) {
+      ol = o;
+      hl = h;
+    }
+    used += c;
+  }
+  if (l == top) {
+    hl = imax(q - s.act[top] + (1 << top), 0) >> top;
+    ol = imax(hl - (s.cache - used), 0);
+  }
+  if (ol >= hl) ol = hl = 0;
+  *lo = ol;
+  *hi = hl;
+  *base = below + hl - 1;
+}
+
+// Number of nodes query q sees (row_bounds' total) without per-level arrays:
+// the coarsest level's bin base is (finer counts) + hi - 1.
+TC_HD int visible_count(int q, const Sched& s) {
+  int lo, hi, base;
+  level_info(q, s.nl - 1, s, &lo, &hi, &base);
+  return base + 1 - lo;
 }
 
 // O(1) hull of the level-l ranges over queries [q0, q1) (range_spec.py:187-202):

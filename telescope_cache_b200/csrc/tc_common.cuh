@@ -125,6 +125,130 @@ __device__ __forceinline__ float run_elem(const uint32_t* run, int i) {
   return bits_to_float<T>((i & 1) ? (uint16_t)(w >> 16) : (uint16_t)(w & 0xffffu));
 }
 
+// ---------------------------------------------------------------------------
+// Relative-bias staging by the CTA's otherwise idle warps 2-3, so that the
+// softmax threads read the bias from shared memory instead of waiting on
+// scattered global loads.
+// ---------------------------------------------------------------------------
+constexpr int kRunStride = 72;  // elements per staged row (144 B: 16-B accesses conflict-light)
+
+// q-major kernels (forward, Pass A), 64-node tiles: for every tile of the
+// walk and every query row r of the block, run_s[buf][r][i] =
+// rl[row, pad + base_r - k0 - 63 + i] for i < 64 (zeros for rows without a
+// visible node in the tile).  Thread t (0..63 of warps 2-3) owns rows t and
+// t + 64: per row and tile it loads the 16-byte aligned 144-byte superset of
+// the run (9 vector loads), realigns it in registers and stores it with
+// 16-byte writes.  The loads of tile j + 1 are issued before tile j is
+// realigned and stored, so one tile's latency is always hidden.
+__device__ __forceinline__ void stage_runs(int t, int q0, int q1, int N, int Hq, int hq, int b, const Sched& s,
+                                           const uint16_t* rl, int64_t stride, int pad, uint16_t* run_s,
+                                           uint64_t* run_full, uint64_t* run_empty, volatile int* abort_flag,
+                                           int32_t* status) {
+  int64_t roff[2];
+  bool rok[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int q = q0 + t + 64 * h;
+    rok[h] = q < N;
+    roff[h] = rok[h] ? (((int64_t)b * N + q) * Hq + hq) * stride + pad : 0;
+  }
+  TileWalk it{-1, 0, 0, q0, q1, 64};
+  int cur = -1;
+  int lo[2] = {0, 0}, hi[2] = {0, 0}, base[2] = {0, 0};
+  uint4 raw[2][9];
+  int sh[2] = {0, 0};
+  bool vis[2] = {false, false};
+  auto issue = [&]() {
+    if (it.lev != cur) {
+      cur = it.lev;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        lo[h] = hi[h] = base[h] = 0;
+        if (rok[h]) level_info(q0 + t + 64 * h, cur, s, &lo[h], &hi[h], &base[h]);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      vis[h] = lo[h] < hi[h] && lo[h] - it.k0 < 64 && hi[h] - it.k0 > 0;
+      const int64_t e0 = roff[h] + base[h] - it.k0 - 63;
+      const int64_t a = e0 & ~int64_t(7);
+      sh[h] = (int)(e0 - a);
+      if (vis[h]) {
+        const uint4* src = reinterpret_cast<const uint4*>(rl + a);
+#pragma unroll
+        for (int i = 0; i < 9; ++i) raw[h][i] = __ldg(src + i);
+      }
+    }
+  };
+  bool ok = it.start(s);
+  if (ok) issue();
+  for (int j = 0; ok; ++j) {
+    uint4 pend[2][9];
+    int psh[2];
+    bool pvis[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      psh[h] = sh[h];
+      pvis[h] = vis[h];
+#pragma unroll
+      for (int i = 0; i < 9; ++i) pend[h][i] = raw[h][i];
+    }
+    ok = it.advance(s);
+    if (ok) issue();  // next tile's loads in flight while this one is stored
+    const int buf = j & 1;
+    if (j >= 2 && !__all_sync(0xffffffffu, ptx::mbar_wait(&run_empty[buf], ((j >> 1) - 1) & 1, abort_flag, status)))
+      break;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint4* dst = reinterpret_cast<uint4*>(run_s + buf * 128 * kRunStride + (t + 64 * h) * kRunStride);
+      if (!pvis[h]) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = make_uint4(0u, 0u, 0u, 0u);
+        continue;
+      }
+      uint32_t w[36];
+#pragma unroll
+      for (int i = 0; i < 9; ++i) {
+        w[4 * i] = pend[h][i].x;
+        w[4 * i + 1] = pend[h][i].y;
+        w[4 * i + 2] = pend[h][i].z;
+        w[4 * i + 3] = pend[h][i].w;
+      }
+      // drop sh halves: whole words by two select stages, then one funnel shift
+      const int wo = psh[h] >> 1;
+#pragma unroll
+      for (int i = 0; i < 35; ++i) w[i] = (wo & 1) ? w[i + 1] : w[i];
+#pragma unroll
+      for (int i = 0; i < 33; ++i) w[i] = (wo & 2) ? w[i + 2] : w[i];
+      const bool odd = psh[h] & 1;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int m = 4 * i + k;
+          o[k] = odd ? __funnelshift_r(w[m], w[m + 1], 16) : w[m];
+        }
+        dst[i] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    ptx::mbar_arrive(&run_full[buf]);
+  }
+}
+
+// A staged run row as 32 packed words (element 2k in the low half of word k).
+__device__ __forceinline__ void read_run(const uint16_t* row, uint32_t* w) {
+  const uint4* src = reinterpret_cast<const uint4*>(row);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint4 v = src[i];
+    w[4 * i] = v.x;
+    w[4 * i + 1] = v.y;
+    w[4 * i + 2] = v.z;
+    w[4 * i + 3] = v.w;
+  }
+}
+
 // Inverse RoPE (rotate by R(-p)) of a 128-wide fp32 row held by one thread.
 __device__ __forceinline__ void rope_inverse_row(float* v, const float* cos_t, const float* sin_t, int pos) {
   const float* c = cos_t + (int64_t)pos * (HD / 2);

@@ -49,7 +49,7 @@ def _impl_code(impl: Optional[str]) -> int:
     return {None: 0, "auto": 0, "simt": 1, "tensor": 2}[impl]
 
 
-REL_PAD = 128  # zero bins on each side of the relative band (>= one 64-node tile + 8)
+REL_PAD = 136  # zero bins on each side of the relative band (>= one 128-node tile + 8)
 
 
 def _relative_band(st, pj, max_visible, dtype):
