@@ -54,6 +54,12 @@ WORKLOADS = {
 }
 EMB = 2048
 
+# incremental decode after a 32768-token prefill.  The
+# config names no softcap; decode_step's default (20.0) is used.
+DECODE = dict(B=64, T=32768, H=16, D=128, levels=8, W=256, conv=4, softcap=20.0,
+              desc="BASELINE config 4: decode_step after a 32768-token prefill, rope, conv 4, "
+                   "sink, gate")
+
 
 def schedule(wl):
     fmap = {l: l * wl["W"] for l in range(1, wl["levels"])}
@@ -189,6 +195,112 @@ def run_step(T, wl, inp, fmap, cache, tables, timers=None):
     return dq, dk, dv, dpos, out
 
 
+def decode_visible(spec, t0, n):
+    """Visible entries of the newest query at t0 .. t0 + n - 1."""
+    from telescope_cache_b200 import range_spec as R
+    return [sum(hi - lo for lo, hi in (R.range_bounds(spec, t, lv) for lv in range(spec.num_levels)))
+            for t in range(t0, t0 + n)]
+
+
+def decode_bench(args, dev, world, with_e2e=True):
+    """Config 4: prefill (builder + init_decode_state) untimed, then W warm-up
+    and K timed decode_step calls through the public API.  Returns a dict
+    with tokens/s over all ranks (each rank its own batch of 64 rows) and the
+    HBM roofline of the ring reads (K + V of every visible entry)."""
+    import torch
+    import torch.distributed as dist
+
+    import telescope_cache_b200 as T
+    from telescope_cache_b200 import range_spec as R
+
+    c = DECODE
+    B, N, H, D = c["B"], c["T"], c["H"], c["D"]
+    fmap, cache = {l: l * c["W"] for l in range(1, c["levels"])}, c["levels"] * c["W"]
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321 + 7919 * int(os.environ.get("RANK", "0")))
+    kcw = torch.randn(H * D, c["conv"], generator=g, device=dev) / math.sqrt(c["conv"])
+    vcw = torch.randn(H * D, c["conv"], generator=g, device=dev) / math.sqrt(c["conv"])
+    steps = args.warmup + args.steps
+    cos, sin = T.rope_tables(N + steps + args.steps + 1, D, device=dev)
+    sinks = torch.randn(H, generator=g, device=dev)
+    gate_w = (0.02 * torch.randn(H * D, EMB, generator=g, device=dev)).to(bf)
+    q = torch.randn(B, N, H, D, generator=g, device=dev, dtype=bf)
+    k = torch.randn(B, N, H, D, generator=g, device=dev, dtype=bf)
+    v = torch.randn(B, N, H, D, generator=g, device=dev, dtype=bf)
+    kl, vl, wl = T.build_dyadic_summaries(q, k, v, c["levels"] - 1, k_conv_weight=kcw, v_conv_weight=vcw)
+    state = T.init_decode_state(kl, vl, wl, fmap, cache, k_pre_conv=k, v_pre_conv=v,
+                                conv_kernel_size=c["conv"])
+    del q, k, v, kl, vl, wl
+    tok = dict(x=torch.randn(steps, B, 1, EMB, generator=g, device=dev, dtype=bf),
+               q=torch.randn(steps, B, 1, H, D, generator=g, device=dev, dtype=bf),
+               k=torch.randn(steps, B, 1, H, D, generator=g, device=dev, dtype=bf),
+               v=torch.randn(steps, B, 1, H, D, generator=g, device=dev, dtype=bf))
+    kw = dict(k_conv_weight=kcw, v_conv_weight=vcw, softcap=c["softcap"], position_mode="rope",
+              rope_cos=cos, rope_sin=sin, sinks=sinks, gate_weight=gate_w)
+
+    def step(i, src):
+        return T.decode_step(src["x"][i], src["q"][i], src["k"][i], src["v"][i], state, **kw)
+
+    def sync():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    st = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        step(i, tok)
+    sync()
+    t_first = state.t
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for i in range(args.warmup, steps):
+        step(i, tok)
+    b.record(st)
+    sync()
+    ms = a.elapsed_time(b) / args.steps
+    if world > 1:
+        tm = torch.tensor([ms], device=dev)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms = float(tm.item())
+    spec = R.RangeSpec.from_fmap(fmap, cache, t_first + args.steps)
+    vis = decode_visible(spec, t_first, args.steps)
+    ring_bytes = sum(vis) / len(vis) * B * H * 2 * D * 2
+    _, _, hbm, src = peaks()
+    gbs = ring_bytes / (ms * 1e-3) / 1e9
+    res = {"metric": "decode tokens/s", "value": B * world / (ms * 1e-3), "unit": "tokens/s",
+           "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
+           "config": {"workload": "c4", "desc": c["desc"], "B_per_rank": B, "prefill": N, "H": H,
+                      "D": D, "fmap": fmap, "cache_size": cache, "caps": list(state.caps),
+                      "softcap": c["softcap"], "visible_per_step": sum(vis) / len(vis)},
+           "roofline": {"bound": "hbm", "kernel": "decode_step (whole public call)",
+                        "achieved": gbs, "peak": hbm, "peak_source": f"{src} hbm_gbs", "unit": "GB/s",
+                        "frac": gbs / hbm, "algorithmic_bytes_per_step": ring_bytes,
+                        "traffic": None}}
+    if with_e2e:
+        # every step copies its token inputs from pinned host memory and reads
+        # the output back
+        host = {k_: t_.cpu().pin_memory() for k_, t_ in tok.items()}
+        out_host = torch.empty(B, 1, H, D, dtype=bf, pin_memory=True)
+        h2d = sum(t_[0].numel() * t_.element_size() for t_ in host.values())
+        sync()
+        a.record(st)  # continues at t_first + K with the same token values
+        for i in range(args.warmup, steps):
+            dev_tok = {k_: t_[i].to(dev, non_blocking=True) for k_, t_ in host.items()}
+            out, _ = T.decode_step(dev_tok["x"], dev_tok["q"], dev_tok["k"], dev_tok["v"], state, **kw)
+            out_host.copy_(out, non_blocking=True)
+        b.record(st)
+        sync()
+        ems = a.elapsed_time(b) / args.steps
+        if world > 1:
+            tm = torch.tensor([ems], device=dev)
+            dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+            ems = float(tm.item())
+        res["e2e"] = {"value": B * world / (ems * 1e-3), "unit": "tokens/s", "ms_per_step": ems,
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_host.numel() * 2}
+    return res
+
+
 def cpu_reference_sample(wl, seconds_budget=20.0):
     """Time the CPU oracle (fwd + bwd) on a bounded sample of the workload:
     consecutive query rows of one (batch, head) slice, in the steady state
@@ -260,16 +372,53 @@ def reference_arm(args, wl):
     return 0
 
 
+def decode_main(args):
+    """--workload c4: the decode tokens/s line on its own."""
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the decode reference arm is not implemented; the default c3 line "
+                              "carries the reference comparison"}))
+        return 0
+    import torch
+    import torch.distributed as dist
+
+    from telescope_cache_b200 import _lib
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    n0 = _lib.launch_count()
+    with ClockSampler(local) as clocks:
+        res = decode_bench(args, dev, world, with_e2e=not args.no_e2e)
+    if rank == 0:
+        res.update({"n_gpus": world, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                    "dtype": "bf16", "data": "synthetic", "cpu_baseline": None,
+                    "clocks": clocks.summary(), "gpu_launches": _lib.launch_count() - n0})
+        print(json.dumps(res))
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS) + ["c4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="skip the config-4 decode measurement added to the c3 line")
     args = ap.parse_args()
+    if args.workload == "c4":
+        return decode_main(args)
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         return reference_arm(args, wl)
@@ -395,6 +544,11 @@ def main():
             "clocks": clocks.summary(),
             "gpu_launches": launches,
         }
+    if args.workload == "c3" and not args.no_decode:
+        dec = decode_bench(args, dev, world, with_e2e=not args.no_e2e)
+        if rank == 0:
+            line["decode"] = dec
+    if rank == 0:
         print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()

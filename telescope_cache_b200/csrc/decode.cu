@@ -3,10 +3,16 @@
 //
 // One CTA per (batch row, KV head) owns that head's slice of every ring, so
 // the ruler-tick merge, the level-0 write and the attention read need no
-// cross-CTA ordering.  Eight warps split the visible entries (about
-// cache_size of them) and keep private online-softmax states that are merged
-// through shared memory at the end.
+// cross-CTA ordering.  The attention read is HBM-bound (every visible K and
+// V row once): for Dk = Dv = 128 and 16-bit rings, half a warp reads one
+// 256-byte row with 16-byte loads, a warp holds 8 entries per group and
+// issues the next group's loads before the current group's math, so each
+// thread keeps 8 row loads in flight.  Other shapes take a generic variant
+// (one entry per warp).  Eight warps keep private online-softmax states that
+// are merged through shared memory at the end.
 #include "common.cuh"
+
+#include <type_traits>
 
 using namespace tc;
 
@@ -19,23 +25,24 @@ struct DecParams {
   float scale;
 };
 
-__device__ __forceinline__ int ring_slot(const tc_decode_args& a, int l, int j) {
-  return a.ring_off[l] + j % a.caps[l];
-}
+template <int DM> struct DecShared {
+  float kt[DM], vt[DM];
+  float qs[MAXE][DM];           // query rows of the group (rotated for rope)
+  float st[MAXE][32];           // relative states of the group
+  float wbuf[NW][DM];           // generic variant: one key per warp for the rotation
+  float part_m[NW][MAXE], part_l[NW][MAXE];
+  float part_acc[NW][MAXE][DM];
+  int lo_s[TC_MAX_LEVELS], hi_s[TC_MAX_LEVELS], base_s[TC_MAX_LEVELS], pre_s[TC_MAX_LEVELS + 1];
+  int roff_s[TC_MAX_LEVELS + 1], caps_s[TC_MAX_LEVELS];
+  float w_new;
+};
 
+// Steps 1-4 of the step (conv, merge weight, ruler-tick merge, level-0
+// write), then the visible ranges of query t and the query rows.  Returns
+// false when the mode does not attend (every thread agrees).
 template <typename T, int DM>
-__global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
+__device__ bool decode_prologue(const DecParams& P, DecShared<DM>& S) {
   const tc_decode_args& a = P.a;
-  constexpr int DC = DM / 32;
-  __shared__ float kt[DM], vt[DM];
-  __shared__ float qs[MAXE][DM];
-  __shared__ float st[MAXE][32];
-  __shared__ float wbuf[NW][DM];
-  __shared__ float part_m[NW][MAXE], part_l[NW][MAXE];
-  __shared__ float part_acc[NW][MAXE][DM];
-  __shared__ int lo_s[TC_MAX_LEVELS], hi_s[TC_MAX_LEVELS], base_s[TC_MAX_LEVELS], pre_s[TC_MAX_LEVELS + 1];
-  __shared__ float w_new;
-
   const int b = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int E = a.Hq / a.Hkv;
@@ -46,6 +53,7 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
   const auto kidx = [&](int slot, int d) { return (((int64_t)b * total + slot) * a.Hkv + h) * a.Dk + d; };
   const auto vidx = [&](int slot, int d) { return (((int64_t)b * total + slot) * a.Hkv + h) * a.Dv + d; };
   const auto widx = [&](int slot) { return ((int64_t)b * total + slot) * a.Hkv + h; };
+  const auto ring_slot = [&](int l, int j) { return a.ring_off[l] + j % a.caps[l]; };
 
   const bool advance = a.mode != TC_DECODE_ATTEND;
   const bool attend = a.mode != TC_DECODE_ADVANCE;
@@ -75,7 +83,7 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
       y = x + acc;
     }
     y = round_to<T>(y);
-    if (isk) kt[dd] = y; else vt[dd] = y;
+    if (isk) S.kt[dd] = y; else S.vt[dd] = y;
     T* nout = static_cast<T*>(isk ? a.k_new : a.v_new);
     if (nout) nout[((int64_t)b * a.Hkv + h) * D + dd] = from_f<T>(y);
   }
@@ -83,12 +91,12 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
   const T* qt = static_cast<const T*>(a.q_t);
   for (int i = tid; i < E * a.Dk; i += NT) {
     const int e = i / a.Dk, d = i - e * a.Dk;
-    qs[e][d] = to_f(qt[((int64_t)b * a.Hq + h * E + e) * a.Dk + d]);
+    S.qs[e][d] = to_f(qt[((int64_t)b * a.Hq + h * E + e) * a.Dk + d]);
   }
   if (a.position_mode == TC_POS_RELATIVE) {
     for (int i = tid; i < E * a.d_rel; i += NT) {
       const int e = i / a.d_rel, r = i - e * a.d_rel;
-      st[e][r] = load_any(a.rel_states, ((int64_t)b * a.Hq + h * E + e) * a.d_rel + r, a.rel_dtype);
+      S.st[e][r] = load_any(a.rel_states, ((int64_t)b * a.Hq + h * E + e) * a.d_rel + r, a.rel_dtype);
     }
   }
   __syncthreads();
@@ -102,7 +110,7 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
       float m = -INFINITY, s = 0.f;
       for (int e = 0; e < E; ++e) {
         float dot = 0.f;
-        for (int d = lane; d < a.Dk; d += 32) dot += qs[e][d] * kt[d];
+        for (int d = lane; d < a.Dk; d += 32) dot += S.qs[e][d] * S.kt[d];
 #pragma unroll
         for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
         dot *= P.scale;
@@ -112,7 +120,7 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
       }
       wv = m + logf(s);
     }
-    if (lane == 0) w_new = round_any(wv, a.w_dtype);
+    if (lane == 0) S.w_new = round_any(wv, a.w_dtype);
   }
 
   // 3. the ruler tick: at most one level >= 1 creates node j at t
@@ -126,7 +134,7 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
   }
   if (fired > 0) {
     const int l = fired;
-    const int c0 = ring_slot(a, l - 1, 2 * jn), c1 = ring_slot(a, l - 1, 2 * jn + 1), par = ring_slot(a, l, jn);
+    const int c0 = ring_slot(l - 1, 2 * jn), c1 = ring_slot(l - 1, 2 * jn + 1), par = ring_slot(l, jn);
     const float w0 = load_any(a.ring_w, widx(c0), a.w_dtype), w1 = load_any(a.ring_w, widx(c1), a.w_dtype);
     const float m = fmaxf(w0, w1);
     const float e0 = expf(w0 - m), e1 = expf(w1 - m);
@@ -140,12 +148,12 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
   __syncthreads();
   // 4. token t at level 0, after the merge (its slot may be a merged child's)
   if (advance) {
-    const int s0 = ring_slot(a, 0, t);
-    for (int d = tid; d < a.Dk; d += NT) rk[kidx(s0, d)] = from_f<T>(kt[d]);
-    for (int d = tid; d < a.Dv; d += NT) rv[vidx(s0, d)] = from_f<T>(vt[d]);
-    if (tid == 0) store_any(a.ring_w, widx(s0), a.w_dtype, w_new);
+    const int s0 = ring_slot(0, t);
+    for (int d = tid; d < a.Dk; d += NT) rk[kidx(s0, d)] = from_f<T>(S.kt[d]);
+    for (int d = tid; d < a.Dv; d += NT) rv[vidx(s0, d)] = from_f<T>(S.vt[d]);
+    if (tid == 0) store_any(a.ring_w, widx(s0), a.w_dtype, S.w_new);
   }
-  if (!attend) return;
+  if (!attend) return false;
   // visible ranges of query t and the rotated query rows
   if (tid == 0) {
     int lo[TC_MAX_LEVELS], hi[TC_MAX_LEVELS];
@@ -155,13 +163,16 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
       if (lo[l] >= hi[l]) lo[l] = hi[l] = 0;
     }
     for (int l = 0; l < a.num_levels; ++l) {
-      lo_s[l] = lo[l];
-      hi_s[l] = hi[l];
-      base_s[l] = bin_base(l, lo, hi);
-      pre_s[l] = acc;
+      S.lo_s[l] = lo[l];
+      S.hi_s[l] = hi[l];
+      S.base_s[l] = bin_base(l, lo, hi);
+      S.pre_s[l] = acc;
+      S.roff_s[l] = a.ring_off[l];
+      S.caps_s[l] = a.caps[l];
       acc += hi[l] - lo[l];
     }
-    pre_s[a.num_levels] = acc;
+    S.pre_s[a.num_levels] = acc;
+    S.roff_s[a.num_levels] = a.ring_off[a.num_levels];
   }
   __syncthreads();
   if (a.position_mode == TC_POS_ROPE) {
@@ -172,100 +183,34 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
       const int e = i / a.Dk, d = i - e * a.Dk;
       const int ii = d < hd ? d : d - hd;
       const float c = a.rope_cos[(int64_t)t * hd + ii], s = a.rope_sin[(int64_t)t * hd + ii];
-      const float x1 = qs[e][ii], x2 = qs[e][ii + hd];
+      const float x1 = S.qs[e][ii], x2 = S.qs[e][ii + hd];
       rq[cnt] = round_to<T>(d < hd ? x1 * c - x2 * s : x2 * c + x1 * s);
     }
     __syncthreads();
     cnt = 0;
-    for (int i = tid; i < E * a.Dk; i += NT, ++cnt) qs[i / a.Dk][i % a.Dk] = rq[cnt];
+    for (int i = tid; i < E * a.Dk; i += NT, ++cnt) S.qs[i / a.Dk][i % a.Dk] = rq[cnt];
   }
   __syncthreads();
+  return true;
+}
 
-  // 5. attention over the visible entries; warp w takes entries w, w+NW, ...
-  const int M = pre_s[a.num_levels];
-  float m_e[MAXE], l_e[MAXE], acc[MAXE][DC];
-#pragma unroll
-  for (int e = 0; e < MAXE; ++e) {
-    m_e[e] = -INFINITY;
-    l_e[e] = 0.f;
-#pragma unroll
-    for (int i = 0; i < DC; ++i) acc[e][i] = 0.f;
-  }
-  int lev = 0;
-  for (int idx = warp; idx < M; idx += NW) {
-    while (idx >= pre_s[lev + 1]) ++lev;
-    const int j = lo_s[lev] + (idx - pre_s[lev]);
-    const int slot = ring_slot(a, lev, j);
-    float kv[DC], vv[DC];
-#pragma unroll
-    for (int i = 0; i < DC; ++i) {
-      const int d = lane + 32 * i;
-      kv[i] = d < a.Dk ? to_f(rk[kidx(slot, d)]) : 0.f;
-      vv[i] = d < a.Dv ? to_f(rv[vidx(slot, d)]) : 0.f;
-    }
-    if (a.position_mode == TC_POS_ROPE) {
-      // rotate the key at its summary position (j + 1) 2^l - 1, via the warp buffer
-#pragma unroll
-      for (int i = 0; i < DC; ++i) wbuf[warp][lane + 32 * i] = kv[i];
-      __syncwarp();
-      const int pos = ((j + 1) << lev) - 1;
-      const int hd = a.Dk / 2;
-#pragma unroll
-      for (int i = 0; i < DC; ++i) {
-        const int d = lane + 32 * i;
-        if (d < a.Dk) {
-          const int ii = d < hd ? d : d - hd;
-          const float c = a.rope_cos[(int64_t)pos * hd + ii], s = a.rope_sin[(int64_t)pos * hd + ii];
-          const float x1 = wbuf[warp][ii], x2 = wbuf[warp][ii + hd];
-          kv[i] = round_to<T>(d < hd ? x1 * c - x2 * s : x2 * c + x1 * s);
-        }
-      }
-      __syncwarp();
-    }
-    const int dist = base_s[lev] - j;
-    for (int e = 0; e < E; ++e) {
-      float part = 0.f;
-#pragma unroll
-      for (int i = 0; i < DC; ++i) part += qs[e][lane + 32 * i] * kv[i];
-#pragma unroll
-      for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-      float x = part * P.scale;
-      if (a.position_mode == TC_POS_RELATIVE) {
-        float bsum = lane < a.d_rel ? st[e][lane] * load_any(a.rel_proj, (int64_t)lane * a.rel_bins + dist, a.rel_dtype) : 0.f;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
-        x += bsum;
-      }
-      if (a.has_softcap) x = a.softcap * tanhf(x / a.softcap);
-      const float mn = fmaxf(m_e[e], x);
-      const float corr = expf(m_e[e] - mn);
-      const float pv = expf(x - mn);
-      l_e[e] = l_e[e] * corr + pv;
-#pragma unroll
-      for (int i = 0; i < DC; ++i) acc[e][i] = acc[e][i] * corr + pv * vv[i];
-      m_e[e] = mn;
-    }
-  }
-  // 6. merge the warps' partial softmax states
-  for (int e = 0; e < E; ++e) {
-    if (lane == 0) {
-      part_m[warp][e] = m_e[e];
-      part_l[warp][e] = l_e[e];
-    }
-#pragma unroll
-    for (int i = 0; i < DC; ++i) part_acc[warp][e][lane + 32 * i] = acc[e][i];
-  }
-  __syncthreads();
+// Merge the warps' partial softmax states (part_m / part_l / part_acc), then
+// the sink, the gate and the stores of out and the pre-sink lse.
+template <typename T, int DM>
+__device__ void decode_epilogue(const DecParams& P, DecShared<DM>& S) {
+  const tc_decode_args& a = P.a;
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int E = a.Hq / a.Hkv;
   T* out = static_cast<T*>(a.out);
-  for (int i = tid; i < E * a.Dv; i += NT) {
+  for (int i = threadIdx.x; i < E * a.Dv; i += NT) {
     const int e = i / a.Dv, d = i - e * a.Dv;
     float mx = -INFINITY;
-    for (int w = 0; w < NW; ++w) mx = fmaxf(mx, part_m[w][e]);
+    for (int w = 0; w < NW; ++w) mx = fmaxf(mx, S.part_m[w][e]);
     float ls = 0.f, o = 0.f;
     for (int w = 0; w < NW; ++w) {
-      const float f = part_m[w][e] == -INFINITY ? 0.f : expf(part_m[w][e] - mx);
-      ls += part_l[w][e] * f;
-      o += part_acc[w][e][d] * f;
+      const float f = S.part_m[w][e] == -INFINITY ? 0.f : expf(S.part_m[w][e] - mx);
+      ls += S.part_l[w][e] * f;
+      o += S.part_acc[w][e][d] * f;
     }
     const int hq = h * E + e;
     float y = round_to<T>(o / ls);
@@ -281,6 +226,352 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
     out[((int64_t)b * a.Hq + hq) * a.Dv + d] = from_f<T>(y);
     if (d == 0) a.lse[(int64_t)b * a.Hq + hq] = lse;
   }
+}
+
+// Generic variant: any Dk, Dv <= DM, any element type; warp w takes entries
+// w, w + NW, ... one at a time.
+template <typename T, int DM>
+__global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
+  __shared__ DecShared<DM> S;
+  if (!decode_prologue<T, DM>(P, S)) return;
+  const tc_decode_args& a = P.a;
+  constexpr int DC = DM / 32;
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = a.Hq / a.Hkv;
+  const int total = S.roff_s[a.num_levels];
+  const T* rk = static_cast<const T*>(a.ring_k);
+  const T* rv = static_cast<const T*>(a.ring_v);
+  const auto kidx = [&](int slot, int d) { return (((int64_t)b * total + slot) * a.Hkv + h) * a.Dk + d; };
+  const auto vidx = [&](int slot, int d) { return (((int64_t)b * total + slot) * a.Hkv + h) * a.Dv + d; };
+
+  const int M = S.pre_s[a.num_levels];
+  float m_e[MAXE], l_e[MAXE], acc[MAXE][DC];
+#pragma unroll
+  for (int e = 0; e < MAXE; ++e) {
+    m_e[e] = -INFINITY;
+    l_e[e] = 0.f;
+#pragma unroll
+    for (int i = 0; i < DC; ++i) acc[e][i] = 0.f;
+  }
+  int lev = 0;
+  for (int idx = warp; idx < M; idx += NW) {
+    while (idx >= S.pre_s[lev + 1]) ++lev;
+    const int j = S.lo_s[lev] + (idx - S.pre_s[lev]);
+    const int slot = S.roff_s[lev] + j % S.caps_s[lev];
+    float kv[DC], vv[DC];
+#pragma unroll
+    for (int i = 0; i < DC; ++i) {
+      const int d = lane + 32 * i;
+      kv[i] = d < a.Dk ? to_f(rk[kidx(slot, d)]) : 0.f;
+      vv[i] = d < a.Dv ? to_f(rv[vidx(slot, d)]) : 0.f;
+    }
+    if (a.position_mode == TC_POS_ROPE) {
+      // rotate the key at its summary position (j + 1) 2^l - 1, via the warp buffer
+#pragma unroll
+      for (int i = 0; i < DC; ++i) S.wbuf[warp][lane + 32 * i] = kv[i];
+      __syncwarp();
+      const int pos = ((j + 1) << lev) - 1;
+      const int hd = a.Dk / 2;
+#pragma unroll
+      for (int i = 0; i < DC; ++i) {
+        const int d = lane + 32 * i;
+        if (d < a.Dk) {
+          const int ii = d < hd ? d : d - hd;
+          const float c = a.rope_cos[(int64_t)pos * hd + ii], s = a.rope_sin[(int64_t)pos * hd + ii];
+          const float x1 = S.wbuf[warp][ii], x2 = S.wbuf[warp][ii + hd];
+          kv[i] = round_to<T>(d < hd ? x1 * c - x2 * s : x2 * c + x1 * s);
+        }
+      }
+      __syncwarp();
+    }
+    const int dist = S.base_s[lev] - j;
+    for (int e = 0; e < E; ++e) {
+      float part = 0.f;
+#pragma unroll
+      for (int i = 0; i < DC; ++i) part += S.qs[e][lane + 32 * i] * kv[i];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      float x = part * P.scale;
+      if (a.position_mode == TC_POS_RELATIVE) {
+        float bsum = lane < a.d_rel ? S.st[e][lane] * load_any(a.rel_proj, (int64_t)lane * a.rel_bins + dist, a.rel_dtype) : 0.f;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
+        x += bsum;
+      }
+      if (a.has_softcap) x = a.softcap * tanhf(x / a.softcap);
+      const float mn = fmaxf(m_e[e], x);
+      const float corr = expf(m_e[e] - mn);
+      const float pv = expf(x - mn);
+      l_e[e] = l_e[e] * corr + pv;
+#pragma unroll
+      for (int i = 0; i < DC; ++i) acc[e][i] = acc[e][i] * corr + pv * vv[i];
+      m_e[e] = mn;
+    }
+  }
+  for (int e = 0; e < E; ++e) {
+    if (lane == 0) {
+      S.part_m[warp][e] = m_e[e];
+      S.part_l[warp][e] = l_e[e];
+    }
+#pragma unroll
+    for (int i = 0; i < DC; ++i) S.part_acc[warp][e][lane + 32 * i] = acc[e][i];
+  }
+  __syncthreads();
+  decode_epilogue<T, DM>(P, S);
+}
+
+// Two fp32 lanes per instruction (sm_100 f32x2 FMA / MUL).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+        "l"(*reinterpret_cast<uint64_t*>(&c)));
+  return *reinterpret_cast<float2*>(&d);
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
+  return *reinterpret_cast<float2*>(&d);
+}
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// A 32-bit word of two 16-bit elements (low first) as floats.
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t u) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+  } else {
+    return __half22float2(*reinterpret_cast<const __half2*>(&u));
+  }
+}
+// Round a pair to T and back (the reference stores the rotated key in T).
+template <typename T>
+__device__ __forceinline__ float2 round2(float2 v) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    __nv_bfloat162 r = __floats2bfloat162_rn(v.x, v.y);
+    return unpack2<T>(*reinterpret_cast<uint32_t*>(&r));
+  } else {
+    return __half22float2(__floats2half2_rn(v.x, v.y));
+  }
+}
+
+__device__ __forceinline__ uint4 shfl_xor4(const uint4& v, int m) {
+  return make_uint4(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m),
+                    __shfl_xor_sync(0xffffffffu, v.z, m), __shfl_xor_sync(0xffffffffu, v.w, m));
+}
+
+// Dk = Dv = 128, 16-bit rings, E query heads per KV head.  Group g0 covers
+// entries g0 .. g0 + 63; lane (half, l16) of warp w holds dims 8*l16 .. +7 of
+// entries g0 + 8w + 2i + half, i = 0..3.  Logits are kept in log2 units
+// (exp2 / tanh instructions); the partial maxima go to the epilogue in
+// natural units.
+template <typename T, int E>
+__global__ void __launch_bounds__(NT) decode_kernel128(DecParams P) {
+  __shared__ DecShared<128> S;
+  __shared__ int r0_s[TC_MAX_LEVELS];  // lo % cap: ring position of each level's first visible node
+  if (!decode_prologue<T, 128>(P, S)) return;
+  const tc_decode_args& a = P.a;
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = lane >> 4, l16 = lane & 15;
+  const int nl = a.num_levels;
+  if (threadIdx.x < nl) r0_s[threadIdx.x] = S.lo_s[threadIdx.x] % S.caps_s[threadIdx.x];
+  __syncthreads();
+  const int total = S.roff_s[nl];
+  const uint4* rk = static_cast<const uint4*>(a.ring_k);
+  const uint4* rv = static_cast<const uint4*>(a.ring_v);
+  const int64_t row0 = (int64_t)b * total * a.Hkv + h;  // row of (b, slot, h) = row0 + slot * Hkv
+  const bool rope = a.position_mode == TC_POS_ROPE, rel = a.position_mode == TC_POS_RELATIVE;
+  const bool cap = a.has_softcap;
+  constexpr float kLog2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
+  // logit2 = cap log2e tanh((dot scale + bias) / cap), or (dot scale + bias) log2e
+  const float k_in = cap ? P.scale / a.softcap : P.scale * kLog2e;
+  const float k_bias = cap ? 1.f / a.softcap : kLog2e;
+  const float k_out = a.softcap * kLog2e;
+  // rotate-half: dims below 64 take -partner * sin, the others +partner * sin
+  const uint32_t sgn = l16 < 8 ? 0x80008000u : 0u;
+
+  float2 q[E][4];
+#pragma unroll
+  for (int e = 0; e < E; ++e)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[e][i] = make_float2(S.qs[e][l16 * 8 + 2 * i], S.qs[e][l16 * 8 + 2 * i + 1]);
+  float m[E], l[E];
+  float2 acc[E][4];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    m[e] = -INFINITY;
+    l[e] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[e][i] = make_float2(0.f, 0.f);
+  }
+  const int M = S.pre_s[nl];
+  int lev = 0;  // entries of a lane only move forward through the levels
+  uint4 kn[4], vn[4];
+  int jn[4], ln[4];
+  auto fetch = [&](int g0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = g0 + warp * 8 + 2 * i + half;
+      jn[i] = -1;
+      ln[i] = 0;
+      kn[i] = vn[i] = make_uint4(0u, 0u, 0u, 0u);
+      if (idx < M) {
+        while (idx >= S.pre_s[lev + 1]) ++lev;
+        // slot = off + j % cap with j = lo + d and d < cap: one conditional subtract
+        const int d = idx - S.pre_s[lev], cp = S.caps_s[lev];
+        const int rr = r0_s[lev] + d;
+        const int64_t row = row0 + (int64_t)(S.roff_s[lev] + (rr >= cp ? rr - cp : rr)) * a.Hkv;
+        kn[i] = __ldg(rk + row * 16 + l16);
+        vn[i] = __ldg(rv + row * 16 + l16);
+        jn[i] = S.lo_s[lev] + d;
+        ln[i] = lev;
+      }
+    }
+  };
+  if (M > 0) fetch(0);
+  for (int g0 = 0; g0 < M; g0 += 64) {
+    uint4 kc[4], vc[4];
+    int jc[4], lc[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      kc[i] = kn[i];
+      vc[i] = vn[i];
+      jc[i] = jn[i];
+      lc[i] = ln[i];
+    }
+    if (g0 + 64 < M) fetch(g0 + 64);  // next group's rows in flight during this group's math
+    float x[E][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const bool ok = jc[i] >= 0;
+      const uint32_t kw[4] = {kc[i].x, kc[i].y, kc[i].z, kc[i].w};
+      float2 kf[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) kf[c] = unpack2<T>(kw[c]);
+      if (rope) {
+        // dims d and d + 64 sit in lanes l16 and l16 ^ 8 of the same half
+        const uint4 pk = shfl_xor4(kc[i], 8);
+        const uint32_t pw[4] = {pk.x ^ sgn, pk.y ^ sgn, pk.z ^ sgn, pk.w ^ sgn};
+        const int pos = ok ? ((jc[i] + 1) << lc[i]) - 1 : 0;
+        const float4* cr = reinterpret_cast<const float4*>(a.rope_cos + (int64_t)pos * 64 + (l16 & 7) * 8);
+        const float4* sr = reinterpret_cast<const float4*>(a.rope_sin + (int64_t)pos * 64 + (l16 & 7) * 8);
+        const float4 c0 = __ldg(cr), c1 = __ldg(cr + 1), s0 = __ldg(sr), s1 = __ldg(sr + 1);
+        const float2 cs[4] = {make_float2(c0.x, c0.y), make_float2(c0.z, c0.w), make_float2(c1.x, c1.y),
+                              make_float2(c1.z, c1.w)};
+        const float2 sn[4] = {make_float2(s0.x, s0.y), make_float2(s0.z, s0.w), make_float2(s1.x, s1.y),
+                              make_float2(s1.z, s1.w)};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) kf[c] = round2<T>(ffma2(unpack2<T>(pw[c]), sn[c], fmul2(kf[c], cs[c])));
+      }
+      float pr0 = 0.f, pr1 = 0.f;  // relative: proj[r, dist] for r = l16, l16 + 16
+      if (rel && ok) {
+        const int dist = S.base_s[lc[i]] - jc[i];
+        if (l16 < a.d_rel) pr0 = load_any(a.rel_proj, (int64_t)l16 * a.rel_bins + dist, a.rel_dtype);
+        if (l16 + 16 < a.d_rel) pr1 = load_any(a.rel_proj, (int64_t)(l16 + 16) * a.rel_bins + dist, a.rel_dtype);
+      }
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        float2 d2 = fmul2(q[e][0], kf[0]);
+#pragma unroll
+        for (int c = 1; c < 4; ++c) d2 = ffma2(q[e][c], kf[c], d2);
+        float dot = d2.x + d2.y;
+#pragma unroll
+        for (int o = 8; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        float bias = 0.f;
+        if (rel) {
+          bias = (l16 < a.d_rel ? S.st[e][l16] * pr0 : 0.f) + (l16 + 16 < a.d_rel ? S.st[e][l16 + 16] * pr1 : 0.f);
+#pragma unroll
+          for (int o = 8; o; o >>= 1) bias += __shfl_xor_sync(0xffffffffu, bias, o);
+        }
+        float y = fmaf(dot, k_in, bias * k_bias);
+        if (cap) y = tanh_approx(y) * k_out;
+        x[e][i] = ok ? y : -INFINITY;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      float gm = fmaxf(fmaxf(x[e][0], x[e][1]), fmaxf(x[e][2], x[e][3]));
+      gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 16));
+      const float mn = fmaxf(m[e], gm);
+      if (mn == -INFINITY) continue;  // warp-uniform: no visible entry yet
+      const float corr = ex2_approx(m[e] - mn);
+      const float2 c2 = make_float2(corr, corr);
+      float p[4], ps = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        p[i] = ex2_approx(x[e][i] - mn);
+        ps += p[i];
+      }
+      l[e] = fmaf(l[e], corr, ps);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[e][c] = fmul2(acc[e][c], c2);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t vw[4] = {vc[i].x, vc[i].y, vc[i].z, vc[i].w};
+        const float2 p2 = make_float2(p[i], p[i]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[e][c] = ffma2(p2, unpack2<T>(vw[c]), acc[e][c]);
+      }
+      m[e] = mn;
+    }
+  }
+  // the two halves hold different entries of the same dims: add them
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    l[e] += __shfl_xor_sync(0xffffffffu, l[e], 16);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      acc[e][c].x += __shfl_xor_sync(0xffffffffu, acc[e][c].x, 16);
+      acc[e][c].y += __shfl_xor_sync(0xffffffffu, acc[e][c].y, 16);
+    }
+    if (lane == 0) {
+      S.part_m[warp][e] = m[e] * kLn2;
+      S.part_l[warp][e] = l[e];
+    }
+    if (half == 0) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        S.part_acc[warp][e][l16 * 8 + 2 * c] = acc[e][c].x;
+        S.part_acc[warp][e][l16 * 8 + 2 * c + 1] = acc[e][c].y;
+      }
+    }
+  }
+  __syncthreads();
+  decode_epilogue<T, 128>(P, S);
+}
+
+template <typename T>
+int launch_decode(const DecParams& P, int E, int d, dim3 grid, cudaStream_t st) {
+  if constexpr (sizeof(T) == 2) {
+    if (P.a.Dk == 128 && P.a.Dv == 128) {
+      switch (E) {
+        case 1: decode_kernel128<T, 1><<<grid, NT, 0, st>>>(P); return launch_status();
+        case 2: decode_kernel128<T, 2><<<grid, NT, 0, st>>>(P); return launch_status();
+        case 4: decode_kernel128<T, 4><<<grid, NT, 0, st>>>(P); return launch_status();
+        case 8: decode_kernel128<T, 8><<<grid, NT, 0, st>>>(P); return launch_status();
+        default: break;
+      }
+    }
+  }
+  if (d <= 32) decode_kernel<T, 32><<<grid, NT, 0, st>>>(P);
+  else if (d <= 64) decode_kernel<T, 64><<<grid, NT, 0, st>>>(P);
+  else if (d <= 128) decode_kernel<T, 128><<<grid, NT, 0, st>>>(P);
+  else return TC_ERR_UNSUPPORTED;
+  return launch_status();
 }
 
 }  // namespace
@@ -307,11 +598,6 @@ extern "C" int tc_decode_step(const tc_decode_args* a, void* stream) {
   const int d = a->Dk > a->Dv ? a->Dk : a->Dv;
   dim3 grid(a->B, a->Hkv);
   cudaStream_t st = (cudaStream_t)stream;
-  TC_DISPATCH(a->dtype, T, {
-    if (d <= 32) decode_kernel<T, 32><<<grid, NT, 0, st>>>(P);
-    else if (d <= 64) decode_kernel<T, 64><<<grid, NT, 0, st>>>(P);
-    else if (d <= 128) decode_kernel<T, 128><<<grid, NT, 0, st>>>(P);
-    else return TC_ERR_UNSUPPORTED;
-  });
-  return launch_status();
+  TC_DISPATCH(a->dtype, T, { return launch_decode<T>(P, E, d, grid, st); });
+  return TC_ERR_ARG;
 }

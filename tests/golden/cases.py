@@ -24,6 +24,13 @@ GEOS = {
     # head dim 128, GQA 2:1, four levels all live inside N
     "d128": dict(B=1, N=512, Hq=2, Hkv=1, Dk=128, Dv=128,
                  fmap={1: 64, 2: 128, 3: 192}, cache=256),
+    # head dim 128 with 1, 4 and 8 query heads per KV head (decode variants)
+    "d128_mha": dict(B=2, N=512, Hq=2, Hkv=2, Dk=128, Dv=128,
+                     fmap={1: 64, 2: 128, 3: 192}, cache=256),
+    "d128_gqa4": dict(B=1, N=512, Hq=4, Hkv=1, Dk=128, Dv=128,
+                      fmap={1: 64, 2: 128, 3: 192}, cache=256),
+    "d128_gqa8": dict(B=1, N=512, Hq=8, Hkv=1, Dk=128, Dv=128,
+                      fmap={1: 64, 2: 128, 3: 192}, cache=256),
 }
 
 EMB, D_REL = 32, 6
@@ -109,6 +116,14 @@ CASES = [
     case("dec_full_tiny", "decode", "tiny", weights="linear", conv=4, sink=True, gate=True,
          tail=7, seed=509),
     case("dec_nocap_tiny", "decode", "tiny", softcap=None, tail=3, seed=510),
+    # head dim 128, 16-bit rings (the vectorised decode kernel), E = 1, 2, 4, 8
+    case("dec_rope_d128_bf16", "decode", "d128_mha", dtype="bf16", weights="linear", conv=4,
+         position="rope", sink=True, gate=True, tail=40, seed=511),
+    case("dec_rel_d128_bf16", "decode", "d128", dtype="bf16", position="relative", sink=True,
+         softcap=50.0, tail=24, seed=512),
+    case("dec_plain_gqa4_bf16", "decode", "d128_gqa4", dtype="bf16", conv=4, tail=20, seed=513),
+    case("dec_nocap_gqa8_bf16", "decode", "d128_gqa8", dtype="bf16", position="rope",
+         softcap=None, tail=16, seed=514),
 ]
 
 CASE_BY_NAME = {c["name"]: c for c in CASES}
