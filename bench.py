@@ -61,6 +61,13 @@ DECODE = dict(B=64, T=32768, H=16, D=128, levels=8, W=256, conv=4, softcap=20.0,
                    "sink, gate")
 
 
+# DRAM bytes per launch of the dominant op (the backward: Pass A + Pass B), from
+# the ncu capture of the c3_small case (profiles/attn_kernels_c3_small_full.txt)
+# scaled by the 16x (batch, head) units of config 3; traffic is proportional to
+# the units.  None where no capture covers the workload.
+TRAFFIC = {"c3": 16 * (0.416797e9 + 1.037636e9 + 0.409435e9 + 0.060640e9)}
+
+
 def schedule(wl):
     fmap = {l: l * wl["W"] for l in range(1, wl["levels"])}
     return fmap, wl["levels"] * wl["W"]
@@ -517,7 +524,9 @@ def main():
     achieved = dom[1] / (dom[2] * 1e-3) / 1e12
     roofline = {"bound": "tensor", "kernel": f"attention {dom[0]}", "achieved": achieved,
                 "peak": sustained, "peak_source": f"{src} bf16_tflops_sustained", "unit": "TFLOP/s",
-                "frac": achieved / sustained, "traffic": None,
+                "frac": achieved / sustained, "traffic": TRAFFIC.get(args.workload),
+                "traffic_note": "DRAM bytes per backward (Pass A + Pass B), ncu c3_small x16"
+                if args.workload in TRAFFIC else None,
                 "forward_tflops": fwd_flops / (fms * 1e-3) / 1e12,
                 "backward_tflops": bwd_flops / (bms * 1e-3) / 1e12,
                 "forward_ms": fms, "backward_ms": bms}
