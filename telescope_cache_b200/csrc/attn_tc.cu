@@ -7,10 +7,13 @@
 //   warp 0      TMA producer: Q once, then K/V tiles into an NS-stage ring
 //   warp 1      MMA issuer:   S_j = Q K_j^T into TMEM (double buffered),
 //                             O += P_{j-1} V_{j-1} (P from shared memory)
-//   warps 4..7  softmax:      one thread per query row (= TMEM lane):
-//                             exact per-row level mask, relative bias,
-//                             softcap, online softmax in log2 units with lazy
-//                             O rescaling, P -> shared memory, final O / l.
+//   warps 2, 3  relative bias staging: bulk copies of each row's bias run
+//   warps 4..11 softmax:      two threads per query row (= TMEM lane), each
+//                             with half of the tile's columns: exact per-row
+//                             level mask, relative bias, softcap, online
+//                             softmax in log2 units with lazy O rescaling (the
+//                             row maximum is exchanged through shared memory),
+//                             P -> shared memory, final O / l.
 // Every mbarrier wait is bounded (see tc_ptx.cuh); a timeout sets
 // TC_DEV_WAIT_TIMEOUT in the device status word and the CTA drains.
 #include "tc_common.cuh"
@@ -33,7 +36,8 @@ template <int BK> struct FwdShape {
   static constexpr int PTILE = 128 * BK * 2;          // P tile [128 x BK]
   static constexpr int TMEM_COLS = BK == 64 ? 256 : 512;
   static constexpr int O_COL = 2 * BK;
-  static constexpr int SMEM = QTILE + 2 * NS * KVTILE + PTILE + 1024 + 256;
+  // + 1024 alignment slack, 256 barriers, 3 x 256 row-maximum / row-sum exchange
+  static constexpr int SMEM = QTILE + 2 * NS * KVTILE + PTILE + 1024 + 256 + 3 * 256 * 4;
 };
 
 struct TcParams {
@@ -50,7 +54,7 @@ struct TcParams {
 };
 
 template <typename T, int BK, bool REL>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, TcParams p) {
   using Sh = FwdShape<BK>;
@@ -71,9 +75,12 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* o_done = p_full + 1;
   uint64_t* run_full = o_done + 1;   // relative: staged bias runs ready (warps 2-3)
   uint64_t* run_empty = run_full + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(run_empty + 2);
+  uint64_t* xch = run_empty + 2;     // [2] row-maximum exchange, [2] final row sum
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xch + 3);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  uint16_t* run_s = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [2][128][72]
+  float* xs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [3][2][128]
+  uint16_t* run_s = reinterpret_cast<uint16_t*>(xs + 3 * 256);                   // [2][128][72]
+  uint8_t* sh_s = reinterpret_cast<uint8_t*>(run_s + 2 * 128 * kRunStride);      // [2][128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * BQ, hq = blockIdx.y, b = blockIdx.z;
@@ -88,11 +95,12 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
+      mbar_init(&s_free[i], kComputeThreads);
       mbar_init(&run_full[i], 64);
-      mbar_init(&run_empty[i], 128);
+      mbar_init(&run_empty[i], kComputeThreads);
     }
-    mbar_init(p_full, 128);
+    for (int i = 0; i < 3; ++i) mbar_init(&xch[i], kComputeThreads);
+    mbar_init(p_full, kComputeThreads);
     mbar_init(o_done, 1);
     *abort_flag = 0;
     mbar_fence_init();
@@ -182,14 +190,16 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp < 4) {
     // ---------------- relative bias staging (warps 2, 3) ----------------
     if constexpr (REL)
-      stage_runs(threadIdx.x - 64, q0, q1, p.N, p.Hq, hq, b, p.s, p.rl, p.rl_stride, p.rl_pad, run_s, run_full,
-                 run_empty, abort_flag, status);
+      stage_runs(threadIdx.x - 64, q0, q1, p.N, p.Hq, hq, b, p.s, p.rl, p.rl_stride, p.rl_pad, run_s, sh_s,
+                 run_full, run_empty, abort_flag, status);
   } else {
-    // ---------------- softmax / epilogue: one query row per thread ----------------
-    const int r = threadIdx.x - 128;
+    // ---------------- softmax / epilogue: two threads per query row ----------------
+    constexpr int HC = BK / 2;  // columns per thread: [HC ch, HC ch + HC) of each tile
+    const int r = (threadIdx.x - 128) & 127;
+    const int ch = (threadIdx.x - 128) >> 7;
     const int q = q0 + r;
     const bool row_ok = q < p.N;
-    const uint32_t lane_base = (uint32_t)((warp - 4) * 32) << 16;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     // logit2 = (S * scale + bias) * log2(e), softcapped: cap * tanh(. / cap) * log2(e)
     const float kq = p.has_cap ? p.scale / p.cap : p.scale * kLog2e;
     const float kb = p.has_cap ? 1.f / p.cap : kLog2e;
@@ -200,7 +210,7 @@ __global__ void __launch_bounds__(256, 1)
     bool ok = it.start(p.s);
     int j = 0;
     bool alive = true;
-    float sv[BK];
+    float sv[HC];
     for (; ok; ++j, ok = it.advance(p.s)) {
       if (it.lev != cur) {
         cur = it.lev;
@@ -215,40 +225,33 @@ __global__ void __launch_bounds__(256, 1)
       if (!alive) break;
       tc_fence_after();
 #pragma unroll
-      for (int c4 = 0; c4 < BK / 32; ++c4) tmem_ld32(tmem + lane_base + bb * BK + c4 * 32, sv + 32 * c4);
+      for (int c4 = 0; c4 < HC / 32; ++c4) tmem_ld32(tmem + lane_base + bb * BK + ch * HC + c4 * 32, sv + 32 * c4);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[bb]);
-      const int jlo = lo - it.k0, jhi = hi - it.k0;
-      const bool interior = jlo <= 0 && jhi >= BK;  // every column visible: no mask
+      const int jlo = lo - it.k0 - ch * HC, jhi = hi - it.k0 - ch * HC;  // this thread's columns
+      const bool interior = jlo <= 0 && jhi >= HC;  // every column visible: no mask
       float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if constexpr (REL) {
         static_assert(!REL || BK == 64, "the relative bias path uses 64-node tiles");
-        // columns c see bin distance base - k0 - c: staged run element 63 - c
+        // column c = 32 ch + cl sees bin distance base - k0 - c: run element
+        // 63 - c = element 31 - cl of this thread's 32-element window
         alive = __all_sync(0xffffffffu, mbar_wait(&run_full[bb], (j >> 1) & 1, abort_flag, status));
         if (!alive) break;
-        // 8 columns per 16-byte read: columns 8*c8 .. 8*c8+7 use elements
-        // 63-8*c8 .. 56-8*c8, i.e. vector 7-c8 read back to front.
-        const uint4* runp = reinterpret_cast<const uint4*>(run_s + bb * 128 * kRunStride + r * kRunStride);
-#pragma unroll
-        for (int c8 = 0; c8 < BK / 8; ++c8) {
-          const uint4 v = runp[7 - c8];
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int c = c8 * 8 + i, e = 7 - i;
-            const uint16_t h = (e & 1) ? (uint16_t)(w[e >> 1] >> 16) : (uint16_t)(w[e >> 1] & 0xffffu);
-            float x = fmaf(sv[c], kq, bits_to_float<T>(h) * kb);
-            if (p.has_cap) x = tanh_fast(x) * kc;
-            if (!interior) x = (c >= jlo && c < jhi) ? x : -INFINITY;
-            sv[c] = x;
-            mxp[c & 3] = fmaxf(mxp[c & 3], x);
-          }
-        }
+        uint32_t run[16];
+        load_run32(run_s + (bb * 128 + r) * kRunStride, sh_s[bb * 128 + r], ch, run);
         mbar_arrive(&run_empty[bb]);
+#pragma unroll
+        for (int c = 0; c < HC; ++c) {
+          float x = fmaf(sv[c], kq, run_elem<T>(run, 31 - c) * kb);
+          if (p.has_cap) x = tanh_fast(x) * kc;
+          if (!interior) x = (c >= jlo && c < jhi) ? x : -INFINITY;
+          sv[c] = x;
+          mxp[c & 3] = fmaxf(mxp[c & 3], x);
+        }
       } else {
 #pragma unroll
-        for (int c = 0; c < BK; ++c) {
+        for (int c = 0; c < HC; ++c) {
           float x = sv[c] * kq;
           if (p.has_cap) x = tanh_fast(x) * kc;
           if (!interior) x = (c >= jlo && c < jhi) ? x : -INFINITY;
@@ -256,7 +259,12 @@ __global__ void __launch_bounds__(256, 1)
           mxp[c & 3] = fmaxf(mxp[c & 3], x);
         }
       }
-      const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
+      // row maximum over both halves (bounded wait on the exchange barrier)
+      xs[bb * 256 + ch * 128 + r] = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
+      mbar_arrive(&xch[bb]);
+      alive = __all_sync(0xffffffffu, mbar_wait(&xch[bb], (j >> 1) & 1, abort_flag, status));
+      if (!alive) break;
+      const float mx = fmaxf(xs[bb * 256 + r], xs[bb * 256 + 128 + r]);
       bool rescale = false;
       float alpha = 1.f;
       if (mx > -INFINITY) {
@@ -277,29 +285,29 @@ __global__ void __launch_bounds__(256, 1)
         tc_fence_after();
         float ov[32];
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          tmem_ld32(tmem + lane_base + Sh::O_COL + c4 * 32, ov);
+        for (int c4 = 0; c4 < 2; ++c4) {
+          const uint32_t oa = tmem + lane_base + Sh::O_COL + ch * 64 + c4 * 32;
+          tmem_ld32(oa, ov);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-          tmem_st32(tmem + lane_base + Sh::O_COL + c4 * 32, ov);
+          tmem_st32(oa, ov);
         }
         tmem_wait_st();
       }
       float sp[4] = {0.f, 0.f, 0.f, 0.f};
       const bool live = m_used > -INFINITY;
 #pragma unroll
-      for (int c8 = 0; c8 < BK / 8; ++c8) {
+      for (int c8 = 0; c8 < HC / 8; ++c8) {
         float pv[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           pv[i] = live ? exp2_fast(sv[c8 * 8 + i] - m_used) : 0.f;
           sp[i & 3] += pv[i];
         }
-        *reinterpret_cast<uint4*>(p_s + sw128_offset(r, c8 * 8, 128)) = pack8<T>(pv, 1.f);
+        *reinterpret_cast<uint4*>(p_s + sw128_offset(r, ch * HC + c8 * 8, 128)) = pack8<T>(pv, 1.f);
       }
-      const float sum = (sp[0] + sp[1]) + (sp[2] + sp[3]);
-      ell += sum;
+      ell += (sp[0] + sp[1]) + (sp[2] + sp[3]);
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
@@ -308,20 +316,27 @@ __global__ void __launch_bounds__(256, 1)
       alive = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, abort_flag, status));
     }
     if (alive && j >= 1) {
+      // the row sum of both halves
+      xs[2 * 256 + ch * 128 + r] = ell;
+      mbar_arrive(&xch[2]);
+      alive = __all_sync(0xffffffffu, mbar_wait(&xch[2], 0, abort_flag, status));
+    }
+    if (alive && j >= 1) {
       tc_fence_after();
-      const float inv = ell > 0.f ? 1.f / ell : 0.f;
-      T* out = static_cast<T*>(p.out) + (((int64_t)b * p.N + q) * p.Hq + hq) * HD;
+      const float ell_row = xs[2 * 256 + r] + xs[2 * 256 + 128 + r];
+      const float inv = ell_row > 0.f ? 1.f / ell_row : 0.f;
+      T* out = static_cast<T*>(p.out) + (((int64_t)b * p.N + q) * p.Hq + hq) * HD + ch * 64;
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c4 = 0; c4 < 2; ++c4) {
         float ov[32];
-        tmem_ld32(tmem + lane_base + Sh::O_COL + c4 * 32, ov);
+        tmem_ld32(tmem + lane_base + Sh::O_COL + ch * 64 + c4 * 32, ov);
         tmem_wait_ld();
         if (row_ok) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(out + c4 * 32 + i * 8) = pack8<T>(ov + i * 8, inv);
         }
       }
-      if (row_ok) p.lse[((int64_t)b * p.N + q) * p.Hq + hq] = (m_used + log2f(ell)) * kLn2;
+      if (row_ok && ch == 0) p.lse[((int64_t)b * p.N + q) * p.Hq + hq] = (m_used + log2f(ell_row)) * kLn2;
     }
   }
   tc_fence_before();
@@ -354,10 +369,10 @@ int launch_fwd(const AttnParams& a, int dtype, cudaStream_t st) {
   p.rl_stride = a.rl_stride;
   p.rl_pad = a.rl_pad;
   p.s = a.s;
-  constexpr int smem = FwdShape<BK>::SMEM + (REL ? 2 * 128 * kRunStride * 2 : 0);
+  constexpr int smem = FwdShape<BK>::SMEM + (REL ? 2 * 128 * kRunStride * 2 + 256 : 0);
   auto k = fwd_tc_kernel<T, BK, REL>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TC_ERR_CUDA;
-  k<<<dim3((a.N + BQ - 1) / BQ, a.Hq, a.B), 256, smem, st>>>(mq, mk, mv, p);
+  k<<<dim3((a.N + BQ - 1) / BQ, a.Hq, a.B), kThreads, smem, st>>>(mq, mk, mv, p);
   return launch_status();
 }
 

@@ -32,7 +32,7 @@ constexpr int kSmemA = 2 * T128 + 4 * T64 + 128 * 128 + 1024 + 256;
 // relative Pass A: + an fp32 dX staging tile [128 x 65], per-row run info,
 // row totals and the double-buffered bias runs [2][128][kRunStride]
 constexpr int kDxfStride = 65;
-constexpr int kSmemArel = kSmemA + 128 * kDxfStride * 4 + 128 * 3 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2;
+constexpr int kSmemArel = kSmemA + 128 * kDxfStride * 4 + 128 * 3 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2 + 256;
 // Pass B: tiles + per-step query info [2][64] (int4) + bias offsets [2][64]
 // (bytes) + barriers; relative adds the staged bias columns [2][64][kColStride]
 constexpr int kColStride = 136;  // 272 B: the 16-byte aligned superset of a 128-node run
@@ -85,7 +85,7 @@ struct BwdScalars {
 // Pass A
 // ---------------------------------------------------------------------------
 template <typename T, bool REL>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmg,
                      const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(256, 1)
   int* rinfo = reinterpret_cast<int*>(dxf + 128 * kDxfStride);
   int* mtot = rinfo + 128 * 3;
   uint16_t* run_s = reinterpret_cast<uint16_t*>(mtot + 128);
+  uint8_t* sh_s = reinterpret_cast<uint8_t*>(run_s + 2 * 128 * kRunStride);  // [2][128] run offsets
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * 128, hq = blockIdx.y, b = blockIdx.z;
@@ -127,11 +128,11 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
+      mbar_init(&s_free[i], kComputeThreads);
       mbar_init(&run_full[i], 64);
-      mbar_init(&run_empty[i], 128);
+      mbar_init(&run_empty[i], kComputeThreads);
     }
-    mbar_init(x_full, 128);
+    mbar_init(x_full, kComputeThreads);
     mbar_init(x_free, 1);
     mbar_init(dq_done, 1);
     *abort_flag = 0;
@@ -219,19 +220,20 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp < 4) {
     // relative bias staging (warps 2, 3)
     if constexpr (REL)
-      stage_runs(threadIdx.x - 64, q0, q1, p.N, p.Hq, hq, b, p.s, p.rl, p.rl_stride, p.rl_pad, run_s, run_full,
-                 run_empty, abort_flag, status);
+      stage_runs(threadIdx.x - 64, q0, q1, p.N, p.Hq, hq, b, p.s, p.rl, p.rl_stride, p.rl_pad, run_s, sh_s,
+                 run_full, run_empty, abort_flag, status);
   } else {
-    const int r = threadIdx.x - 128;
+    const int r = (threadIdx.x - 128) & 127;  // query row = TMEM lane
+    const int ch = (threadIdx.x - 128) >> 7;  // node columns [32 ch, 32 ch + 32) of each tile
     const int q = q0 + r;
     const bool row_ok = q < p.N;
-    const uint32_t lane_base = (uint32_t)((warp - 4) * 32) << 16;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const BwdScalars sc(p);
     const int64_t row = ((int64_t)b * p.N + q) * p.Hq + hq;
     const float lse2 = row_ok ? p.lse[row] * kLog2e : 0.f;
     const float dlt = row_ok ? p.delta[row] : 0.f;
     const bool want_drel = REL && p.drel != nullptr;
-    if (want_drel) mtot[r] = row_ok ? visible_count(q, p.s) : 0;
+    if (want_drel && ch == 0) mtot[r] = row_ok ? visible_count(q, p.s) : 0;
     int lo = 0, hi = 0, base = 0, cur = -1;
     TileWalk it{-1, 0, 0, q0, q1, 64};
     bool ok = it.start(p.s);
@@ -254,11 +256,9 @@ __global__ void __launch_bounds__(256, 1)
       alive = __all_sync(0xffffffffu, mbar_wait(&s_full[bb], (j >> 1) & 1, abort_flag, status));
       if (!alive) break;
       tc_fence_after();
-      float sv[64], dp[64];
-      tmem_ld32(tmem + lane_base + bb * 64, sv);
-      tmem_ld32(tmem + lane_base + bb * 64 + 32, sv + 32);
-      tmem_ld32(tmem + lane_base + 128 + bb * 64, dp);
-      tmem_ld32(tmem + lane_base + 128 + bb * 64 + 32, dp + 32);
+      float sv[32], dp[32];
+      tmem_ld32(tmem + lane_base + bb * 64 + ch * 32, sv);
+      tmem_ld32(tmem + lane_base + 128 + bb * 64 + ch * 32, dp);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[bb]);
@@ -267,41 +267,33 @@ __global__ void __launch_bounds__(256, 1)
         if (!alive) break;
       }
       const int jlo = lo - it.k0, jhi = hi - it.k0;
-      // column c has bin distance base - k0 - c: staged run element 63 - c
-      // (columns 8*c8 .. 8*c8+7 are vector 7-c8 of the row, back to front)
-      const uint4* runp = nullptr;
+      // column c = 32 ch + cl has bin distance base - k0 - c: run element
+      // 63 - c, i.e. element 31 - cl of this thread's 32-element window
+      uint32_t run[REL ? 16 : 1];
       if constexpr (REL) {
         alive = __all_sync(0xffffffffu, mbar_wait(&run_full[bb], (j >> 1) & 1, abort_flag, status));
         if (!alive) break;
-        runp = reinterpret_cast<const uint4*>(run_s + bb * 128 * kRunStride + r * kRunStride);
+        load_run32(run_s + (bb * 128 + r) * kRunStride, sh_s[bb * 128 + r], ch, run);
+        mbar_arrive(&run_empty[bb]);
       }
       // the single dX staging tile is free once every warp wrote out the last one
-      if (want_drel && j >= 1) named_bar(1, 128);
+      if (want_drel && j >= 1) named_bar(1, kComputeThreads);
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
+      for (int cc8 = 0; cc8 < 4; ++cc8) {
+        const int c8 = ch * 4 + cc8;
         float dx[8];
-        uint32_t w[4] = {0u, 0u, 0u, 0u};
-        if constexpr (REL) {
-          const uint4 v = runp[7 - c8];
-          w[0] = v.x;
-          w[1] = v.y;
-          w[2] = v.z;
-          w[3] = v.w;
-        }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int c = c8 * 8 + i, e = 7 - i;
-          const uint16_t h = (e & 1) ? (uint16_t)(w[e >> 1] >> 16) : (uint16_t)(w[e >> 1] & 0xffffu);
+          const int c = c8 * 8 + i, cl = cc8 * 8 + i;
           float l2, g;
-          sc.logit(sv[c], REL ? bits_to_float<T>(h) : 0.f, p.has_cap, &l2, &g);
+          sc.logit(sv[cl], REL ? run_elem<T>(run, 31 - cl) : 0.f, p.has_cap, &l2, &g);
           const bool valid = c >= jlo && c < jhi;
           const float pr = valid ? exp2_fast(l2 - lse2) : 0.f;
-          dx[i] = valid ? pr * (dp[c] - dlt) * g : 0.f;
+          dx[i] = valid ? pr * (dp[cl] - dlt) * g : 0.f;
           if (want_drel) dxf[r * kDxfStride + c] = dx[i];
         }
         *reinterpret_cast<uint4*>(x_s + sw128_offset(r, c8 * 8, 128)) = pack8<T>(dx, 1.f);
       }
-      if constexpr (REL) mbar_arrive(&run_empty[bb]);
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(x_full);
@@ -310,16 +302,18 @@ __global__ void __launch_bounds__(256, 1)
         // valid columns [cs, ce) are distances base - k0 - c, one ascending run
         // in memory; the warp then writes its 32 rows' runs coalesced.
         const int cs = max(jlo, 0), ce = min(jhi, 64);
-        int* ri = rinfo + r * 3;
-        ri[0] = base - it.k0 - (ce - 1);
-        ri[1] = (row_ok && lo < hi && ce > cs) ? ce - cs : 0;
-        ri[2] = ce;
-        named_bar(1, 128);
-        const int w4 = warp - 4;
+        if (ch == 0) {
+          int* ri = rinfo + r * 3;
+          ri[0] = base - it.k0 - (ce - 1);
+          ri[1] = (row_ok && lo < hi && ce > cs) ? ce - cs : 0;
+          ri[2] = ce;
+        }
+        named_bar(1, kComputeThreads);
+        const int w8 = warp - 4;  // 16 rows per compute warp
         const float* src = dxf;
         const int* inf = rinfo;
-        for (int k = 0; k < 32; ++k) {
-          const int rr = w4 * 32 + k;
+        for (int k = 0; k < 16; ++k) {
+          const int rr = w8 * 16 + k;
           const int n = inf[rr * 3 + 1];
           if (n == 0) continue;
           const int dmin = inf[rr * 3], cend = inf[rr * 3 + 2];
@@ -328,12 +322,12 @@ __global__ void __launch_bounds__(256, 1)
         }
       }
     }
-    if (want_drel) {  // all four warps reach this barrier, also after an abort
+    if (want_drel) {  // every compute warp reaches this barrier, also after an abort
       // distances at or beyond a row's visible count are never attended: zero them
-      named_bar(1, 128);
-      const int w4 = warp - 4;
-      for (int k = 0; k < 32; ++k) {
-        const int rr = w4 * 32 + k;
+      named_bar(1, kComputeThreads);
+      const int w8 = warp - 4;
+      for (int k = 0; k < 16; ++k) {
+        const int rr = w8 * 16 + k;
         if (q0 + rr >= p.N) break;
         float* dst = p.drel + (((int64_t)b * p.N + q0 + rr) * p.Hq + hq) * p.bins;
         for (int d = mtot[rr] + lane; d < p.bins; d += 32) dst[d] = 0.f;
@@ -342,23 +336,8 @@ __global__ void __launch_bounds__(256, 1)
     if (alive && j >= 1) alive = __all_sync(0xffffffffu, mbar_wait(dq_done, 0, abort_flag, status));
     if (alive) {
       tc_fence_after();
-      float v[128];
-      if (j >= 1) {
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(tmem + lane_base + 256 + c4 * 32, v + c4 * 32);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 128; ++i) v[i] *= p.scale;
-      } else {
-#pragma unroll
-        for (int i = 0; i < 128; ++i) v[i] = 0.f;
-      }
-      if (row_ok) {
-        if (p.rope) rope_inverse_row(v, p.cos_t, p.sin_t, q);
-        T* out = static_cast<T*>(p.dq) + row * HD;
-#pragma unroll
-        for (int c8 = 0; c8 < 16; ++c8) *reinterpret_cast<uint4*>(out + c8 * 8) = pack8<T>(v + c8 * 8, 1.f);
-      }
+      store_half_row<T>(tmem + lane_base + 256, ch, j >= 1, static_cast<T*>(p.dq) + row * HD, p.scale,
+                        p.rope != 0, p.cos_t, p.sin_t, q, row_ok);
     }
   }
   tc_fence_before();
@@ -392,7 +371,7 @@ struct QSteps {
 };
 
 template <typename T, bool REL>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmg,
                       const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                       BwdParams p) {
@@ -441,11 +420,11 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
+      mbar_init(&s_free[i], kComputeThreads);
       mbar_init(&info_full[i], 64);
-      mbar_init(&info_empty[i], 128);
+      mbar_init(&info_empty[i], kComputeThreads);
     }
-    mbar_init(x_full, 128);
+    mbar_init(x_full, kComputeThreads);
     mbar_init(x_free, 1);
     mbar_init(kv_done, 1);
     *abort_flag = 0;
@@ -583,10 +562,11 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
   } else {
-    const int r = threadIdx.x - 128;     // node row = TMEM lane
-    const int jn = k0 + r;               // level-local node index
+    const int r = (threadIdx.x - 128) & 127;  // node row = TMEM lane
+    const int ch = (threadIdx.x - 128) >> 7;  // query columns [32 ch, 32 ch + 32) of each step
+    const int jn = k0 + r;                    // level-local node index
     const bool node_ok = r < nk;
-    const uint32_t lane_base = (uint32_t)((warp - 4) * 32) << 16;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const BwdScalars sc(p);
     QSteps w;
     bool ok = w.start(qlo, qhi, p.E);
@@ -597,11 +577,9 @@ __global__ void __launch_bounds__(256, 1)
       alive = __all_sync(0xffffffffu, mbar_wait(&s_full[bb], (i >> 1) & 1, abort_flag, status));
       if (!alive) break;
       tc_fence_after();
-      float sv[64], dp[64];
-      tmem_ld32(tmem + lane_base + bb * 64, sv);
-      tmem_ld32(tmem + lane_base + bb * 64 + 32, sv + 32);
-      tmem_ld32(tmem + lane_base + 128 + bb * 64, dp);
-      tmem_ld32(tmem + lane_base + 128 + bb * 64 + 32, dp + 32);
+      float sv[32], dp[32];
+      tmem_ld32(tmem + lane_base + bb * 64 + ch * 32, sv);
+      tmem_ld32(tmem + lane_base + 128 + bb * 64 + ch * 32, dp);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[bb]);
@@ -615,13 +593,14 @@ __global__ void __launch_bounds__(256, 1)
       const uint8_t* bo = bo_s + bb * 64;
       const uint16_t* bcol = bias_s + bb * 64 * kColStride + 127 - r;
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
+      for (int cc8 = 0; cc8 < 4; ++cc8) {
+        const int c8 = ch * 4 + cc8;
         float pr[8], dx[8];
         uint2 bo8 = make_uint2(0u, 0u);
         if constexpr (REL) bo8 = *reinterpret_cast<const uint2*>(bo + c8 * 8);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const int c = c8 * 8 + k;
+          const int c = c8 * 8 + k, cl = cc8 * 8 + k;
           const int4 ci = inf[c];
           const bool valid = node_ok && jn >= ci.x && jn < ci.y;
           float bias = 0.f;
@@ -631,9 +610,9 @@ __global__ void __launch_bounds__(256, 1)
             bias = bits_to_float<T>(bcol[c * kColStride + o]);
           }
           float l2, g;
-          sc.logit(sv[c], bias, p.has_cap, &l2, &g);
+          sc.logit(sv[cl], bias, p.has_cap, &l2, &g);
           pr[k] = valid ? exp2_fast(l2 - __int_as_float(ci.z)) : 0.f;
-          dx[k] = valid ? pr[k] * (dp[c] - __int_as_float(ci.w)) * g : 0.f;
+          dx[k] = valid ? pr[k] * (dp[cl] - __int_as_float(ci.w)) * g : 0.f;
         }
         const uint32_t off = sw128_offset(r, c8 * 8, 128);
         *reinterpret_cast<uint4*>(pt_s + off) = pack8<T>(pr, 1.f);
@@ -648,35 +627,10 @@ __global__ void __launch_bounds__(256, 1)
     if (alive) {
       tc_fence_after();
       const int64_t orow = ((int64_t)b * (p.s.off[p.s.nl]) + row0 + r) * p.Hkv + hkv;
-      float v[128];
-      // dV
-      if (i >= 1) {
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(tmem + lane_base + 256 + c4 * 32, v + c4 * 32);
-        tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int k = 0; k < 128; ++k) v[k] = 0.f;
-      }
-      if (node_ok) {
-        T* out = static_cast<T*>(p.dv) + orow * HD;
-#pragma unroll
-        for (int c8 = 0; c8 < 16; ++c8) *reinterpret_cast<uint4*>(out + c8 * 8) = pack8<T>(v + c8 * 8, 1.f);
-      }
-      // dK
-      if (i >= 1) {
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(tmem + lane_base + 384 + c4 * 32, v + c4 * 32);
-        tmem_wait_ld();
-#pragma unroll
-        for (int k = 0; k < 128; ++k) v[k] *= p.scale;
-      }
-      if (node_ok) {
-        if (p.rope && i >= 1) rope_inverse_row(v, p.cos_t, p.sin_t, ((jn + 1) << lev) - 1);
-        T* out = static_cast<T*>(p.dk) + orow * HD;
-#pragma unroll
-        for (int c8 = 0; c8 < 16; ++c8) *reinterpret_cast<uint4*>(out + c8 * 8) = pack8<T>(v + c8 * 8, 1.f);
-      }
+      store_half_row<T>(tmem + lane_base + 256, ch, i >= 1, static_cast<T*>(p.dv) + orow * HD, 1.f, false,
+                        nullptr, nullptr, 0, node_ok);
+      store_half_row<T>(tmem + lane_base + 384, ch, i >= 1, static_cast<T*>(p.dk) + orow * HD, p.scale,
+                        p.rope != 0, p.cos_t, p.sin_t, ((jn + 1) << lev) - 1, node_ok);
     }
   }
   tc_fence_before();
@@ -729,7 +683,7 @@ int launch_bwd(const AttnParams& a, int dtype, cudaStream_t st) {
   auto ka = bwd_dq_tc_kernel<T, REL>;
   constexpr int smem_a = REL ? kSmemArel : kSmemA;
   if (cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_a) != cudaSuccess) return TC_ERR_CUDA;
-  ka<<<dim3((a.N + 127) / 128, a.Hq, a.B), 256, smem_a, st>>>(mq128, mg128, mk64, mv64, p);
+  ka<<<dim3((a.N + 127) / 128, a.Hq, a.B), kThreads, smem_a, st>>>(mq128, mg128, mk64, mv64, p);
   if (int rc = launch_status()) return rc;
   const int ntiles = p.tiles[a.s.nl];
   if (ntiles > 0) {
@@ -737,7 +691,7 @@ int launch_bwd(const AttnParams& a, int dtype, cudaStream_t st) {
     constexpr int smem_b = REL ? kSmemBrel : kSmemB;
     if (cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_b) != cudaSuccess)
       return TC_ERR_CUDA;
-    kb<<<dim3(ntiles, a.Hkv, a.B), 256, smem_b, st>>>(mq64, mg64, mk128, mv128, p);
+    kb<<<dim3(ntiles, a.Hkv, a.B), kThreads, smem_b, st>>>(mq64, mg64, mk128, mv128, p);
     if (int rc = launch_status()) return rc;
   }
   return TC_OK;

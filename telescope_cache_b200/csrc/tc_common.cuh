@@ -133,17 +133,17 @@ __device__ __forceinline__ float run_elem(const uint32_t* run, int i) {
 constexpr int kRunStride = 72;  // elements per staged row (144 B: 16-B accesses conflict-light)
 
 // q-major kernels (forward, Pass A), 64-node tiles: for every tile of the
-// walk and every query row r of the block, run_s[buf][r][i] =
-// rl[row, pad + base_r - k0 - 63 + i] for i < 64 (zeros for rows without a
-// visible node in the tile).  Thread t (0..63 of warps 2-3) owns rows t and
-// t + 64: per row and tile it loads the 16-byte aligned 144-byte superset of
-// the run (9 vector loads), realigns it in registers and stores it with
-// 16-byte writes.  The loads of tile j + 1 are issued before tile j is
-// realigned and stored, so one tile's latency is always hidden.
+// walk and every query row r of the block, the bias run of the row
+// (rl[row, pad + base_r - k0 - 63 + i], i < 64) lands in run_s[buf][r] as its
+// 16-byte aligned 144-byte superset: run element i is raw element
+// sh_s[buf][r] + i.  Thread t (0..63 of warps 2-3) owns rows t and t + 64 and
+// issues one bulk copy per visible row; completion is counted on
+// run_full[buf] (one arrival per thread plus the copied bytes).  Rows without
+// a visible node in the tile are not copied: their columns are masked.
 __device__ __forceinline__ void stage_runs(int t, int q0, int q1, int N, int Hq, int hq, int b, const Sched& s,
                                            const uint16_t* rl, int64_t stride, int pad, uint16_t* run_s,
-                                           uint64_t* run_full, uint64_t* run_empty, volatile int* abort_flag,
-                                           int32_t* status) {
+                                           uint8_t* sh_s, uint64_t* run_full, uint64_t* run_empty,
+                                           volatile int* abort_flag, int32_t* status) {
   int64_t roff[2];
   bool rok[2];
 #pragma unroll
@@ -155,10 +155,11 @@ __device__ __forceinline__ void stage_runs(int t, int q0, int q1, int N, int Hq,
   TileWalk it{-1, 0, 0, q0, q1, 64};
   int cur = -1;
   int lo[2] = {0, 0}, hi[2] = {0, 0}, base[2] = {0, 0};
-  uint4 raw[2][9];
-  int sh[2] = {0, 0};
-  bool vis[2] = {false, false};
-  auto issue = [&]() {
+  bool ok = it.start(s);
+  for (int j = 0; ok; ++j, ok = it.advance(s)) {
+    const int buf = j & 1;
+    if (j >= 2 && !__all_sync(0xffffffffu, ptx::mbar_wait(&run_empty[buf], ((j >> 1) - 1) & 1, abort_flag, status)))
+      break;
     if (it.lev != cur) {
       cur = it.lev;
 #pragma unroll
@@ -167,85 +168,93 @@ __device__ __forceinline__ void stage_runs(int t, int q0, int q1, int N, int Hq,
         if (rok[h]) level_info(q0 + t + 64 * h, cur, s, &lo[h], &hi[h], &base[h]);
       }
     }
+    bool vis[2];
+    int64_t src[2];
+    uint32_t bytes = 0;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       vis[h] = lo[h] < hi[h] && lo[h] - it.k0 < 64 && hi[h] - it.k0 > 0;
       const int64_t e0 = roff[h] + base[h] - it.k0 - 63;
-      const int64_t a = e0 & ~int64_t(7);
-      sh[h] = (int)(e0 - a);
-      if (vis[h]) {
-        const uint4* src = reinterpret_cast<const uint4*>(rl + a);
-#pragma unroll
-        for (int i = 0; i < 9; ++i) raw[h][i] = __ldg(src + i);
-      }
+      src[h] = e0 & ~int64_t(7);
+      sh_s[buf * 128 + t + 64 * h] = (uint8_t)(e0 - src[h]);
+      if (vis[h]) bytes += kRunStride * 2;
     }
-  };
-  bool ok = it.start(s);
-  if (ok) issue();
-  for (int j = 0; ok; ++j) {
-    uint4 pend[2][9];
-    int psh[2];
-    bool pvis[2];
+    if (bytes) ptx::mbar_expect_tx(&run_full[buf], bytes);  // this thread's arrival + its bytes
+    else ptx::mbar_arrive(&run_full[buf]);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      psh[h] = sh[h];
-      pvis[h] = vis[h];
-#pragma unroll
-      for (int i = 0; i < 9; ++i) pend[h][i] = raw[h][i];
-    }
-    ok = it.advance(s);
-    if (ok) issue();  // next tile's loads in flight while this one is stored
-    const int buf = j & 1;
-    if (j >= 2 && !__all_sync(0xffffffffu, ptx::mbar_wait(&run_empty[buf], ((j >> 1) - 1) & 1, abort_flag, status)))
-      break;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint4* dst = reinterpret_cast<uint4*>(run_s + buf * 128 * kRunStride + (t + 64 * h) * kRunStride);
-      if (!pvis[h]) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) dst[i] = make_uint4(0u, 0u, 0u, 0u);
-        continue;
-      }
-      uint32_t w[36];
-#pragma unroll
-      for (int i = 0; i < 9; ++i) {
-        w[4 * i] = pend[h][i].x;
-        w[4 * i + 1] = pend[h][i].y;
-        w[4 * i + 2] = pend[h][i].z;
-        w[4 * i + 3] = pend[h][i].w;
-      }
-      // drop sh halves: whole words by two select stages, then one funnel shift
-      const int wo = psh[h] >> 1;
-#pragma unroll
-      for (int i = 0; i < 35; ++i) w[i] = (wo & 1) ? w[i + 1] : w[i];
-#pragma unroll
-      for (int i = 0; i < 33; ++i) w[i] = (wo & 2) ? w[i + 2] : w[i];
-      const bool odd = psh[h] & 1;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        uint32_t o[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int m = 4 * i + k;
-          o[k] = odd ? __funnelshift_r(w[m], w[m + 1], 16) : w[m];
-        }
-        dst[i] = make_uint4(o[0], o[1], o[2], o[3]);
-      }
-    }
-    ptx::mbar_arrive(&run_full[buf]);
+    for (int h = 0; h < 2; ++h)
+      if (vis[h])
+        ptx::bulk_load(run_s + (buf * 128 + t + 64 * h) * kRunStride, rl + src[h], kRunStride * 2, &run_full[buf]);
   }
 }
 
-// A staged run row as 32 packed words (element 2k in the low half of word k).
-__device__ __forceinline__ void read_run(const uint16_t* row, uint32_t* w) {
-  const uint4* src = reinterpret_cast<const uint4*>(row);
+// The 32 run elements [32 (1 - ch), 32 (1 - ch) + 32) of a staged row whose
+// run starts at raw element sh, as 16 packed words (element 2k + 32 (1 - ch)
+// in the low half of word k): 5 aligned 16-byte reads, two select stages
+// (whole words) and one funnel shift (half words).
+__device__ __forceinline__ void load_run32(const uint16_t* raw_row, int sh, int ch, uint32_t* out) {
+  const uint4* src = reinterpret_cast<const uint4*>(raw_row) + 4 * (1 - ch);
+  uint32_t w[20];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < 5; ++i) {
     const uint4 v = src[i];
     w[4 * i] = v.x;
     w[4 * i + 1] = v.y;
     w[4 * i + 2] = v.z;
     w[4 * i + 3] = v.w;
+  }
+  const int wo = sh >> 1;
+#pragma unroll
+  for (int i = 0; i < 19; ++i) w[i] = (wo & 1) ? w[i + 1] : w[i];
+#pragma unroll
+  for (int i = 0; i < 17; ++i) w[i] = (wo & 2) ? w[i + 2] : w[i];
+  const bool odd = sh & 1;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) out[k] = odd ? __funnelshift_r(w[k], w[k + 1], 16) : w[k];
+}
+
+// Compute roles of the tensor-core kernels: two threads per TMEM lane (row),
+// warps 4..11; thread (r, ch) owns columns [half * ch, half * (ch + 1)) of
+// each tile.  Warps w and w + 4 read the same TMEM lanes (32 * (w % 4) ..).
+constexpr int kComputeThreads = 256;
+constexpr int kThreads = 128 + kComputeThreads;
+
+// Epilogue of a 128-wide fp32 TMEM row split between the row's two threads:
+// this thread owns columns [64 ch, 64 ch + 64).  It loads them (and, for the
+// inverse RoPE, the partner columns c ^ 64), scales by `mul`, rotates by
+// R(-pos) and stores its 64 elements of the 128-wide `out` row when `store`.
+// have = false stores zeros (nothing was accumulated).  Warp-collective.
+template <typename T>
+__device__ __forceinline__ void store_half_row(uint32_t taddr, int ch, bool have, T* out, float mul, bool rope,
+                                               const float* cos_t, const float* sin_t, int pos, bool store) {
+#pragma unroll
+  for (int h2 = 0; h2 < 2; ++h2) {
+    const int c0 = ch * 64 + h2 * 32;
+    float a[32], pb[32];
+    if (have) {
+      ptx::tmem_ld32(taddr + c0, a);
+      if (rope) ptx::tmem_ld32(taddr + (c0 ^ 64), pb);
+      ptx::tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) a[i] = pb[i] = 0.f;
+    }
+    if (!store) continue;
+    if (rope && have) {
+      const float* cr = cos_t + (int64_t)pos * (HD / 2) + (c0 & 63);
+      const float* sr = sin_t + (int64_t)pos * (HD / 2) + (c0 & 63);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float cc = __ldg(cr + i), ss = __ldg(sr + i);
+        // first half: x1 c + x2 s; second half: x2 c - x1 s (x1 = dims < 64)
+        a[i] = ch == 0 ? (a[i] * cc + pb[i] * ss) * mul : (a[i] * cc - pb[i] * ss) * mul;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) a[i] *= mul;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(out + c0 + i * 8) = pack8<T>(a + i * 8, 1.f);
   }
 }
 
