@@ -6,10 +6,14 @@
 // (fwd_hull) in BK-node tiles (BK = 128, or 64 for the relative bias):
 //   warp 0      TMA producer: Q once, then K/V tiles into an NS-stage ring
 //   warp 1      MMA issuer:   S_j = Q K_j^T into TMEM (double buffered),
-//                             O += P_{j-1} V_{j-1} (P from shared memory)
+//                             O += P_{j-1} V_{j-1} (P from shared memory,
+//                             double buffered for 64-node tiles, so the
+//                             softmax only waits on a PV product before a
+//                             lazy O rescale or a P buffer reuse)
 //   warps 2, 3  relative bias staging: bulk copies of each row's bias run
-//   warps 4..11 softmax:      two threads per query row (= TMEM lane), each
-//                             with half of the tile's columns: exact per-row
+//   warps 4..   softmax:      kRowThreads threads per query row (= TMEM
+//                             lane), each with a slice of the tile's
+//                             columns: exact per-row
 //                             level mask, relative bias, softcap, online
 //                             softmax in log2 units with lazy O rescaling (the
 //                             row maximum is exchanged through shared memory),
@@ -34,10 +38,11 @@ template <int BK> struct FwdShape {
   static constexpr int KVBLK = BK * 128;              // one 64-column block of a K/V tile
   static constexpr int KVTILE = 2 * KVBLK;            // one K or V tile
   static constexpr int PTILE = 128 * BK * 2;          // P tile [128 x BK]
+  static constexpr int NP = BK == 64 ? 2 : 1;         // P buffers
   static constexpr int TMEM_COLS = BK == 64 ? 256 : 512;
   static constexpr int O_COL = 2 * BK;
-  // + 1024 alignment slack, 256 barriers, 3 x 256 row-maximum / row-sum exchange
-  static constexpr int SMEM = QTILE + 2 * NS * KVTILE + PTILE + 1024 + 256 + 3 * 256 * 4;
+  // + 1024 alignment slack, 256 barriers, [3][kRowThreads][128] row-maximum / row-sum exchange
+  static constexpr int SMEM = QTILE + 2 * NS * KVTILE + NP * PTILE + 1024 + 256 + 3 * kRowThreads * 128 * 4;
 };
 
 struct TcParams {
@@ -53,7 +58,36 @@ struct TcParams {
   Sched s;
 };
 
-template <typename T, int BK, bool REL>
+// Logits of this thread's HC columns of a tile, in place: log2 units
+// (s * scale + bias) * log2e, or with the softcap the unscaled tanh((s * scale
+// + bias) / cap), whose log2 logit is t * cap * log2e; masked columns are
+// -inf.  Returns the maximum of the values stored.
+template <typename T, int HC, bool REL, bool CAP, bool MASK>
+__device__ __forceinline__ float fwd_logits(float* sv, const uint32_t* run, float kq, float kb, int jlo, int jhi) {
+  const float2 kq2 = make_float2(kq, kq), kb2 = make_float2(kb, kb);
+  float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < HC; c += 2) {
+    float2 y = make_float2(sv[c], sv[c + 1]);
+    if constexpr (REL) y = ffma2(y, kq2, fmul2(bias_pair<T>(run[(HC - 2 - c) / 2]), kb2));
+    else y = fmul2(y, kq2);
+    if constexpr (CAP) {
+      y.x = tanh_fast(y.x);
+      y.y = tanh_fast(y.y);
+    }
+    if constexpr (MASK) {
+      y.x = (c >= jlo && c < jhi) ? y.x : -INFINITY;
+      y.y = (c + 1 >= jlo && c + 1 < jhi) ? y.y : -INFINITY;
+    }
+    sv[c] = y.x;
+    sv[c + 1] = y.y;
+    if ((c >> 1) & 1) m1 = fmax3(m1, y.x, y.y);
+    else m0 = fmax3(m0, y.x, y.y);
+  }
+  return fmaxf(m0, m1);
+}
+
+template <typename T, int BK, bool REL, bool CAP>
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, TcParams p) {
@@ -65,21 +99,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* k_s = q_s + QTILE;
   uint8_t* v_s = k_s + NS * Sh::KVTILE;
   uint8_t* p_s = v_s + NS * Sh::KVTILE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + Sh::PTILE);
+  constexpr int NP = Sh::NP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + NP * Sh::PTILE);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + NS;
   uint64_t* s_full = kv_empty + NS;
   uint64_t* s_free = s_full + 2;
-  uint64_t* p_full = s_free + 2;
-  uint64_t* o_done = p_full + 1;
-  uint64_t* run_full = o_done + 1;   // relative: staged bias runs ready (warps 2-3)
+  uint64_t* p_full = s_free + 2;     // [NP] P(j) in buffer j % NP written
+  uint64_t* p_empty = p_full + NP;   // [NP] PV(j) done: buffer free, O up to date
+  uint64_t* run_full = p_empty + NP; // relative: staged bias runs ready (warps 2-3)
   uint64_t* run_empty = run_full + 2;
   uint64_t* xch = run_empty + 2;     // [2] row-maximum exchange, [2] final row sum
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xch + 3);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  float* xs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [3][2][128]
-  uint16_t* run_s = reinterpret_cast<uint16_t*>(xs + 3 * 256);                   // [2][128][72]
+  float* xs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [3][kRowThreads][128]
+  uint16_t* run_s = reinterpret_cast<uint16_t*>(xs + 3 * kRowThreads * 128);     // [2][128][72]
   uint8_t* sh_s = reinterpret_cast<uint8_t*>(run_s + 2 * 128 * kRunStride);      // [2][128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -100,8 +135,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&run_empty[i], kComputeThreads);
     }
     for (int i = 0; i < 3; ++i) mbar_init(&xch[i], kComputeThreads);
-    mbar_init(p_full, kComputeThreads);
-    mbar_init(o_done, 1);
+    for (int i = 0; i < NP; ++i) {
+      mbar_init(&p_full[i], kComputeThreads);
+      mbar_init(&p_empty[i], 1);
+    }
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -149,13 +186,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t qa = smem_addr(q_s), pa = smem_addr(p_s);
       auto issue_pv = [&](int t) {
         const uint32_t va = smem_addr(v_s + (t % NS) * Sh::KVTILE);
+        const uint32_t pb = pa + (t % NP) * Sh::PTILE;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128(pa + (kk >> 2) * QBLK + (kk & 3) * 32, 16, 1024);
+          const uint64_t ad = sdesc_sw128(pb + (kk >> 2) * QBLK + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(va + kk * 2048, Sh::KVBLK, 1024);
           mma_f16(tmem + Sh::O_COL, ad, bd, kIdPV, (t > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(o_done);
+        mma_commit(&p_empty[t % NP]);
         mma_commit(&kv_empty[t % NS]);
       };
       bool alive = mbar_wait(q_full, 0, abort_flag, status);
@@ -177,12 +215,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(&s_full[bb]);
         if (j >= 1) {
-          if (!mbar_wait(p_full, (j - 1) & 1, abort_flag, status)) { alive = false; break; }
+          const int t = j - 1;
+          if (!mbar_wait(&p_full[t % NP], (t / NP) & 1, abort_flag, status)) { alive = false; break; }
           tc_fence_after();
-          issue_pv(j - 1);
+          issue_pv(t);
         }
       }
-      if (alive && j >= 1 && mbar_wait(p_full, (j - 1) & 1, abort_flag, status)) {
+      if (alive && j >= 1 && mbar_wait(&p_full[(j - 1) % NP], ((j - 1) / NP) & 1, abort_flag, status)) {
         tc_fence_after();
         issue_pv(j - 1);
       }
@@ -193,8 +232,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       stage_runs(threadIdx.x - 64, q0, q1, p.N, p.Hq, hq, b, p.s, p.rl, p.rl_stride, p.rl_pad, run_s, sh_s,
                  run_full, run_empty, abort_flag, status);
   } else {
-    // ---------------- softmax / epilogue: two threads per query row ----------------
-    constexpr int HC = BK / 2;  // columns per thread: [HC ch, HC ch + HC) of each tile
+    // ---------------- softmax / epilogue: kRowThreads threads per query row ----------------
+    constexpr int HC = BK / kRowThreads;   // columns per thread: [HC ch, HC ch + HC) of each tile
+    constexpr int OC = HD / kRowThreads;   // output columns per thread
+    constexpr int XS = kRowThreads * 128;  // one exchange slot
     const int r = (threadIdx.x - 128) & 127;
     const int ch = (threadIdx.x - 128) >> 7;
     const int q = q0 + r;
@@ -224,47 +265,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       alive = __all_sync(0xffffffffu, mbar_wait(&s_full[bb], (j >> 1) & 1, abort_flag, status));
       if (!alive) break;
       tc_fence_after();
-#pragma unroll
-      for (int c4 = 0; c4 < HC / 32; ++c4) tmem_ld32(tmem + lane_base + bb * BK + ch * HC + c4 * 32, sv + 32 * c4);
+      tmem_ld<HC>(tmem + lane_base + bb * BK + ch * HC, sv);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[bb]);
       const int jlo = lo - it.k0 - ch * HC, jhi = hi - it.k0 - ch * HC;  // this thread's columns
-      const bool interior = jlo <= 0 && jhi >= HC;  // every column visible: no mask
-      float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // every column of the warp's rows visible: the unmasked variant
+      const bool interior = __all_sync(0xffffffffu, jlo <= 0 && jhi >= HC);
+      uint32_t run[REL ? HC / 2 : 1];
       if constexpr (REL) {
         static_assert(!REL || BK == 64, "the relative bias path uses 64-node tiles");
-        // column c = 32 ch + cl sees bin distance base - k0 - c: run element
-        // 63 - c = element 31 - cl of this thread's 32-element window
+        // column c = HC ch + cl sees bin distance base - k0 - c: run element
+        // 63 - c = element HC - 1 - cl of this thread's window
         alive = __all_sync(0xffffffffu, mbar_wait(&run_full[bb], (j >> 1) & 1, abort_flag, status));
         if (!alive) break;
-        uint32_t run[16];
-        load_run32(run_s + (bb * 128 + r) * kRunStride, sh_s[bb * 128 + r], ch, run);
+        load_run_part<HC>(run_s + (bb * 128 + r) * kRunStride, sh_s[bb * 128 + r], ch, run);
         mbar_arrive(&run_empty[bb]);
-#pragma unroll
-        for (int c = 0; c < HC; ++c) {
-          float x = fmaf(sv[c], kq, run_elem<T>(run, 31 - c) * kb);
-          if (p.has_cap) x = tanh_fast(x) * kc;
-          if (!interior) x = (c >= jlo && c < jhi) ? x : -INFINITY;
-          sv[c] = x;
-          mxp[c & 3] = fmaxf(mxp[c & 3], x);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < HC; ++c) {
-          float x = sv[c] * kq;
-          if (p.has_cap) x = tanh_fast(x) * kc;
-          if (!interior) x = (c >= jlo && c < jhi) ? x : -INFINITY;
-          sv[c] = x;
-          mxp[c & 3] = fmaxf(mxp[c & 3], x);
-        }
       }
-      // row maximum over both halves (bounded wait on the exchange barrier)
-      xs[bb * 256 + ch * 128 + r] = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
+      float mloc = interior ? fwd_logits<T, HC, REL, CAP, false>(sv, run, kq, kb, jlo, jhi)
+                            : fwd_logits<T, HC, REL, CAP, true>(sv, run, kq, kb, jlo, jhi);
+      if constexpr (CAP) mloc *= kc;  // log2 units (kc > 0 keeps the order; -inf stays -inf)
+      // row maximum over the row's threads (bounded wait on the exchange barrier)
+      xs[bb * XS + ch * 128 + r] = mloc;
       mbar_arrive(&xch[bb]);
       alive = __all_sync(0xffffffffu, mbar_wait(&xch[bb], (j >> 1) & 1, abort_flag, status));
       if (!alive) break;
-      const float mx = fmaxf(xs[bb * 256 + r], xs[bb * 256 + 128 + r]);
+      float mx = xs[bb * XS + r];
+#pragma unroll
+      for (int k = 1; k < kRowThreads; ++k) mx = fmaxf(mx, xs[bb * XS + k * 128 + r]);
       bool rescale = false;
       float alpha = 1.f;
       if (mx > -INFINITY) {
@@ -276,17 +304,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           rescale = true;
         }
       }
-      if (j >= 1) {
-        alive = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, abort_flag, status));
-        if (!alive) break;
-      }
+      // PV(j - 1) done (and every earlier one: commits complete in order); a
+      // buffer's barrier is at most one phase ahead of this thread's waits
+      auto pv_done = [&](int t) {
+        return __all_sync(0xffffffffu, mbar_wait(&p_empty[t % NP], (t / NP) & 1, abort_flag, status));
+      };
       if (__any_sync(0xffffffffu, rescale)) {
+        if (j >= 1 && !(alive = pv_done(j - 1))) break;
         ell *= alpha;
         tc_fence_after();
         float ov[32];
 #pragma unroll
-        for (int c4 = 0; c4 < 2; ++c4) {
-          const uint32_t oa = tmem + lane_base + Sh::O_COL + ch * 64 + c4 * 32;
+        for (int c4 = 0; c4 < OC / 32; ++c4) {
+          const uint32_t oa = tmem + lane_base + Sh::O_COL + ch * OC + c4 * 32;
           tmem_ld32(oa, ov);
           tmem_wait_ld();
 #pragma unroll
@@ -295,41 +325,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_wait_st();
       }
-      float sp[4] = {0.f, 0.f, 0.f, 0.f};
-      const bool live = m_used > -INFINITY;
+      if (j >= NP && !(alive = pv_done(j - NP))) break;  // P buffer j % NP free
+      uint8_t* pbuf = p_s + (j % NP) * Sh::PTILE;
+      // p = exp2(logit2 - m); a row with no visible entry yet has only -inf
+      // logits, and m = 0 keeps exp2(-inf) = 0
+      const float m_eff = m_used > -INFINITY ? m_used : 0.f;
+      const float2 negm = make_float2(-m_eff, -m_eff), kc2 = make_float2(kc, kc);
+      float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int c8 = 0; c8 < HC / 8; ++c8) {
         float pv[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          pv[i] = live ? exp2_fast(sv[c8 * 8 + i] - m_used) : 0.f;
-          sp[i & 3] += pv[i];
+        for (int i = 0; i < 8; i += 2) {
+          const float2 y = make_float2(sv[c8 * 8 + i], sv[c8 * 8 + i + 1]);
+          const float2 a = CAP ? ffma2(y, kc2, negm) : fadd2(y, negm);
+          pv[i] = exp2_fast(a.x);
+          pv[i + 1] = exp2_fast(a.y);
+          if ((i >> 1) & 1) s1 = fadd2(s1, make_float2(pv[i], pv[i + 1]));
+          else s0 = fadd2(s0, make_float2(pv[i], pv[i + 1]));
         }
-        *reinterpret_cast<uint4*>(p_s + sw128_offset(r, ch * HC + c8 * 8, 128)) = pack8<T>(pv, 1.f);
+        *reinterpret_cast<uint4*>(pbuf + sw128_offset(r, ch * HC + c8 * 8, 128)) = pack8<T>(pv, 1.f);
       }
-      ell += (sp[0] + sp[1]) + (sp[2] + sp[3]);
+      const float2 st2 = fadd2(s0, s1);
+      ell += st2.x + st2.y;
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[j % NP]);
     }
     if (alive && j >= 1) {
-      alive = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, abort_flag, status));
+      alive = __all_sync(0xffffffffu,
+                         mbar_wait(&p_empty[(j - 1) % NP], ((j - 1) / NP) & 1, abort_flag, status));
     }
     if (alive && j >= 1) {
-      // the row sum of both halves
-      xs[2 * 256 + ch * 128 + r] = ell;
+      // the row sum over the row's threads
+      xs[2 * XS + ch * 128 + r] = ell;
       mbar_arrive(&xch[2]);
       alive = __all_sync(0xffffffffu, mbar_wait(&xch[2], 0, abort_flag, status));
     }
     if (alive && j >= 1) {
       tc_fence_after();
-      const float ell_row = xs[2 * 256 + r] + xs[2 * 256 + 128 + r];
-      const float inv = ell_row > 0.f ? 1.f / ell_row : 0.f;
-      T* out = static_cast<T*>(p.out) + (((int64_t)b * p.N + q) * p.Hq + hq) * HD + ch * 64;
+      float ell_row = 0.f;
 #pragma unroll
-      for (int c4 = 0; c4 < 2; ++c4) {
+      for (int k = 0; k < kRowThreads; ++k) ell_row += xs[2 * XS + k * 128 + r];
+      const float inv = ell_row > 0.f ? 1.f / ell_row : 0.f;
+      T* out = static_cast<T*>(p.out) + (((int64_t)b * p.N + q) * p.Hq + hq) * HD + ch * OC;
+#pragma unroll
+      for (int c4 = 0; c4 < OC / 32; ++c4) {
         float ov[32];
-        tmem_ld32(tmem + lane_base + Sh::O_COL + ch * 64 + c4 * 32, ov);
+        tmem_ld32(tmem + lane_base + Sh::O_COL + ch * OC + c4 * 32, ov);
         tmem_wait_ld();
         if (row_ok) {
 #pragma unroll
@@ -348,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <typename T, int BK, bool REL>
+template <typename T, int BK, bool REL, bool CAP>
 int launch_fwd(const AttnParams& a, int dtype, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
   if (int rc = make_map(&mq, a.q, dtype, a.B, a.N, a.Hq, 128)) return rc;
@@ -370,17 +413,17 @@ int launch_fwd(const AttnParams& a, int dtype, cudaStream_t st) {
   p.rl_pad = a.rl_pad;
   p.s = a.s;
   constexpr int smem = FwdShape<BK>::SMEM + (REL ? 2 * 128 * kRunStride * 2 + 256 : 0);
-  auto k = fwd_tc_kernel<T, BK, REL>;
+  auto k = fwd_tc_kernel<T, BK, REL, CAP>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TC_ERR_CUDA;
   k<<<dim3((a.N + BQ - 1) / BQ, a.Hq, a.B), kThreads, smem, st>>>(mq, mk, mv, p);
   return launch_status();
 }
 
-template <typename T>
+template <typename T, bool CAP>
 int fwd_dispatch(const AttnParams& a, int dtype, cudaStream_t st) {
-  if (a.pos_mode == TC_POS_RELATIVE) return launch_fwd<T, 64, true>(a, dtype, st);
-  if (a.tile_n == 64) return launch_fwd<T, 64, false>(a, dtype, st);
-  return launch_fwd<T, 128, false>(a, dtype, st);
+  if (a.pos_mode == TC_POS_RELATIVE) return launch_fwd<T, 64, true, CAP>(a, dtype, st);
+  if (a.tile_n == 64) return launch_fwd<T, 64, false, CAP>(a, dtype, st);
+  return launch_fwd<T, 128, false, CAP>(a, dtype, st);
 }
 
 }  // namespace
@@ -391,8 +434,9 @@ bool tc_supported(const AttnParams& p, int dtype) {
 }
 
 int attn_fwd_tc(const AttnParams& a, int dtype, cudaStream_t st) {
-  if (dtype == TC_BF16) return fwd_dispatch<__nv_bfloat16>(a, dtype, st);
-  return fwd_dispatch<__half>(a, dtype, st);
+  if (dtype == TC_BF16)
+    return a.has_cap ? fwd_dispatch<__nv_bfloat16, true>(a, dtype, st) : fwd_dispatch<__nv_bfloat16, false>(a, dtype, st);
+  return a.has_cap ? fwd_dispatch<__half, true>(a, dtype, st) : fwd_dispatch<__half, false>(a, dtype, st);
 }
 
 }  // namespace tc

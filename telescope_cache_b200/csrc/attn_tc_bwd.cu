@@ -36,6 +36,8 @@ constexpr int kSmemArel = kSmemA + 128 * kDxfStride * 4 + 128 * 3 * 4 + 128 * 4 
 // Pass B: tiles + per-step query info [2][64] (int4) + bias offsets [2][64]
 // (bytes) + barriers; relative adds the staged bias columns [2][64][kColStride]
 constexpr int kColStride = 136;  // 272 B: the 16-byte aligned superset of a 128-node run
+constexpr int HC = 64 / kRowThreads;                     // tile columns per compute thread
+constexpr int kRowsPerWarp = 128 / (kComputeThreads / 32);  // drel write-out rows per compute warp
 constexpr int kSmemB = 2 * T128 + 4 * T64 + 2 * 128 * 128 + 2 * 64 * 16 + 2 * 64 + 256 + 1024;
 constexpr int kSmemBrel = kSmemB + 2 * 64 * kColStride * 2;
 
@@ -224,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                  run_full, run_empty, abort_flag, status);
   } else {
     const int r = (threadIdx.x - 128) & 127;  // query row = TMEM lane
-    const int ch = (threadIdx.x - 128) >> 7;  // node columns [32 ch, 32 ch + 32) of each tile
+    const int ch = (threadIdx.x - 128) >> 7;  // node columns [HC ch, HC ch + HC) of each tile
     const int q = q0 + r;
     const bool row_ok = q < p.N;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
@@ -256,9 +258,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       alive = __all_sync(0xffffffffu, mbar_wait(&s_full[bb], (j >> 1) & 1, abort_flag, status));
       if (!alive) break;
       tc_fence_after();
-      float sv[32], dp[32];
-      tmem_ld32(tmem + lane_base + bb * 64 + ch * 32, sv);
-      tmem_ld32(tmem + lane_base + 128 + bb * 64 + ch * 32, dp);
+      float sv[HC], dp[HC];
+      tmem_ld<HC>(tmem + lane_base + bb * 64 + ch * HC, sv);
+      tmem_ld<HC>(tmem + lane_base + 128 + bb * 64 + ch * HC, dp);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[bb]);
@@ -267,26 +269,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!alive) break;
       }
       const int jlo = lo - it.k0, jhi = hi - it.k0;
-      // column c = 32 ch + cl has bin distance base - k0 - c: run element
-      // 63 - c, i.e. element 31 - cl of this thread's 32-element window
-      uint32_t run[REL ? 16 : 1];
+      // column c = HC ch + cl has bin distance base - k0 - c: run element
+      // 63 - c, i.e. element HC - 1 - cl of this thread's window
+      uint32_t run[REL ? HC / 2 : 1];
       if constexpr (REL) {
         alive = __all_sync(0xffffffffu, mbar_wait(&run_full[bb], (j >> 1) & 1, abort_flag, status));
         if (!alive) break;
-        load_run32(run_s + (bb * 128 + r) * kRunStride, sh_s[bb * 128 + r], ch, run);
+        load_run_part<HC>(run_s + (bb * 128 + r) * kRunStride, sh_s[bb * 128 + r], ch, run);
         mbar_arrive(&run_empty[bb]);
       }
       // the single dX staging tile is free once every warp wrote out the last one
       if (want_drel && j >= 1) named_bar(1, kComputeThreads);
 #pragma unroll
-      for (int cc8 = 0; cc8 < 4; ++cc8) {
-        const int c8 = ch * 4 + cc8;
+      for (int cc8 = 0; cc8 < HC / 8; ++cc8) {
+        const int c8 = ch * (HC / 8) + cc8;
         float dx[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int c = c8 * 8 + i, cl = cc8 * 8 + i;
           float l2, g;
-          sc.logit(sv[cl], REL ? run_elem<T>(run, 31 - cl) : 0.f, p.has_cap, &l2, &g);
+          sc.logit(sv[cl], REL ? run_elem<T>(run, HC - 1 - cl) : 0.f, p.has_cap, &l2, &g);
           const bool valid = c >= jlo && c < jhi;
           const float pr = valid ? exp2_fast(l2 - lse2) : 0.f;
           dx[i] = valid ? pr * (dp[cl] - dlt) * g : 0.f;
@@ -309,11 +311,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           ri[2] = ce;
         }
         named_bar(1, kComputeThreads);
-        const int w8 = warp - 4;  // 16 rows per compute warp
+        const int wc = warp - 4;  // kRowsPerWarp rows per compute warp
         const float* src = dxf;
         const int* inf = rinfo;
-        for (int k = 0; k < 16; ++k) {
-          const int rr = w8 * 16 + k;
+        for (int k = 0; k < kRowsPerWarp; ++k) {
+          const int rr = wc * kRowsPerWarp + k;
           const int n = inf[rr * 3 + 1];
           if (n == 0) continue;
           const int dmin = inf[rr * 3], cend = inf[rr * 3 + 2];
@@ -325,9 +327,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (want_drel) {  // every compute warp reaches this barrier, also after an abort
       // distances at or beyond a row's visible count are never attended: zero them
       named_bar(1, kComputeThreads);
-      const int w8 = warp - 4;
-      for (int k = 0; k < 16; ++k) {
-        const int rr = w8 * 16 + k;
+      const int wc = warp - 4;
+      for (int k = 0; k < kRowsPerWarp; ++k) {
+        const int rr = wc * kRowsPerWarp + k;
         if (q0 + rr >= p.N) break;
         float* dst = p.drel + (((int64_t)b * p.N + q0 + rr) * p.Hq + hq) * p.bins;
         for (int d = mtot[rr] + lane; d < p.bins; d += 32) dst[d] = 0.f;
@@ -336,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (alive && j >= 1) alive = __all_sync(0xffffffffu, mbar_wait(dq_done, 0, abort_flag, status));
     if (alive) {
       tc_fence_after();
-      store_half_row<T>(tmem + lane_base + 256, ch, j >= 1, static_cast<T*>(p.dq) + row * HD, p.scale,
+      store_row_part<T>(tmem + lane_base + 256, ch, j >= 1, static_cast<T*>(p.dq) + row * HD, p.scale,
                         p.rope != 0, p.cos_t, p.sin_t, q, row_ok);
     }
   }
@@ -563,7 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     const int r = (threadIdx.x - 128) & 127;  // node row = TMEM lane
-    const int ch = (threadIdx.x - 128) >> 7;  // query columns [32 ch, 32 ch + 32) of each step
+    const int ch = (threadIdx.x - 128) >> 7;  // query columns [HC ch, HC ch + HC) of each step
     const int jn = k0 + r;                    // level-local node index
     const bool node_ok = r < nk;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
@@ -577,9 +579,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       alive = __all_sync(0xffffffffu, mbar_wait(&s_full[bb], (i >> 1) & 1, abort_flag, status));
       if (!alive) break;
       tc_fence_after();
-      float sv[32], dp[32];
-      tmem_ld32(tmem + lane_base + bb * 64 + ch * 32, sv);
-      tmem_ld32(tmem + lane_base + 128 + bb * 64 + ch * 32, dp);
+      float sv[HC], dp[HC];
+      tmem_ld<HC>(tmem + lane_base + bb * 64 + ch * HC, sv);
+      tmem_ld<HC>(tmem + lane_base + 128 + bb * 64 + ch * HC, dp);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[bb]);
@@ -593,8 +595,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint8_t* bo = bo_s + bb * 64;
       const uint16_t* bcol = bias_s + bb * 64 * kColStride + 127 - r;
 #pragma unroll
-      for (int cc8 = 0; cc8 < 4; ++cc8) {
-        const int c8 = ch * 4 + cc8;
+      for (int cc8 = 0; cc8 < HC / 8; ++cc8) {
+        const int c8 = ch * (HC / 8) + cc8;
         float pr[8], dx[8];
         uint2 bo8 = make_uint2(0u, 0u);
         if constexpr (REL) bo8 = *reinterpret_cast<const uint2*>(bo + c8 * 8);
@@ -627,9 +629,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (alive) {
       tc_fence_after();
       const int64_t orow = ((int64_t)b * (p.s.off[p.s.nl]) + row0 + r) * p.Hkv + hkv;
-      store_half_row<T>(tmem + lane_base + 256, ch, i >= 1, static_cast<T*>(p.dv) + orow * HD, 1.f, false,
+      store_row_part<T>(tmem + lane_base + 256, ch, i >= 1, static_cast<T*>(p.dv) + orow * HD, 1.f, false,
                         nullptr, nullptr, 0, node_ok);
-      store_half_row<T>(tmem + lane_base + 384, ch, i >= 1, static_cast<T*>(p.dk) + orow * HD, p.scale,
+      store_row_part<T>(tmem + lane_base + 384, ch, i >= 1, static_cast<T*>(p.dk) + orow * HD, p.scale,
                         p.rope != 0, p.cos_t, p.sin_t, ((jn + 1) << lev) - 1, node_ok);
     }
   }

@@ -28,6 +28,31 @@ __device__ __forceinline__ float exp2_fast(float x) {
   return y;
 }
 
+// Two fp32 lanes per instruction (sm_100 f32x2 FMA / MUL / ADD) and the
+// three-input maximum.
+__device__ __forceinline__ uint64_t f2_bits(float2 v) { return *reinterpret_cast<uint64_t*>(&v); }
+__device__ __forceinline__ float2 bits_f2(uint64_t u) { return *reinterpret_cast<float2*>(&u); }
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 template <typename T> struct Pack2;
 template <> struct Pack2<__nv_bfloat16> {
   static constexpr int kFmt = 1;
@@ -118,6 +143,19 @@ __device__ __forceinline__ float bits_to_float(uint16_t h) {
   }
 }
 
+// Bias of tile columns (c, c + 1), c even, from word (HC - 2 - c) / 2 of a
+// thread's run window: the window runs backwards in columns, so column c is
+// the high half and column c + 1 the low half.
+template <typename T>
+__device__ __forceinline__ float2 bias_pair(uint32_t w) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return make_float2(__uint_as_float(w & 0xffff0000u), __uint_as_float(w << 16));
+  } else {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    return make_float2(f.y, f.x);
+  }
+}
+
 // Element i (0..63) of a run loaded by load_run64, as float.
 template <typename T>
 __device__ __forceinline__ float run_elem(const uint32_t* run, int i) {
@@ -188,15 +226,18 @@ __device__ __forceinline__ void stage_runs(int t, int q0, int q1, int N, int Hq,
   }
 }
 
-// The 32 run elements [32 (1 - ch), 32 (1 - ch) + 32) of a staged row whose
-// run starts at raw element sh, as 16 packed words (element 2k + 32 (1 - ch)
-// in the low half of word k): 5 aligned 16-byte reads, two select stages
+// The HC run elements [64 - HC (ch + 1), 64 - HC ch) of a staged row whose
+// run starts at raw element sh (the window of the thread owning tile
+// columns [HC ch, HC ch + HC)), as HC / 2 packed words (the window's element
+// 2k in the low half of word k): aligned 16-byte reads, two select stages
 // (whole words) and one funnel shift (half words).
-__device__ __forceinline__ void load_run32(const uint16_t* raw_row, int sh, int ch, uint32_t* out) {
-  const uint4* src = reinterpret_cast<const uint4*>(raw_row) + 4 * (1 - ch);
-  uint32_t w[20];
+template <int HC>
+__device__ __forceinline__ void load_run_part(const uint16_t* raw_row, int sh, int ch, uint32_t* out) {
+  constexpr int NW = HC / 2, NV = (NW + 4 + 3) / 4;  // words needed (+ up to 3 + 1), vectors read
+  const uint4* src = reinterpret_cast<const uint4*>(raw_row) + (64 - HC * (ch + 1)) / 8;
+  uint32_t w[4 * NV];
 #pragma unroll
-  for (int i = 0; i < 5; ++i) {
+  for (int i = 0; i < NV; ++i) {
     const uint4 v = src[i];
     w[4 * i] = v.x;
     w[4 * i + 1] = v.y;
@@ -205,31 +246,35 @@ __device__ __forceinline__ void load_run32(const uint16_t* raw_row, int sh, int 
   }
   const int wo = sh >> 1;
 #pragma unroll
-  for (int i = 0; i < 19; ++i) w[i] = (wo & 1) ? w[i + 1] : w[i];
+  for (int i = 0; i < NW + 3; ++i) w[i] = (wo & 1) ? w[i + 1] : w[i];
 #pragma unroll
-  for (int i = 0; i < 17; ++i) w[i] = (wo & 2) ? w[i + 2] : w[i];
+  for (int i = 0; i < NW + 1; ++i) w[i] = (wo & 2) ? w[i + 2] : w[i];
   const bool odd = sh & 1;
 #pragma unroll
-  for (int k = 0; k < 16; ++k) out[k] = odd ? __funnelshift_r(w[k], w[k + 1], 16) : w[k];
+  for (int k = 0; k < NW; ++k) out[k] = odd ? __funnelshift_r(w[k], w[k + 1], 16) : w[k];
 }
 
-// Compute roles of the tensor-core kernels: two threads per TMEM lane (row),
-// warps 4..11; thread (r, ch) owns columns [half * ch, half * (ch + 1)) of
-// each tile.  Warps w and w + 4 read the same TMEM lanes (32 * (w % 4) ..).
-constexpr int kComputeThreads = 256;
+// Compute roles of the tensor-core kernels: kRowThreads threads per TMEM lane
+// (row), warps 4 .. 4 + 4 kRowThreads - 1; thread (r, ch) owns columns
+// [HC ch, HC ch + HC) of each tile (HC = tile width / kRowThreads).  Warps w,
+// w + 4, ... read the same TMEM lanes (32 (w % 4) ..).
+constexpr int kRowThreads = 4;
+constexpr int kComputeThreads = 128 * kRowThreads;
 constexpr int kThreads = 128 + kComputeThreads;
 
-// Epilogue of a 128-wide fp32 TMEM row split between the row's two threads:
-// this thread owns columns [64 ch, 64 ch + 64).  It loads them (and, for the
-// inverse RoPE, the partner columns c ^ 64), scales by `mul`, rotates by
-// R(-pos) and stores its 64 elements of the 128-wide `out` row when `store`.
-// have = false stores zeros (nothing was accumulated).  Warp-collective.
+// Epilogue of a 128-wide fp32 TMEM row split between the row's kRowThreads
+// threads: this thread owns columns [OC ch, OC ch + OC), OC = 128 /
+// kRowThreads.  It loads them 32 at a time (and, for the inverse RoPE, the
+// partner columns c ^ 64), scales by `mul`, rotates by R(-pos) and stores its
+// elements of the 128-wide `out` row when `store`.  have = false stores zeros
+// (nothing was accumulated).  Warp-collective.
 template <typename T>
-__device__ __forceinline__ void store_half_row(uint32_t taddr, int ch, bool have, T* out, float mul, bool rope,
+__device__ __forceinline__ void store_row_part(uint32_t taddr, int ch, bool have, T* out, float mul, bool rope,
                                                const float* cos_t, const float* sin_t, int pos, bool store) {
+  constexpr int OC = HD / kRowThreads;
 #pragma unroll
-  for (int h2 = 0; h2 < 2; ++h2) {
-    const int c0 = ch * 64 + h2 * 32;
+  for (int h2 = 0; h2 < OC / 32; ++h2) {
+    const int c0 = ch * OC + h2 * 32;
     float a[32], pb[32];
     if (have) {
       ptx::tmem_ld32(taddr + c0, a);
@@ -243,11 +288,12 @@ __device__ __forceinline__ void store_half_row(uint32_t taddr, int ch, bool have
     if (rope && have) {
       const float* cr = cos_t + (int64_t)pos * (HD / 2) + (c0 & 63);
       const float* sr = sin_t + (int64_t)pos * (HD / 2) + (c0 & 63);
+      const bool first = c0 < 64;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const float cc = __ldg(cr + i), ss = __ldg(sr + i);
         // first half: x1 c + x2 s; second half: x2 c - x1 s (x1 = dims < 64)
-        a[i] = ch == 0 ? (a[i] * cc + pb[i] * ss) * mul : (a[i] * cc - pb[i] * ss) * mul;
+        a[i] = first ? (a[i] * cc + pb[i] * ss) * mul : (a[i] * cc - pb[i] * ss) * mul;
       }
     } else {
 #pragma unroll

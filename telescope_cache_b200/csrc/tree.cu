@@ -12,6 +12,8 @@
 // (reference.py:545-584).
 #include "common.cuh"
 
+#include <type_traits>
+
 using namespace tc;
 
 namespace {
@@ -196,6 +198,254 @@ __global__ void __launch_bounds__(kThreads) tree_chunk_kernel(TreeParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Dk = Dv = 128, 16-bit K/V: the HBM-bound fast path.  CTA = 64 tokens of one
+// (batch, KV head); thread (rb, cg) = (tid / 16, tid % 16) owns rows
+// 4 rb .. 4 rb + 3 and dims 8 cg .. 8 cg + 7 of K and V and moves them with
+// 16-byte loads / stores.  Merge levels 1 and 2 stay in the thread; levels
+// 3 .. 6 go through shared memory.  Same arithmetic as tree_chunk_kernel.
+// ---------------------------------------------------------------------------
+constexpr int kChunk128 = 64;
+
+template <typename T>
+__device__ __forceinline__ void unpack8f(const uint4& w, float* f) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      f[2 * i] = __uint_as_float(u[i] << 16);
+      f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+    } else {
+      const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+      f[2 * i] = p.x;
+      f[2 * i + 1] = p.y;
+    }
+  }
+}
+template <typename T>
+__device__ __forceinline__ uint4 pack8f(const float* f) {
+  uint32_t u[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      __nv_bfloat162 v = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      u[i] = *reinterpret_cast<uint32_t*>(&v);
+    } else {
+      __half2 v = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+      u[i] = *reinterpret_cast<uint32_t*>(&v);
+    }
+  }
+  return make_uint4(u[0], u[1], u[2], u[3]);
+}
+
+// parent = round(a0 c0 + (1 - a0) c1) for 8 dims; returns nothing, writes out
+template <typename T>
+__device__ __forceinline__ void merge8(const float* c0, const float* c1, float a0, float* out) {
+#pragma unroll
+  for (int d = 0; d < 8; ++d) out[d] = round_to<T>(a0 * c0[d] + (1.f - a0) * c1[d]);
+}
+
+// alpha0 and the parent log-weight of a child pair (w0, w1)
+template <typename TW>
+__device__ __forceinline__ void pair_weights(float w0, float w1, float* a0, float* wp) {
+  const float m = fmaxf(w0, w1);
+  const float e0 = expf(w0 - m), e1 = expf(w1 - m);
+  *a0 = e0 / (e0 + e1);
+  *wp = round_to<TW>(m + logf(e0 + e1));
+}
+
+template <typename T, typename TW>
+__global__ void __launch_bounds__(kThreads) tree_chunk128_kernel(TreeParams p) {
+  constexpr int D = 128;
+  // shared: raw rows with the conv halo (16-bit), then levels 2.. as fp32
+  extern __shared__ uint4 smem4[];
+  const int c0 = blockIdx.x * kChunk128;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int rows = min(kChunk128, p.N - c0);
+  const int K = p.conv_k, halo = K > 0 ? K - 1 : 0;
+  const int tid = threadIdx.x, rb = tid >> 4, cg = tid & 15;
+  const T* kin = static_cast<const T*>(p.k);
+  const T* vin = static_cast<const T*>(p.v);
+  const auto row_off = [&](int t, int H) { return (((int64_t)b * p.N + t) * H + h) * D; };
+
+  float kx[4][8], vx[4][8];
+  if (K > 0) {
+    // stage rows [c0 - halo, c0 + rows) with 16-byte copies, zeros before t = 0
+    uint4* ks = smem4;                                // [(halo + 64) * 16]
+    uint4* vs = ks + (halo + kChunk128) * 16;
+    const int nvec = (halo + rows) * 16;
+    for (int i = tid; i < nvec; i += kThreads) {
+      const int r = i >> 4, c = i & 15;
+      const int t = c0 - halo + r;
+      uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+      if (t >= 0) {
+        kv = __ldg(reinterpret_cast<const uint4*>(kin + row_off(t, p.Hkv)) + c);
+        vv = __ldg(reinterpret_cast<const uint4*>(vin + row_off(t, p.Hkv)) + c);
+      }
+      ks[i] = kv;
+      vs[i] = vv;
+    }
+    __syncthreads();
+    // causal depthwise conv, fp32 taps (ascending) then the fp32 residual, one rounding
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int d = 0; d < 8; ++d) kx[i][d] = vx[i][d] = 0.f;
+    for (int j = 0; j < K; ++j) {
+      float wk[8], wv[8];
+#pragma unroll
+      for (int d = 0; d < 8; ++d) {
+        const int64_t c = (int64_t)h * D + cg * 8 + d;
+        wk[d] = load_any(p.kcw, c * K + j, p.conv_dtype);
+        wv[d] = load_any(p.vcw, c * K + j, p.conv_dtype);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float xk[8], xv[8];
+        unpack8f<T>(ks[(4 * rb + i + j) * 16 + cg], xk);
+        unpack8f<T>(vs[(4 * rb + i + j) * 16 + cg], xv);
+#pragma unroll
+        for (int d = 0; d < 8; ++d) {
+          kx[i][d] += wk[d] * xk[d];
+          vx[i][d] += wv[d] * xv[d];
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float xk[8], xv[8];
+      unpack8f<T>(ks[(4 * rb + i + halo) * 16 + cg], xk);
+      unpack8f<T>(vs[(4 * rb + i + halo) * 16 + cg], xv);
+#pragma unroll
+      for (int d = 0; d < 8; ++d) {
+        kx[i][d] = round_to<T>(xk[d] + kx[i][d]);
+        vx[i][d] = round_to<T>(xv[d] + vx[i][d]);
+      }
+    }
+    __syncthreads();  // the staging area is reused below
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = 4 * rb + i;
+      uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+      if (r < rows) {
+        kv = __ldg(reinterpret_cast<const uint4*>(kin + row_off(c0 + r, p.Hkv)) + cg);
+        vv = __ldg(reinterpret_cast<const uint4*>(vin + row_off(c0 + r, p.Hkv)) + cg);
+      }
+      unpack8f<T>(kv, kx[i]);
+      unpack8f<T>(vv, vx[i]);
+    }
+  }
+
+  // level-0 weights: precomputed, or logsumexp over the group's queries of
+  // q_e . k / sqrt(Dk) (reduced over the 16 lanes of the row group)
+  const int E = p.Hq / p.Hkv;
+  float w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = 4 * rb + i;
+    const bool ok = r < rows;
+    if (p.w0 != nullptr) {
+      w[i] = ok ? round_to<TW>(to_f(static_cast<const TW*>(p.w0)[((int64_t)b * p.N + c0 + r) * p.Hkv + h])) : 0.f;
+    } else {
+      const T* q = static_cast<const T*>(p.q);
+      float m = -INFINITY, s = 0.f;
+      for (int e = 0; e < E; ++e) {
+        float qf[8];
+        uint4 qv = make_uint4(0u, 0u, 0u, 0u);
+        if (ok) qv = __ldg(reinterpret_cast<const uint4*>(q + (((int64_t)b * p.N + c0 + r) * p.Hq + h * E + e) * D) + cg);
+        unpack8f<T>(qv, qf);
+        float dot = 0.f;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) dot += qf[d] * kx[i][d];
+#pragma unroll
+        for (int o = 8; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        dot *= p.inv_sqrt_dk;
+        const float mn = fmaxf(m, dot);
+        s = s * expf(m - mn) + expf(dot - mn);
+        m = mn;
+      }
+      w[i] = round_to<TW>(m + logf(s));
+    }
+  }
+
+  T* kp = static_cast<T*>(p.kp);
+  T* vp = static_cast<T*>(p.vp);
+  TW* wpk = static_cast<TW*>(p.wp);
+  const auto store_row = [&](int l, int j, const float* kr, const float* vr, float wr) {
+    const int64_t row = ((int64_t)b * p.total + p.off[l] + (c0 >> l) + j) * p.Hkv + h;
+    reinterpret_cast<uint4*>(kp + row * D)[cg] = pack8f<T>(kr);
+    reinterpret_cast<uint4*>(vp + row * D)[cg] = pack8f<T>(vr);
+    if (cg == 0) wpk[row] = from_f<TW>(wr);
+  };
+  // level 0
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (4 * rb + i < rows) store_row(0, 4 * rb + i, kx[i], vx[i], w[i]);
+  const int levels_here = min(6, p.nlev - 1);
+  // levels 1 and 2 inside the thread: rows 4 rb .. 4 rb + 3 -> 2 rb, 2 rb + 1 -> rb
+  int n = rows;
+  float k1[2][8], v1[2][8], w1[2];
+  if (levels_here >= 1) {
+    const int np = n >> 1;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      float a0;
+      pair_weights<TW>(w[2 * i], w[2 * i + 1], &a0, &w1[i]);
+      merge8<T>(kx[2 * i], kx[2 * i + 1], a0, k1[i]);
+      merge8<T>(vx[2 * i], vx[2 * i + 1], a0, v1[i]);
+      if (2 * rb + i < np) store_row(1, 2 * rb + i, k1[i], v1[i], w1[i]);
+    }
+    n = np;
+  }
+  float k2[8], v2[8], w2 = 0.f;
+  if (levels_here >= 2) {
+    const int np = n >> 1;
+    float a0;
+    pair_weights<TW>(w1[0], w1[1], &a0, &w2);
+    merge8<T>(k1[0], k1[1], a0, k2);
+    merge8<T>(v1[0], v1[1], a0, v2);
+    if (rb < np) store_row(2, rb, k2, v2, w2);
+    n = np;
+  }
+  if (levels_here >= 3) {
+    // levels 3 .. 6 through shared memory: ping-pong [2][16 rows][K 128 | V 128] fp32 + w
+    float* buf = reinterpret_cast<float*>(smem4);
+    float* wb = buf + 2 * 16 * 2 * D;
+    const auto kslot = [&](int pp, int j) { return buf + (pp * 16 + j) * 2 * D; };
+#pragma unroll
+    for (int d = 0; d < 8; ++d) {
+      kslot(0, rb)[cg * 8 + d] = k2[d];
+      kslot(0, rb)[D + cg * 8 + d] = v2[d];
+    }
+    if (cg == 0) wb[rb] = w2;
+    int pp = 0;
+    for (int l = 3; l <= levels_here; ++l) {
+      __syncthreads();
+      const int np = n >> 1;
+      const int j = tid >> 4;
+      if (j < np) {
+        const float* ch0 = kslot(pp, 2 * j);
+        const float* ch1 = kslot(pp, 2 * j + 1);
+        float a0, wr, kr[8], vr[8];
+        pair_weights<TW>(wb[pp * 16 + 2 * j], wb[pp * 16 + 2 * j + 1], &a0, &wr);
+        merge8<T>(ch0 + cg * 8, ch1 + cg * 8, a0, kr);
+        merge8<T>(ch0 + D + cg * 8, ch1 + D + cg * 8, a0, vr);
+        float* dst = kslot(pp ^ 1, j);
+#pragma unroll
+        for (int d = 0; d < 8; ++d) {
+          dst[cg * 8 + d] = kr[d];
+          dst[D + cg * 8 + d] = vr[d];
+        }
+        if (cg == 0) wb[(pp ^ 1) * 16 + j] = wr;
+        store_row(l, j, kr, vr, wr);
+      }
+      pp ^= 1;
+      n = np;
+    }
+  }
+}
+
 // Levels deeper than the chunk: parent (l, j) from children (l-1, 2j), (l-1, 2j+1)
 // read back from the packed buffers.  One warp-strided loop per parent row.
 template <typename T, typename TW>
@@ -224,7 +474,34 @@ __global__ void __launch_bounds__(kThreads) tree_level_kernel(TreeParams p, int 
 }
 
 template <typename T, typename TW>
+int launch_tree128(TreeParams& p, cudaStream_t st) {
+  const int halo = p.conv_k > 0 ? p.conv_k - 1 : 0;
+  const size_t stage = (size_t)2 * (halo + kChunk128) * 16 * sizeof(uint4);
+  const size_t levels = sizeof(float) * (2 * 16 * 2 * 128 + 2 * 16);
+  const size_t smem = stage > levels ? stage : levels;
+  auto kern = tree_chunk128_kernel<T, TW>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return TC_ERR_CUDA;
+  dim3 grid((p.N + kChunk128 - 1) / kChunk128, p.Hkv, p.B);
+  kern<<<grid, kThreads, smem, st>>>(p);
+  int rc = launch_status();
+  if (rc) return rc;
+  for (int l = 7; l < p.nlev; ++l) {
+    const int np = p.N >> l;
+    if (np == 0) break;
+    dim3 g2((np + 7) / 8, p.Hkv, p.B);
+    tree_level_kernel<T, TW><<<g2, kThreads, 0, st>>>(p, l);
+    rc = launch_status();
+    if (rc) return rc;
+  }
+  return TC_OK;
+}
+
+template <typename T, typename TW>
 int launch_tree(TreeParams& p, cudaStream_t st) {
+  if constexpr (sizeof(T) == 2) {
+    if (p.Dk == 128 && p.Dv == 128 && p.conv_k <= 8) return launch_tree128<T, TW>(p, st);
+  }
   const int chunk = 1 << p.chunk_log2;
   const int halo = p.conv_k > 0 ? p.conv_k - 1 : 0;
   const size_t smem = sizeof(float) * ((size_t)(halo + chunk) * (p.Dk + p.Dv) + chunk + chunk / 2);

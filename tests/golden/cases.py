@@ -31,6 +31,12 @@ GEOS = {
                       fmap={1: 64, 2: 128, 3: 192}, cache=256),
     "d128_gqa8": dict(B=1, N=512, Hq=8, Hkv=1, Dk=128, Dv=128,
                       fmap={1: 64, 2: 128, 3: 192}, cache=256),
+    # head dim 128 with a ragged last 64-token chunk and odd level lengths
+    "d128_odd": dict(B=2, N=301, Hq=2, Hkv=2, Dk=128, Dv=128,
+                     fmap={1: 64, 2: 128, 3: 192}, cache=256),
+    # eight levels: merges past one 64-token chunk
+    "d128_deep": dict(B=1, N=700, Hq=2, Hkv=2, Dk=128, Dv=128,
+                      fmap={l: 64 * l for l in range(1, 8)}, cache=512),
 }
 
 EMB, D_REL = 32, 6
@@ -67,6 +73,9 @@ CASES = [
     case("tree_conv_four", "tree", "four_levels", conv=3, seed=12),
     case("tree_conv_lin_odd", "tree", "odd_n", conv=4, weights="linear", seed=13),
     case("tree_bf16_d128", "tree", "d128", dtype="bf16", conv=4, seed=14),
+    case("tree_bf16_d128_odd", "tree", "d128_odd", dtype="bf16", conv=3, seed=15),
+    case("tree_lin_d128_odd", "tree", "d128_odd", dtype="bf16", weights="linear", seed=16),
+    case("tree_bf16_d128_deep", "tree", "d128_deep", dtype="bf16", conv=4, seed=17),
     # Phase 2 forward (boundary rows; sink applied post-attention)
     case("fwd_plain_tiny", "fwd", "tiny", seed=100),
     case("fwd_plain_evict", "fwd", "evict", seed=101),
