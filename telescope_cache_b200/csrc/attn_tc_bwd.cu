@@ -29,16 +29,17 @@ constexpr int T64 = 64 * 128 * 2;    // [64 rows x 128] tile
 constexpr int B128 = 128 * 128;      // one 64-col block of a 128-row tile
 constexpr int B64 = 64 * 128;        // one 64-col block of a 64-row tile
 constexpr int kSmemA = 2 * T128 + 4 * T64 + 128 * 128 + 1024 + 256;
-// relative Pass A: + an fp32 dX staging tile [128 x 65], per-row run info,
+// relative Pass A: + an fp32 dX staging tile [128 x 66], per-row run info,
 // row totals and the double-buffered bias runs [2][128][kRunStride]
-constexpr int kDxfStride = 65;
+constexpr int kDxfStride = 66;  // even: 8-byte column pairs; 16 rows per phase hit distinct banks
 constexpr int kSmemArel = kSmemA + 128 * kDxfStride * 4 + 128 * 3 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2 + 256;
-// Pass B: tiles + per-step query info [2][64] (int4) + bias offsets [2][64]
-// (bytes) + barriers; relative adds the staged bias columns [2][64][kColStride]
+// Pass B: tiles + per-step query info [2][64] x {lo, hi, -lse2, -Delta} + the
+// per-warp interior flags [2][2] + bias offsets [2][64] (bytes) + barriers;
+// relative adds the staged bias columns [2][64][kColStride]
 constexpr int kColStride = 136;  // 272 B: the 16-byte aligned superset of a 128-node run
 constexpr int HC = 64 / kRowThreads;                     // tile columns per compute thread
 constexpr int kRowsPerWarp = 128 / (kComputeThreads / 32);  // drel write-out rows per compute warp
-constexpr int kSmemB = 2 * T128 + 4 * T64 + 2 * 128 * 128 + 2 * 64 * 16 + 2 * 64 + 256 + 1024;
+constexpr int kSmemB = 2 * T128 + 4 * T64 + 2 * 128 * 128 + 2 * 64 * 16 + 16 + 2 * 64 + 256 + 1024;
 constexpr int kSmemBrel = kSmemB + 2 * 64 * kColStride * 2;
 
 struct BwdParams {
@@ -83,10 +84,33 @@ struct BwdScalars {
   }
 };
 
+// dX = P (dP - Delta) softcap' for two columns, with P = exp2(logit2 - lse2):
+// y = s * kq + bias * kb (bias 0 without REL); with the softcap t = tanh(y),
+// logit2 = t * kc and softcap' = 1 - t^2, else logit2 = y.  nl2 = -lse2 and
+// nd = -Delta per column.  Returns P in *pr and dX.
+template <bool REL, bool CAP>
+__device__ __forceinline__ float2 dx_pair(float2 s, float2 bias, float2 dp, float2 nl2, float2 nd, float kq, float kb,
+                                          float kc, float2* pr) {
+  float2 y = REL ? ffma2(s, make_float2(kq, kq), fmul2(bias, make_float2(kb, kb))) : fmul2(s, make_float2(kq, kq));
+  float2 a, g = make_float2(1.f, 1.f);
+  if constexpr (CAP) {
+    const float2 t = make_float2(tanh_fast(y.x), tanh_fast(y.y));
+    a = ffma2(t, make_float2(kc, kc), nl2);
+    g = fsub2(g, fmul2(t, t));
+  } else {
+    a = fadd2(y, nl2);
+  }
+  const float2 p = make_float2(exp2_fast(a.x), exp2_fast(a.y));
+  *pr = p;
+  float2 v = fmul2(p, fadd2(dp, nd));
+  if constexpr (CAP) v = fmul2(v, g);
+  return v;
+}
+
 // ---------------------------------------------------------------------------
 // Pass A
 // ---------------------------------------------------------------------------
-template <typename T, bool REL>
+template <typename T, bool REL, bool CAP>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmg,
                      const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, BwdParams p) {
@@ -280,22 +304,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // the single dX staging tile is free once every warp wrote out the last one
       if (want_drel && j >= 1) named_bar(1, kComputeThreads);
+      const int ljlo = jlo - ch * HC, ljhi = jhi - ch * HC;  // this thread's columns
+      const bool interior = __all_sync(0xffffffffu, ljlo <= 0 && ljhi >= HC);
+      const float2 nl2 = make_float2(-lse2, -lse2), nd = make_float2(-dlt, -dlt);
+      float dx[HC];
 #pragma unroll
-      for (int cc8 = 0; cc8 < HC / 8; ++cc8) {
-        const int c8 = ch * (HC / 8) + cc8;
-        float dx[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int c = c8 * 8 + i, cl = cc8 * 8 + i;
-          float l2, g;
-          sc.logit(sv[cl], REL ? run_elem<T>(run, HC - 1 - cl) : 0.f, p.has_cap, &l2, &g);
-          const bool valid = c >= jlo && c < jhi;
-          const float pr = valid ? exp2_fast(l2 - lse2) : 0.f;
-          dx[i] = valid ? pr * (dp[cl] - dlt) * g : 0.f;
-          if (want_drel) dxf[r * kDxfStride + c] = dx[i];
+      for (int c = 0; c < HC; c += 2) {
+        const float2 bias = REL ? bias_pair<T>(run[(HC - 2 - c) / 2]) : make_float2(0.f, 0.f);
+        float2 pr;
+        float2 v = dx_pair<REL, CAP>(make_float2(sv[c], sv[c + 1]), bias, make_float2(dp[c], dp[c + 1]), nl2, nd,
+                                     sc.kq, sc.kb, sc.kc, &pr);
+        if (!interior) {
+          v.x = (c >= ljlo && c < ljhi) ? v.x : 0.f;
+          v.y = (c + 1 >= ljlo && c + 1 < ljhi) ? v.y : 0.f;
         }
-        *reinterpret_cast<uint4*>(x_s + sw128_offset(r, c8 * 8, 128)) = pack8<T>(dx, 1.f);
+        dx[c] = v.x;
+        dx[c + 1] = v.y;
+        if (want_drel) *reinterpret_cast<float2*>(dxf + r * kDxfStride + ch * HC + c) = v;
       }
+#pragma unroll
+      for (int cc8 = 0; cc8 < HC / 8; ++cc8)
+        *reinterpret_cast<uint4*>(x_s + sw128_offset(r, (ch * (HC / 8) + cc8) * 8, 128)) = pack8<T>(dx + cc8 * 8, 1.f);
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(x_full);
@@ -372,7 +401,7 @@ struct QSteps {
   }
 };
 
-template <typename T, bool REL>
+template <typename T, bool REL, bool CAP>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmg,
                       const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
@@ -385,9 +414,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* g_s = q_s + 2 * T64;
   uint8_t* pt_s = g_s + 2 * T64;  // P^T  [128 x 64]
   uint8_t* xt_s = pt_s + 128 * 128;  // dX^T [128 x 64]
-  // per step (double buffered), per query column: {lo, hi, lse * log2e, Delta}
-  int4* info_s = reinterpret_cast<int4*>(xt_s + 128 * 128);  // [2][64]
-  uint8_t* bo_s = reinterpret_cast<uint8_t*>(info_s + 2 * 64);  // [2][64] relative: run offset - 127
+  // per step (double buffered), per query column: lo, hi, -lse * log2e, -Delta
+  int* lo_s = reinterpret_cast<int*>(xt_s + 128 * 128);  // [2][64]
+  int* hi_s = lo_s + 2 * 64;
+  float* nl_s = reinterpret_cast<float*>(hi_s + 2 * 64);
+  float* nd_s = nl_s + 2 * 64;
+  int* in_s = reinterpret_cast<int*>(nd_s + 2 * 64);         // [2][2]: every node of the tile visible to every
+                                                             // query of staging warp 2 / 3's 32 columns
+  uint8_t* bo_s = reinterpret_cast<uint8_t*>(in_s + 4);      // [2][64] relative: run offset - 127
   uint64_t* bars = reinterpret_cast<uint64_t*>(bo_s + 2 * 64);
   uint64_t* kv_full = bars;
   uint64_t* q_full = bars + 1;
@@ -543,7 +577,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         dl = p.delta[row];
       }
       const int ci = buf * 64 + t;
-      info_s[ci] = make_int4(lo, hi, __float_as_int(l2), __float_as_int(dl));
+      lo_s[ci] = lo;
+      hi_s[ci] = hi;
+      nl_s[ci] = -l2;
+      nd_s[ci] = -dl;
+      const bool all_in = __all_sync(0xffffffffu, nk == 128 && lo <= k0 && hi >= k0 + 128);
+      if (lane == 0) in_s[buf * 2 + (t >> 5)] = all_in;
       if constexpr (REL) {
         // nodes k0 + r see distance base - k0 - r: one descending run of 128
         // elements ending at rl[row, pad + base - k0]; some node of the tile
@@ -591,34 +630,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       alive = __all_sync(0xffffffffu, mbar_wait(&info_full[bb], (i >> 1) & 1, abort_flag, status));
       if (!alive) break;
-      const int4* inf = info_s + bb * 64;
       const uint8_t* bo = bo_s + bb * 64;
       const uint16_t* bcol = bias_s + bb * 64 * kColStride + 127 - r;
+      const bool interior = in_s[bb * 2 + ((ch * HC) >> 5)] != 0;
+      float pr[HC], dx[HC];
+#pragma unroll
+      for (int cl = 0; cl < HC; cl += 2) {
+        const int c = ch * HC + cl;
+        float2 bias = make_float2(0.f, 0.f);
+        if constexpr (REL) {
+          // lanes hold consecutive nodes: consecutive (descending) halves
+          bias.x = bits_to_float<T>(bcol[c * kColStride + bo[c]]);
+          bias.y = bits_to_float<T>(bcol[(c + 1) * kColStride + bo[c + 1]]);
+        }
+        const float2 nl2 = *reinterpret_cast<const float2*>(nl_s + bb * 64 + c);
+        const float2 nd = *reinterpret_cast<const float2*>(nd_s + bb * 64 + c);
+        float2 p2;
+        float2 v = dx_pair<REL, CAP>(make_float2(sv[cl], sv[cl + 1]), bias, make_float2(dp[cl], dp[cl + 1]), nl2,
+                                     nd, sc.kq, sc.kb, sc.kc, &p2);
+        if (!interior) {
+          const bool v0 = node_ok && jn >= lo_s[bb * 64 + c] && jn < hi_s[bb * 64 + c];
+          const bool v1 = node_ok && jn >= lo_s[bb * 64 + c + 1] && jn < hi_s[bb * 64 + c + 1];
+          p2.x = v0 ? p2.x : 0.f;
+          p2.y = v1 ? p2.y : 0.f;
+          v.x = v0 ? v.x : 0.f;
+          v.y = v1 ? v.y : 0.f;
+        }
+        pr[cl] = p2.x;
+        pr[cl + 1] = p2.y;
+        dx[cl] = v.x;
+        dx[cl + 1] = v.y;
+      }
 #pragma unroll
       for (int cc8 = 0; cc8 < HC / 8; ++cc8) {
-        const int c8 = ch * (HC / 8) + cc8;
-        float pr[8], dx[8];
-        uint2 bo8 = make_uint2(0u, 0u);
-        if constexpr (REL) bo8 = *reinterpret_cast<const uint2*>(bo + c8 * 8);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int c = c8 * 8 + k, cl = cc8 * 8 + k;
-          const int4 ci = inf[c];
-          const bool valid = node_ok && jn >= ci.x && jn < ci.y;
-          float bias = 0.f;
-          if constexpr (REL) {
-            // lanes hold consecutive nodes: consecutive (descending) halves
-            const uint32_t o = ((k < 4 ? bo8.x : bo8.y) >> (8 * (k & 3))) & 0xffu;
-            bias = bits_to_float<T>(bcol[c * kColStride + o]);
-          }
-          float l2, g;
-          sc.logit(sv[cl], bias, p.has_cap, &l2, &g);
-          pr[k] = valid ? exp2_fast(l2 - __int_as_float(ci.z)) : 0.f;
-          dx[k] = valid ? pr[k] * (dp[cl] - __int_as_float(ci.w)) * g : 0.f;
-        }
-        const uint32_t off = sw128_offset(r, c8 * 8, 128);
-        *reinterpret_cast<uint4*>(pt_s + off) = pack8<T>(pr, 1.f);
-        *reinterpret_cast<uint4*>(xt_s + off) = pack8<T>(dx, 1.f);
+        const uint32_t off = sw128_offset(r, (ch * (HC / 8) + cc8) * 8, 128);
+        *reinterpret_cast<uint4*>(pt_s + off) = pack8<T>(pr + cc8 * 8, 1.f);
+        *reinterpret_cast<uint4*>(xt_s + off) = pack8<T>(dx + cc8 * 8, 1.f);
       }
       mbar_arrive(&info_empty[bb]);
       fence_async_smem();
@@ -644,7 +691,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <typename T, bool REL>
+template <typename T, bool REL, bool CAP>
 int launch_bwd(const AttnParams& a, int dtype, cudaStream_t st) {
   CUtensorMap mq128, mg128, mk64, mv64, mq64, mg64, mk128, mv128;
   if (int rc = make_map(&mq128, a.q, dtype, a.B, a.N, a.Hq, 128)) return rc;
@@ -682,14 +729,14 @@ int launch_bwd(const AttnParams& a, int dtype, cudaStream_t st) {
   for (int l = 0; l < TC_MAX_LEVELS; ++l)
     p.tiles[l + 1] = p.tiles[l] + (l < a.s.nl ? (a.s.len[l] + 127) / 128 : 0);
   if (int rc = delta_launch(a, dtype, st)) return rc;
-  auto ka = bwd_dq_tc_kernel<T, REL>;
+  auto ka = bwd_dq_tc_kernel<T, REL, CAP>;
   constexpr int smem_a = REL ? kSmemArel : kSmemA;
   if (cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_a) != cudaSuccess) return TC_ERR_CUDA;
   ka<<<dim3((a.N + 127) / 128, a.Hq, a.B), kThreads, smem_a, st>>>(mq128, mg128, mk64, mv64, p);
   if (int rc = launch_status()) return rc;
   const int ntiles = p.tiles[a.s.nl];
   if (ntiles > 0) {
-    auto kb = bwd_dkv_tc_kernel<T, REL>;
+    auto kb = bwd_dkv_tc_kernel<T, REL, CAP>;
     constexpr int smem_b = REL ? kSmemBrel : kSmemB;
     if (cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_b) != cudaSuccess)
       return TC_ERR_CUDA;
@@ -706,11 +753,16 @@ bool tc_bwd_supported(const AttnParams& p, int dtype) {
          (p.pos_mode != TC_POS_RELATIVE || p.rl != nullptr);
 }
 
-int attn_bwd_tc(const AttnParams& a, int dtype, cudaStream_t st) {
+template <typename T>
+int bwd_dispatch(const AttnParams& a, int dtype, cudaStream_t st) {
   const bool rel = a.pos_mode == TC_POS_RELATIVE;
-  if (dtype == TC_BF16)
-    return rel ? launch_bwd<__nv_bfloat16, true>(a, dtype, st) : launch_bwd<__nv_bfloat16, false>(a, dtype, st);
-  return rel ? launch_bwd<__half, true>(a, dtype, st) : launch_bwd<__half, false>(a, dtype, st);
+  if (a.has_cap) return rel ? launch_bwd<T, true, true>(a, dtype, st) : launch_bwd<T, false, true>(a, dtype, st);
+  return rel ? launch_bwd<T, true, false>(a, dtype, st) : launch_bwd<T, false, false>(a, dtype, st);
+}
+
+int attn_bwd_tc(const AttnParams& a, int dtype, cudaStream_t st) {
+  if (dtype == TC_BF16) return bwd_dispatch<__nv_bfloat16>(a, dtype, st);
+  return bwd_dispatch<__half>(a, dtype, st);
 }
 
 }  // namespace tc
