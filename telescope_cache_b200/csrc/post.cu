@@ -3,6 +3,8 @@
 // reference's mixed-precision graph: fp32 math, casts where it casts.
 #include "common.cuh"
 
+#include <type_traits>
+
 using namespace tc;
 
 namespace {
@@ -68,6 +70,131 @@ __global__ void sink_bwd_kernel(int64_t rows, int Hq, int Dv, const T* out, cons
 #pragma unroll
   for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
   if (lane == 0) dlse[w] = round_to<T>(dot) * r * (1.f - r);
+}
+
+// ---------------------------------------------------------------------------
+// Vectorised variants for 16-bit tensors (8 elements per thread, 16-byte
+// loads and stores); the same arithmetic as the scalar kernels above.
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ void ld8(const T* p, float* f) {
+  const uint4 w = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      f[2 * i] = __uint_as_float(u[i] << 16);
+      f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+    } else {
+      const float2 p2 = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+      f[2 * i] = p2.x;
+      f[2 * i + 1] = p2.y;
+    }
+  }
+}
+template <typename T>
+__device__ __forceinline__ void st8(T* p, const float* f) {
+  uint32_t u[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      __nv_bfloat162 v = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      u[i] = *reinterpret_cast<uint32_t*>(&v);
+    } else {
+      __half2 v = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+      u[i] = *reinterpret_cast<uint32_t*>(&v);
+    }
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(u[0], u[1], u[2], u[3]);
+}
+
+// RoPE: thread = (row, dims ii .. ii + 7 of the first half and their partners)
+template <typename T>
+__global__ void rope_vec_kernel(int64_t rows, int H, int D, const T* x, T* y, const float* cos_t,
+                                const float* sin_t, int kind, Sched s, int64_t S, const int32_t* positions,
+                                int inverse) {
+  const int hd = D / 2, per = hd / 8;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= rows * H * per) return;
+  const int64_t rowh = t / per;
+  const int ii = (int)(t - rowh * per) * 8;
+  const int64_t srow = (rowh / H) % S;
+  int pos;
+  if (kind == 0) {
+    pos = (int)srow;
+  } else if (kind == 2) {
+    pos = positions[rowh];
+  } else {
+    int l = 0;
+    while (l + 1 < s.nl && srow >= s.off[l + 1]) ++l;
+    pos = (((int)(srow - s.off[l]) + 1) << l) - 1;
+  }
+  float x1[8], x2[8], o1[8], o2[8];
+  ld8<T>(x + rowh * D + ii, x1);
+  ld8<T>(x + rowh * D + ii + hd, x2);
+  const float4* cr = reinterpret_cast<const float4*>(cos_t + (int64_t)pos * hd + ii);
+  const float4* sr = reinterpret_cast<const float4*>(sin_t + (int64_t)pos * hd + ii);
+  const float4 c0 = __ldg(cr), c1 = __ldg(cr + 1), s0 = __ldg(sr), s1 = __ldg(sr + 1);
+  const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  const float sg = inverse ? -1.f : 1.f;
+  const float sn[8] = {sg * s0.x, sg * s0.y, sg * s0.z, sg * s0.w, sg * s1.x, sg * s1.y, sg * s1.z, sg * s1.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    o1[i] = x1[i] * cs[i] - x2[i] * sn[i];
+    o2[i] = x2[i] * cs[i] + x1[i] * sn[i];
+  }
+  st8<T>(y + rowh * D + ii, o1);
+  st8<T>(y + rowh * D + ii + hd, o2);
+}
+
+// sink forward: thread = 8 consecutive elements of one (row, head)
+template <typename T>
+__global__ void sink_fwd_vec_kernel(int64_t rows, int Hq, int Dv, const T* out, const float* lse, int sdt,
+                                    const void* sinks, T* y) {
+  const int per = Dv / 8;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= rows * Hq * per) return;
+  const int64_t rh = t / per;
+  const int h = (int)(rh % Hq);
+  const float r = round_to<T>(1.f / (1.f + expf(-(lse[rh] - load_any(sinks, h, sdt)))));
+  float v[8];
+  ld8<T>(out + t * 8, v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] *= r;
+  st8<T>(y + t * 8, v);
+}
+
+// sink backward: G = Dv / 8 (a power of two <= 32) threads per (row, head)
+template <typename T>
+__global__ void sink_bwd_vec_kernel(int64_t rows, int Hq, int Dv, const T* out, const float* lse, int sdt,
+                                    const void* sinks, const T* g, T* gpre, float* dlse) {
+  const int G = Dv / 8;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t w = t / G;
+  const bool ok = w < rows * Hq;
+  float r = 0.f, dot = 0.f;
+  if (ok) {
+    const int h = (int)(w % Hq);
+    r = 1.f / (1.f + expf(-(lse[w] - load_any(sinks, h, sdt))));
+    const float rt = round_to<T>(r);
+    float gv[8], ov[8], pv[8];
+    ld8<T>(g + t * 8, gv);
+    ld8<T>(out + t * 8, ov);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      pv[i] = gv[i] * rt;
+      dot += gv[i] * ov[i];
+    }
+    st8<T>(gpre + t * 8, pv);
+  }
+  for (int o = G / 2; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+  if (ok && (t % G) == 0) dlse[w] = round_to<T>(dot) * r * (1.f - r);
+}
+
+inline bool aligned16() { return true; }
+template <typename P, typename... R>
+inline bool aligned16(P p, R... rest) {
+  return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && aligned16(rest...);
 }
 
 // dsinks[h] = -sum over rows of dlse[row, h]: one block per head, fixed order.
@@ -177,10 +304,17 @@ extern "C" int tc_rope_apply(int32_t B, int64_t S, int32_t H, int32_t D, int32_t
   }
   const int64_t rows = (int64_t)B * S;
   const int64_t n = rows * H * D;
+  const bool vec = (D / 2) % 8 == 0 && aligned16(x, y, cos_t, sin_t);
   TC_DISPATCH(dtype, T, {
-    rope_kernel<T><<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
-        rows, H, D, static_cast<const T*>(x), static_cast<T*>(y), cos_t, sin_t, pos_kind, s, S, positions,
-        inverse);
+    if (sizeof(T) == 2 && vec) {
+      rope_vec_kernel<T><<<blocks_for(n / 16, 256), 256, 0, (cudaStream_t)stream>>>(
+          rows, H, D, static_cast<const T*>(x), static_cast<T*>(y), cos_t, sin_t, pos_kind, s, S, positions,
+          inverse);
+    } else {
+      rope_kernel<T><<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
+          rows, H, D, static_cast<const T*>(x), static_cast<T*>(y), cos_t, sin_t, pos_kind, s, S, positions,
+          inverse);
+    }
   });
   return launch_status();
 }
@@ -191,8 +325,13 @@ extern "C" int tc_sink_fwd(int64_t rows, int32_t Hq, int32_t Dv, int32_t dtype, 
   const int64_t n = rows * Hq * Dv;
   if (n == 0) return TC_OK;
   TC_DISPATCH(dtype, T, {
-    sink_fwd_kernel<T><<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
-        rows, Hq, Dv, static_cast<const T*>(out), lse, sink_dtype, sinks, static_cast<T*>(y));
+    if (sizeof(T) == 2 && Dv % 8 == 0 && aligned16(out, y)) {
+      sink_fwd_vec_kernel<T><<<blocks_for(n / 8, 256), 256, 0, (cudaStream_t)stream>>>(
+          rows, Hq, Dv, static_cast<const T*>(out), lse, sink_dtype, sinks, static_cast<T*>(y));
+    } else {
+      sink_fwd_kernel<T><<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
+          rows, Hq, Dv, static_cast<const T*>(out), lse, sink_dtype, sinks, static_cast<T*>(y));
+    }
   });
   return launch_status();
 }
@@ -205,10 +344,18 @@ extern "C" int tc_sink_bwd(int64_t rows, int32_t Hq, int32_t Dv, int32_t dtype, 
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t warps = rows * Hq;
   if (warps > 0) {
+    const int G = Dv / 8;
+    const bool vec = Dv % 8 == 0 && G <= 32 && (G & (G - 1)) == 0 && aligned16(out, dout, dout_pre);
     TC_DISPATCH(dtype, T, {
-      sink_bwd_kernel<T><<<blocks_for(warps * 32, 256), 256, 0, st>>>(
-          rows, Hq, Dv, static_cast<const T*>(out), lse, sink_dtype, sinks, static_cast<const T*>(dout),
-          static_cast<T*>(dout_pre), dlse);
+      if (sizeof(T) == 2 && vec) {
+        sink_bwd_vec_kernel<T><<<blocks_for(warps * G, 256), 256, 0, st>>>(
+            rows, Hq, Dv, static_cast<const T*>(out), lse, sink_dtype, sinks, static_cast<const T*>(dout),
+            static_cast<T*>(dout_pre), dlse);
+      } else {
+        sink_bwd_kernel<T><<<blocks_for(warps * 32, 256), 256, 0, st>>>(
+            rows, Hq, Dv, static_cast<const T*>(out), lse, sink_dtype, sinks, static_cast<const T*>(dout),
+            static_cast<T*>(dout_pre), dlse);
+      }
     });
     if (int rc = launch_status()) return rc;
   }
