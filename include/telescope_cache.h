@@ -283,6 +283,8 @@ int tc_gate_apply(int64_t n, int32_t dtype, const void* out, int32_t g_dtype, co
 /* decode step modes */
 #define TC_DECODE_FULL 0     /* advance the state, then attend (decode_step)  */
 #define TC_DECODE_ADVANCE 1  /* advance only (advance_decode_state)           */
+#define TC_DECODE_ROTATE 3   /* rebuild ring_k_rot: every node visible to query t,
+                                rotated at its summary position (rope)      */
 #define TC_DECODE_ATTEND 2   /* attend only, state untouched
                                 (multilevel_attention_decode)                 */
 
@@ -324,6 +326,17 @@ typedef struct tc_decode_args {
   float* lse;                /* [B, Hq] pre-sink                           */
   void* k_new;               /* [B, Hkv, Dk] post-conv key as stored, or NULL */
   void* v_new;               /* [B, Hkv, Dv] */
+  /* Optional fp32 scratch for splitting each (batch, KV head)'s visible
+   * entries over several CTAs (Dk = Dv = 128, 16-bit rings): at least
+   * B * Hkv * 8 * (Hq / Hkv) * 130 floats.  NULL (or smaller) runs the step
+   * unsplit in one launch. */
+  float* workspace;
+  int64_t workspace_floats;
+  /* rope: [B, sum(caps), Hkv, Dk] copies of the ring keys rotated at their
+   * summary positions, or NULL.  Given, FULL / ADVANCE also write the rotated
+   * copies of the rows they create and the attention reads them instead of
+   * rotating every visible key; ROTATE rebuilds it from ring_k. */
+  void* ring_k_rot;
 } tc_decode_args;
 
 /* One fused decode step for token t: short_conv_step, merge weight, the

@@ -18,7 +18,7 @@ MAX_LEVELS = 16
 TC_OK, TC_ERR_ARG, TC_ERR_UNSUPPORTED, TC_ERR_CUDA, TC_ERR_SCHEDULE = 0, 1, 2, 3, 4
 TC_F32, TC_BF16, TC_F16 = 0, 1, 2
 POS = {"none": 0, "rope": 1, "relative": 2}
-DECODE_FULL, DECODE_ADVANCE, DECODE_ATTEND = 0, 1, 2
+DECODE_FULL, DECODE_ADVANCE, DECODE_ATTEND, DECODE_ROTATE = 0, 1, 2, 3
 
 _c_i32, _c_i64, _c_f32, _c_vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -68,7 +68,8 @@ class DecodeArgs(ctypes.Structure):
         ("rope_cos", _c_vp), ("rope_sin", _c_vp), ("rel_states", _c_vp), ("rel_proj", _c_vp),
         ("rel_dtype", _c_i32), ("d_rel", _c_i32), ("rel_bins", _c_i32), ("sinks", _c_vp),
         ("sink_dtype", _c_i32), ("gate_pre", _c_vp), ("gate_dtype", _c_i32), ("out", _c_vp),
-        ("lse", _c_vp), ("k_new", _c_vp), ("v_new", _c_vp),
+        ("lse", _c_vp), ("k_new", _c_vp), ("v_new", _c_vp), ("workspace", _c_vp),
+        ("workspace_floats", _c_i64), ("ring_k_rot", _c_vp),
     ]
 
 

@@ -132,6 +132,20 @@ __device__ bool decode_prologue(const DecParams& P, DecShared<DM>& S) {
       break;
     }
   }
+  // rope with a rotated-key ring: the rows this step creates also go there,
+  // rotated at their summary positions (reference.py:219-302)
+  const bool krot = advance && a.ring_k_rot != nullptr && a.position_mode == TC_POS_ROPE;
+  T* rkr = static_cast<T*>(a.ring_k_rot);
+  const auto put_rotated = [&](int slot, const float* row, int pos) {
+    const int hd = a.Dk / 2;
+    for (int i = tid; i < hd; i += NT) {
+      const float c = a.rope_cos[(int64_t)pos * hd + i], s = a.rope_sin[(int64_t)pos * hd + i];
+      const float x1 = row[i], x2 = row[i + hd];
+      rkr[kidx(slot, i)] = from_f<T>(x1 * c - x2 * s);
+      rkr[kidx(slot, i + hd)] = from_f<T>(x2 * c + x1 * s);
+    }
+  };
+  float* mrow = S.wbuf[0];  // the merged parent key
   if (fired > 0) {
     const int l = fired;
     const int c0 = ring_slot(l - 1, 2 * jn), c1 = ring_slot(l - 1, 2 * jn + 1), par = ring_slot(l, jn);
@@ -139,19 +153,24 @@ __device__ bool decode_prologue(const DecParams& P, DecShared<DM>& S) {
     const float m = fmaxf(w0, w1);
     const float e0 = expf(w0 - m), e1 = expf(w1 - m);
     const float a0 = e0 / (e0 + e1), a1 = e1 / (e0 + e1);
-    for (int d = tid; d < a.Dk; d += NT)
-      rk[kidx(par, d)] = from_f<T>(a0 * to_f(rk[kidx(c0, d)]) + a1 * to_f(rk[kidx(c1, d)]));
+    for (int d = tid; d < a.Dk; d += NT) {
+      const float x = round_to<T>(a0 * to_f(rk[kidx(c0, d)]) + a1 * to_f(rk[kidx(c1, d)]));
+      rk[kidx(par, d)] = from_f<T>(x);
+      mrow[d] = x;
+    }
     for (int d = tid; d < a.Dv; d += NT)
       rv[vidx(par, d)] = from_f<T>(a0 * to_f(rv[vidx(c0, d)]) + a1 * to_f(rv[vidx(c1, d)]));
     if (tid == 0) store_any(a.ring_w, widx(par), a.w_dtype, m + logf(e0 + e1));
   }
   __syncthreads();
+  if (krot && fired > 0) put_rotated(ring_slot(fired, jn), mrow, ((jn + 1) << fired) - 1);
   // 4. token t at level 0, after the merge (its slot may be a merged child's)
   if (advance) {
     const int s0 = ring_slot(0, t);
     for (int d = tid; d < a.Dk; d += NT) rk[kidx(s0, d)] = from_f<T>(S.kt[d]);
     for (int d = tid; d < a.Dv; d += NT) rv[vidx(s0, d)] = from_f<T>(S.vt[d]);
     if (tid == 0) store_any(a.ring_w, widx(s0), a.w_dtype, S.w_new);
+    if (krot) put_rotated(s0, S.kt, t);
   }
   if (!attend) return false;
   // visible ranges of query t and the rotated query rows
@@ -194,24 +213,14 @@ __device__ bool decode_prologue(const DecParams& P, DecShared<DM>& S) {
   return true;
 }
 
-// Merge the warps' partial softmax states (part_m / part_l / part_acc), then
-// the sink, the gate and the stores of out and the pre-sink lse.
-template <typename T, int DM>
-__device__ void decode_epilogue(const DecParams& P, DecShared<DM>& S) {
-  const tc_decode_args& a = P.a;
-  const int b = blockIdx.x, h = blockIdx.y;
+// One output element from the merged softmax state (max mx, sum ls,
+// accumulator o): the sink, the gate, and the stores of out and the pre-sink lse.
+template <typename T>
+__device__ __forceinline__ void finish_elem(const tc_decode_args& a, int b, int h, int e, int d, float mx, float ls,
+                                            float o) {
   const int E = a.Hq / a.Hkv;
   T* out = static_cast<T*>(a.out);
-  for (int i = threadIdx.x; i < E * a.Dv; i += NT) {
-    const int e = i / a.Dv, d = i - e * a.Dv;
-    float mx = -INFINITY;
-    for (int w = 0; w < NW; ++w) mx = fmaxf(mx, S.part_m[w][e]);
-    float ls = 0.f, o = 0.f;
-    for (int w = 0; w < NW; ++w) {
-      const float f = S.part_m[w][e] == -INFINITY ? 0.f : expf(S.part_m[w][e] - mx);
-      ls += S.part_l[w][e] * f;
-      o += S.part_acc[w][e][d] * f;
-    }
+  {
     const int hq = h * E + e;
     float y = round_to<T>(o / ls);
     const float lse = mx + logf(ls);
@@ -228,6 +237,61 @@ __device__ void decode_epilogue(const DecParams& P, DecShared<DM>& S) {
   }
 }
 
+// Merge the warps' partial softmax states (part_m / part_l / part_acc).  With
+// one CTA per (batch, KV head) it finishes the outputs; a split CTA writes
+// its merged state {m, l, acc[Dv]} to the workspace slot (b, h, split, e).
+template <typename T, int DM>
+__device__ void decode_epilogue(const DecParams& P, DecShared<DM>& S) {
+  const tc_decode_args& a = P.a;
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int E = a.Hq / a.Hkv;
+  const bool split = gridDim.z > 1;
+  for (int i = threadIdx.x; i < E * a.Dv; i += NT) {
+    const int e = i / a.Dv, d = i - e * a.Dv;
+    float mx = -INFINITY;
+    for (int w = 0; w < NW; ++w) mx = fmaxf(mx, S.part_m[w][e]);
+    float ls = 0.f, o = 0.f;
+    for (int w = 0; w < NW; ++w) {
+      const float f = S.part_m[w][e] == -INFINITY ? 0.f : expf(S.part_m[w][e] - mx);
+      ls += S.part_l[w][e] * f;
+      o += S.part_acc[w][e][d] * f;
+    }
+    if (split) {
+      float* slot = a.workspace + ((((int64_t)b * a.Hkv + h) * gridDim.z + blockIdx.z) * E + e) * (2 + a.Dv);
+      slot[2 + d] = o;
+      if (d == 0) {
+        slot[0] = mx;
+        slot[1] = ls;
+      }
+    } else {
+      finish_elem<T>(a, b, h, e, d, mx, ls, o);
+    }
+  }
+}
+
+// Merge of the splits' states from the workspace, then the outputs.
+template <typename T>
+__global__ void __launch_bounds__(NT) decode_combine_kernel(DecParams P, int splits) {
+  const tc_decode_args& a = P.a;
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int E = a.Hq / a.Hkv;
+  for (int i = threadIdx.x; i < E * a.Dv; i += NT) {
+    const int e = i / a.Dv, d = i - e * a.Dv;
+    const float* slot0 = a.workspace + (((int64_t)b * a.Hkv + h) * splits * E + e) * (2 + a.Dv);
+    const int64_t step = (int64_t)E * (2 + a.Dv);
+    float mx = -INFINITY;
+    for (int s = 0; s < splits; ++s) mx = fmaxf(mx, slot0[s * step]);
+    float ls = 0.f, o = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      const float ms = slot0[s * step];
+      const float f = ms == -INFINITY ? 0.f : expf(ms - mx);
+      ls += slot0[s * step + 1] * f;
+      o += slot0[s * step + 2 + d] * f;
+    }
+    finish_elem<T>(a, b, h, e, d, mx, ls, o);
+  }
+}
+
 // Generic variant: any Dk, Dv <= DM, any element type; warp w takes entries
 // w, w + NW, ... one at a time.
 template <typename T, int DM>
@@ -240,7 +304,8 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = a.Hq / a.Hkv;
   const int total = S.roff_s[a.num_levels];
-  const T* rk = static_cast<const T*>(a.ring_k);
+  const bool prerot = a.ring_k_rot != nullptr && a.position_mode == TC_POS_ROPE;
+  const T* rk = static_cast<const T*>(prerot ? a.ring_k_rot : a.ring_k);
   const T* rv = static_cast<const T*>(a.ring_v);
   const auto kidx = [&](int slot, int d) { return (((int64_t)b * total + slot) * a.Hkv + h) * a.Dk + d; };
   const auto vidx = [&](int slot, int d) { return (((int64_t)b * total + slot) * a.Hkv + h) * a.Dv + d; };
@@ -266,7 +331,7 @@ __global__ void __launch_bounds__(NT) decode_kernel(DecParams P) {
       kv[i] = d < a.Dk ? to_f(rk[kidx(slot, d)]) : 0.f;
       vv[i] = d < a.Dv ? to_f(rv[vidx(slot, d)]) : 0.f;
     }
-    if (a.position_mode == TC_POS_ROPE) {
+    if (a.position_mode == TC_POS_ROPE && !prerot) {
       // rotate the key at its summary position (j + 1) 2^l - 1, via the warp buffer
 #pragma unroll
       for (int i = 0; i < DC; ++i) S.wbuf[warp][lane + 32 * i] = kv[i];
@@ -391,10 +456,12 @@ __global__ void __launch_bounds__(NT) decode_kernel128(DecParams P) {
   if (threadIdx.x < nl) r0_s[threadIdx.x] = S.lo_s[threadIdx.x] % S.caps_s[threadIdx.x];
   __syncthreads();
   const int total = S.roff_s[nl];
-  const uint4* rk = static_cast<const uint4*>(a.ring_k);
+  // rope with a rotated-key ring: read the rotated keys, rotate nothing
+  const bool prerot = a.ring_k_rot != nullptr && a.position_mode == TC_POS_ROPE;
+  const uint4* rk = static_cast<const uint4*>(prerot ? a.ring_k_rot : a.ring_k);
   const uint4* rv = static_cast<const uint4*>(a.ring_v);
   const int64_t row0 = (int64_t)b * total * a.Hkv + h;  // row of (b, slot, h) = row0 + slot * Hkv
-  const bool rope = a.position_mode == TC_POS_ROPE, rel = a.position_mode == TC_POS_RELATIVE;
+  const bool rope = a.position_mode == TC_POS_ROPE && !prerot, rel = a.position_mode == TC_POS_RELATIVE;
   const bool cap = a.has_softcap;
   constexpr float kLog2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
   // logit2 = cap log2e tanh((dot scale + bias) / cap), or (dot scale + bias) log2e
@@ -418,7 +485,10 @@ __global__ void __launch_bounds__(NT) decode_kernel128(DecParams P) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[e][i] = make_float2(0.f, 0.f);
   }
-  const int M = S.pre_s[nl];
+  // this CTA's entries [e_lo, e_hi) of the visible set (all of it unsplit)
+  const int M_all = S.pre_s[nl];
+  const int e_lo = (int)((int64_t)M_all * blockIdx.z / gridDim.z);
+  const int M = (int)((int64_t)M_all * (blockIdx.z + 1) / gridDim.z);
   int lev = 0;  // entries of a lane only move forward through the levels
   uint4 kn[4], vn[4];
   int jn[4], ln[4];
@@ -442,8 +512,8 @@ __global__ void __launch_bounds__(NT) decode_kernel128(DecParams P) {
       }
     }
   };
-  if (M > 0) fetch(0);
-  for (int g0 = 0; g0 < M; g0 += 64) {
+  if (e_lo < M) fetch(e_lo);
+  for (int g0 = e_lo; g0 < M; g0 += 64) {
     uint4 kc[4], vc[4];
     int jc[4], lc[4];
 #pragma unroll
@@ -554,17 +624,105 @@ __global__ void __launch_bounds__(NT) decode_kernel128(DecParams P) {
   decode_epilogue<T, 128>(P, S);
 }
 
+// ROTATE: ring_k_rot[slot] = R(pos) ring_k[slot] for every node visible to
+// query t (the live nodes), one warp per node.
+template <typename T>
+__global__ void __launch_bounds__(NT) decode_rotate_kernel(DecParams P) {
+  const tc_decode_args& a = P.a;
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ int lo_s[TC_MAX_LEVELS], pre_s[TC_MAX_LEVELS + 1];
+  if (threadIdx.x == 0) {
+    int lo[TC_MAX_LEVELS], hi[TC_MAX_LEVELS];
+    row_bounds_raw(a.t, a.act, a.num_levels, a.cache_size, lo, hi);
+    int acc = 0;
+    for (int l = 0; l < a.num_levels; ++l) {
+      if (lo[l] >= hi[l]) lo[l] = hi[l] = 0;
+      lo_s[l] = lo[l];
+      pre_s[l] = acc;
+      acc += hi[l] - lo[l];
+    }
+    pre_s[a.num_levels] = acc;
+  }
+  __syncthreads();
+  const int total = a.ring_off[a.num_levels], hd = a.Dk / 2;
+  const T* rk = static_cast<const T*>(a.ring_k);
+  T* rkr = static_cast<T*>(a.ring_k_rot);
+  int lev = 0;
+  for (int idx = warp; idx < pre_s[a.num_levels]; idx += NW) {
+    while (idx >= pre_s[lev + 1]) ++lev;
+    const int j = lo_s[lev] + (idx - pre_s[lev]);
+    const int slot = a.ring_off[lev] + j % a.caps[lev];
+    const int pos = ((j + 1) << lev) - 1;
+    const int64_t row = (((int64_t)b * total + slot) * a.Hkv + h) * a.Dk;
+    for (int i = lane; i < hd; i += 32) {
+      const float c = a.rope_cos[(int64_t)pos * hd + i], s = a.rope_sin[(int64_t)pos * hd + i];
+      const float x1 = to_f(rk[row + i]), x2 = to_f(rk[row + i + hd]);
+      rkr[row + i] = from_f<T>(x1 * c - x2 * s);
+      rkr[row + i + hd] = from_f<T>(x2 * c + x1 * s);
+    }
+  }
+}
+
+template <typename T>
+int launch128(const DecParams& P, int E, dim3 grid, cudaStream_t st) {
+  switch (E) {
+    case 1: decode_kernel128<T, 1><<<grid, NT, 0, st>>>(P); return launch_status();
+    case 2: decode_kernel128<T, 2><<<grid, NT, 0, st>>>(P); return launch_status();
+    case 4: decode_kernel128<T, 4><<<grid, NT, 0, st>>>(P); return launch_status();
+    case 8: decode_kernel128<T, 8><<<grid, NT, 0, st>>>(P); return launch_status();
+    default: return TC_ERR_UNSUPPORTED;
+  }
+}
+
+inline int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      n = 148;
+  }
+  return n;
+}
+
+// Splits of each (batch, KV head)'s entries: enough CTAs for ~16 per SM,
+// at least 256 entries per split, at most kMaxSplits and what the workspace holds.
+constexpr int kMaxSplits = 8;
+inline int decode_splits(const tc_decode_args& a, int E) {
+  if (!a.workspace) return 1;
+  const int64_t units = (int64_t)a.B * a.Hkv;
+  int s = (int)((16LL * sm_count() + units - 1) / units);
+  s = s < 1 ? 1 : (s > kMaxSplits ? kMaxSplits : s);
+  const int by_entries = a.cache_size / 256;
+  if (s > by_entries) s = by_entries < 1 ? 1 : by_entries;
+  while (s > 1 && units * s * E * (2 + a.Dv) > a.workspace_floats) --s;
+  return s;
+}
+
 template <typename T>
 int launch_decode(const DecParams& P, int E, int d, dim3 grid, cudaStream_t st) {
+  if (P.a.mode == TC_DECODE_ROTATE) {
+    decode_rotate_kernel<T><<<grid, NT, 0, st>>>(P);
+    return launch_status();
+  }
   if constexpr (sizeof(T) == 2) {
-    if (P.a.Dk == 128 && P.a.Dv == 128) {
-      switch (E) {
-        case 1: decode_kernel128<T, 1><<<grid, NT, 0, st>>>(P); return launch_status();
-        case 2: decode_kernel128<T, 2><<<grid, NT, 0, st>>>(P); return launch_status();
-        case 4: decode_kernel128<T, 4><<<grid, NT, 0, st>>>(P); return launch_status();
-        case 8: decode_kernel128<T, 8><<<grid, NT, 0, st>>>(P); return launch_status();
-        default: break;
+    if (P.a.Dk == 128 && P.a.Dv == 128 && (E == 1 || E == 2 || E == 4 || E == 8)) {
+      const int splits = decode_splits(P.a, E);
+      if (splits == 1) return launch128<T>(P, E, grid, st);
+      // advance (one CTA per unit), the split attention, the combine
+      if (P.a.mode != TC_DECODE_ATTEND) {
+        DecParams adv = P;
+        adv.a.mode = TC_DECODE_ADVANCE;
+        if (int rc = launch128<T>(adv, E, grid, st)) return rc;
       }
+      if (P.a.mode != TC_DECODE_ADVANCE) {
+        DecParams att = P;
+        att.a.mode = TC_DECODE_ATTEND;
+        if (int rc = launch128<T>(att, E, dim3(grid.x, grid.y, splits), st)) return rc;
+        decode_combine_kernel<T><<<grid, NT, 0, st>>>(P, splits);
+        return launch_status();
+      }
+      return TC_OK;
     }
   }
   if (d <= 32) decode_kernel<T, 32><<<grid, NT, 0, st>>>(P);
@@ -579,9 +737,15 @@ int launch_decode(const DecParams& P, int E, int d, dim3 grid, cudaStream_t st) 
 extern "C" int tc_decode_step(const tc_decode_args* a, void* stream) {
   if (!a || a->B <= 0 || a->Hq <= 0 || a->Hkv <= 0 || a->Hq % a->Hkv || a->Dk <= 0 || a->Dv <= 0 ||
       a->num_levels < 1 || a->num_levels > TC_MAX_LEVELS || a->t < 0 || !a->ring_k || !a->ring_v ||
-      !a->ring_w || !a->q_t || !a->out || !a->lse || a->mode < 0 || a->mode > 2)
+      !a->ring_w || a->mode < 0 || a->mode > 3)
     return TC_ERR_ARG;
-  if (a->mode != TC_DECODE_ATTEND) {
+  if (a->mode == TC_DECODE_ROTATE) {
+    if (!a->ring_k_rot || !a->rope_cos || !a->rope_sin || a->Dk % 2 || a->position_mode != TC_POS_ROPE)
+      return TC_ERR_ARG;
+  } else if (!a->q_t || !a->out || !a->lse) {
+    return TC_ERR_ARG;
+  }
+  if (a->mode == TC_DECODE_FULL || a->mode == TC_DECODE_ADVANCE) {
     if (!a->k_t || !a->v_t) return TC_ERR_ARG;
     if (a->conv_k_width > 0 && (!a->k_conv_w || !a->v_conv_w)) return TC_ERR_ARG;
     if (a->conv_k_width > 1 && (!a->conv_k || !a->conv_v)) return TC_ERR_ARG;

@@ -8,7 +8,8 @@ from typing import Optional, Tuple
 import torch
 
 from .. import _lib
-from .decode_state import DecodeState, _check_tick, _decode_launch, _validate_advance
+from .decode_state import (DecodeState, _check_tick, _decode_launch, _ensure_rotated_ring, _rot_key,
+                           _validate_advance)
 from .position import check_relative_bins, compute_relative_states, positional_args
 
 
@@ -82,9 +83,10 @@ def multilevel_attention_decode(
     t = state.t - 1
     cos, sin, st, pj = _decode_positional(state, q_t, t, position_mode, rope_cos, rope_sin,
                                           relative_states, relative_proj)
+    k_rot = _ensure_rotated_ring(state, cos, sin) if position_mode == "rope" else None
     out, lse, _, _ = _decode_launch(state, _lib.DECODE_ATTEND, q_t, softcap=softcap,
                                     position_mode=position_mode, cos=cos, sin=sin, rel_states=st,
-                                    rel_proj=pj, t=t)
+                                    rel_proj=pj, t=t, k_rot=k_rot)
     return out, lse, _decode_stats(state, t, position_mode)
 
 
@@ -147,11 +149,15 @@ def decode_step(
                 f"gate_weight shape {tuple(gate_weight.shape)} != {(Hq * Dv, x_t.shape[-1])}")
         gate_pre = x_t.matmul(gate_weight.t()).reshape(B, Hq * Dv).contiguous()
     _check_tick(state, t)
+    k_rot = _ensure_rotated_ring(state, cos, sin) if position_mode == "rope" else None
     out, lse, _, _ = _decode_launch(
         state, _lib.DECODE_FULL, q_t, k_t, v_t, w_t=w_t, kcw=k_conv_weight, vcw=v_conv_weight,
         softcap=softcap, position_mode=position_mode, cos=cos, sin=sin, rel_states=st, rel_proj=pj,
-        sinks=None if sinks is None else sinks.contiguous(), gate_pre=gate_pre)
+        sinks=None if sinks is None else sinks.contiguous(), gate_pre=gate_pre, k_rot=k_rot)
     state.t = t + 1
+    # the step wrote the rotated copies of the rows it created (rope), so the
+    # ring stays current for these tables; other modes leave it stale
+    state.k_rot_key = _rot_key(state, cos, sin) if k_rot is not None else None
     if gate_pre is not None:
         out = out.to(torch.result_type(out, gate_pre))
     return out, lse

@@ -26,7 +26,12 @@ class DecodeState:
     """One layer's decode cache (reference.py:1703-1736):
     k [B, sum(caps), Hkv, Dk] unrotated post-conv keys, v [B, sum(caps), Hkv, Dv],
     w [B, sum(caps), Hkv, 1] merge log-weights, conv_k/conv_v [B, K-1, Hkv*D]
-    (last K-1 pre-conv rows, newest last) or None, t = tokens consumed."""
+    (last K-1 pre-conv rows, newest last) or None, t = tokens consumed.
+
+    k_rot / k_rot_key are this build's derived cache for rope decode: the ring
+    keys rotated at their summary positions, valid for the rope tables named by
+    the key.  Every decode call keeps it current or marks it stale; it is
+    rebuilt from k when needed, so it never changes results."""
 
     k: torch.Tensor
     v: torch.Tensor
@@ -38,6 +43,8 @@ class DecodeState:
     cache_size: int
     caps: Tuple[int, ...]
     ring_offsets: Tuple[int, ...]
+    k_rot: Optional[torch.Tensor] = None
+    k_rot_key: Optional[tuple] = None
 
     @property
     def num_levels(self) -> int:
@@ -207,9 +214,33 @@ def _check_tick(state: DecodeState, t: int):
                 f"level {level} needs {hi - lo} live slots > cap {state.caps[level]} at t={t}")
 
 
+DECODE_MAX_SPLITS = 8
+
+
+def _rot_key(state: DecodeState, cos, sin):
+    return (cos.data_ptr(), sin.data_ptr(), tuple(cos.shape), state.k.data_ptr(), state.t)
+
+
+def _ensure_rotated_ring(state: DecodeState, cos, sin):
+    """Make state.k_rot hold the live keys rotated with these tables (rebuilt
+    from state.k by one launch when stale).  Returns the ring."""
+    if state.k_rot is None or state.k_rot.shape != state.k.shape or state.k_rot.dtype != state.k.dtype \
+            or state.k_rot.device != state.k.device:
+        state.k_rot = torch.empty_like(state.k)
+        state.k_rot_key = None
+    if state.k_rot_key != _rot_key(state, cos, sin):
+        if state.t >= 1:
+            B, _, Hkv, Dk = state.k.shape
+            dummy = torch.empty(B, 1, Hkv, Dk, device=state.k.device, dtype=state.k.dtype)
+            _decode_launch(state, _lib.DECODE_ROTATE, dummy, position_mode="rope", cos=cos, sin=sin,
+                           t=state.t - 1, k_rot=state.k_rot)
+        state.k_rot_key = _rot_key(state, cos, sin)
+    return state.k_rot
+
+
 def _decode_launch(state: DecodeState, mode, q_t, k_t=None, v_t=None, w_t=None, kcw=None, vcw=None,
                    softcap=None, position_mode="none", cos=None, sin=None, rel_states=None,
-                   rel_proj=None, sinks=None, gate_pre=None, t=None, want_kv=False):
+                   rel_proj=None, sinks=None, gate_pre=None, t=None, want_kv=False, k_rot=None):
     B, _, Hq, Dk = q_t.shape
     Hkv = state.k.shape[2]
     Dv = state.v.shape[-1]
@@ -226,6 +257,11 @@ def _decode_launch(state: DecodeState, mode, q_t, k_t=None, v_t=None, w_t=None, 
     k_new = torch.empty(B, 1, Hkv, Dk, device=q_t.device, dtype=dtype) if want_kv else None
     v_new = torch.empty(B, 1, Hkv, Dv, device=q_t.device, dtype=dtype) if want_kv else None
     L1 = state.num_levels
+    ws = None
+    if Dk == 128 and Dv == 128 and dtype in (torch.bfloat16, torch.float16):
+        # scratch for splitting each (batch, KV head)'s entries over CTAs
+        ws = torch.empty(B * Hkv * DECODE_MAX_SPLITS * (Hq // Hkv) * 130, device=q_t.device,
+                         dtype=torch.float32)
     conv_w = 0 if kcw is None else kcw.shape[1]
     if kcw is not None:
         kcw = kcw.contiguous()
@@ -260,7 +296,8 @@ def _decode_launch(state: DecodeState, mode, q_t, k_t=None, v_t=None, w_t=None, 
         rel_bins=0 if rel_proj is None else rel_proj.shape[1], sinks=p(sinks),
         sink_dtype=_lib.dtype_code(sinks.dtype) if sinks is not None else 0, gate_pre=p(gate_pre),
         gate_dtype=_lib.dtype_code(gate_pre.dtype) if gate_pre is not None else 0,
-        out=out.data_ptr(), lse=lse.data_ptr(), k_new=p(k_new), v_new=p(v_new))
+        out=out.data_ptr(), lse=lse.data_ptr(), k_new=p(k_new), v_new=p(v_new),
+        workspace=p(ws), workspace_floats=0 if ws is None else ws.numel(), ring_k_rot=p(k_rot))
     _lib.check(_lib.lib().tc_decode_step(ctypes.byref(args), _lib.stream_of(q_t)), "tc_decode_step")
     del keep
     return out, lse, k_new, v_new
@@ -318,6 +355,7 @@ def advance_decode_state(state: DecodeState, q_t: torch.Tensor, k_t: torch.Tenso
     _, _, k_new, v_new = _decode_launch(state, _lib.DECODE_ADVANCE, q_t, k_t, v_t, w_t=w_t,
                                         kcw=k_conv_weight, vcw=v_conv_weight, want_kv=True)
     state.t += 1
+    state.k_rot_key = None  # no rope tables here: the rotated ring is stale
     return k_new, v_new
 
 

@@ -34,6 +34,9 @@ GEOS = {
     # head dim 128 with a ragged last 64-token chunk and odd level lengths
     "d128_odd": dict(B=2, N=301, Hq=2, Hkv=2, Dk=128, Dv=128,
                      fmap={1: 64, 2: 128, 3: 192}, cache=256),
+    # cache 640 (the decode attention splits each head's entries over CTAs)
+    "d128_dec": dict(B=2, N=900, Hq=2, Hkv=2, Dk=128, Dv=128,
+                     fmap={1: 128, 2: 256, 3: 384, 4: 512}, cache=640),
     # eight levels: merges past one 64-token chunk
     "d128_deep": dict(B=1, N=700, Hq=2, Hkv=2, Dk=128, Dv=128,
                       fmap={l: 64 * l for l in range(1, 8)}, cache=512),
@@ -133,6 +136,11 @@ CASES = [
     case("dec_plain_gqa4_bf16", "decode", "d128_gqa4", dtype="bf16", conv=4, tail=20, seed=513),
     case("dec_nocap_gqa8_bf16", "decode", "d128_gqa8", dtype="bf16", position="rope",
          softcap=None, tail=16, seed=514),
+    # cache 640: the decode attention splits each head's entries over CTAs
+    case("dec_rope_split_bf16", "decode", "d128_dec", dtype="bf16", conv=4, position="rope",
+         sink=True, gate=True, tail=40, seed=515),
+    case("dec_rel_split_bf16", "decode", "d128_dec", dtype="bf16", position="relative",
+         tail=24, seed=516),
 ]
 
 CASE_BY_NAME = {c["name"]: c for c in CASES}
