@@ -456,20 +456,17 @@ __global__ void __launch_bounds__(NT) decode_kernel128(DecParams P) {
   if (threadIdx.x < nl) r0_s[threadIdx.x] = S.lo_s[threadIdx.x] % S.caps_s[threadIdx.x];
   __syncthreads();
   const int total = S.roff_s[nl];
-  // rope with a rotated-key ring: read the rotated keys, rotate nothing
-  const bool prerot = a.ring_k_rot != nullptr && a.position_mode == TC_POS_ROPE;
-  const uint4* rk = static_cast<const uint4*>(prerot ? a.ring_k_rot : a.ring_k);
+  // rope reads the rotated-key ring (the launcher guarantees it): no rotation here
+  const uint4* rk = static_cast<const uint4*>(a.position_mode == TC_POS_ROPE ? a.ring_k_rot : a.ring_k);
   const uint4* rv = static_cast<const uint4*>(a.ring_v);
   const int64_t row0 = (int64_t)b * total * a.Hkv + h;  // row of (b, slot, h) = row0 + slot * Hkv
-  const bool rope = a.position_mode == TC_POS_ROPE && !prerot, rel = a.position_mode == TC_POS_RELATIVE;
+  const bool rel = a.position_mode == TC_POS_RELATIVE;
   const bool cap = a.has_softcap;
   constexpr float kLog2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
   // logit2 = cap log2e tanh((dot scale + bias) / cap), or (dot scale + bias) log2e
   const float k_in = cap ? P.scale / a.softcap : P.scale * kLog2e;
   const float k_bias = cap ? 1.f / a.softcap : kLog2e;
   const float k_out = a.softcap * kLog2e;
-  // rotate-half: dims below 64 take -partner * sin, the others +partner * sin
-  const uint32_t sgn = l16 < 8 ? 0x80008000u : 0u;
 
   float2 q[E][4];
 #pragma unroll
@@ -532,21 +529,6 @@ __global__ void __launch_bounds__(NT) decode_kernel128(DecParams P) {
       float2 kf[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) kf[c] = unpack2<T>(kw[c]);
-      if (rope) {
-        // dims d and d + 64 sit in lanes l16 and l16 ^ 8 of the same half
-        const uint4 pk = shfl_xor4(kc[i], 8);
-        const uint32_t pw[4] = {pk.x ^ sgn, pk.y ^ sgn, pk.z ^ sgn, pk.w ^ sgn};
-        const int pos = ok ? ((jc[i] + 1) << lc[i]) - 1 : 0;
-        const float4* cr = reinterpret_cast<const float4*>(a.rope_cos + (int64_t)pos * 64 + (l16 & 7) * 8);
-        const float4* sr = reinterpret_cast<const float4*>(a.rope_sin + (int64_t)pos * 64 + (l16 & 7) * 8);
-        const float4 c0 = __ldg(cr), c1 = __ldg(cr + 1), s0 = __ldg(sr), s1 = __ldg(sr + 1);
-        const float2 cs[4] = {make_float2(c0.x, c0.y), make_float2(c0.z, c0.w), make_float2(c1.x, c1.y),
-                              make_float2(c1.z, c1.w)};
-        const float2 sn[4] = {make_float2(s0.x, s0.y), make_float2(s0.z, s0.w), make_float2(s1.x, s1.y),
-                              make_float2(s1.z, s1.w)};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) kf[c] = round2<T>(ffma2(unpack2<T>(pw[c]), sn[c], fmul2(kf[c], cs[c])));
-      }
       float pr0 = 0.f, pr1 = 0.f;  // relative: proj[r, dist] for r = l16, l16 + 16
       if (rel && ok) {
         const int dist = S.base_s[lc[i]] - jc[i];
@@ -706,7 +688,8 @@ int launch_decode(const DecParams& P, int E, int d, dim3 grid, cudaStream_t st) 
     return launch_status();
   }
   if constexpr (sizeof(T) == 2) {
-    if (P.a.Dk == 128 && P.a.Dv == 128 && (E == 1 || E == 2 || E == 4 || E == 8)) {
+    const bool rope_ok = P.a.position_mode != TC_POS_ROPE || P.a.ring_k_rot != nullptr;
+    if (P.a.Dk == 128 && P.a.Dv == 128 && (E == 1 || E == 2 || E == 4 || E == 8) && rope_ok) {
       const int splits = decode_splits(P.a, E);
       if (splits == 1) return launch128<T>(P, E, grid, st);
       // advance (one CTA per unit), the split attention, the combine
