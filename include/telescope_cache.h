@@ -255,6 +255,12 @@ int tc_attn_bwd(const tc_attn_args* a, const tc_schedule* s, void* stream);
  * capture); calls that overlap on the GPU share the array and race. */
 int tc_attn_bwd_noalloc(const tc_attn_args* a, const tc_schedule* s, void* stream);
 
+/* Failure-detection self-test (no reference counterpart): one kernel waits on
+ * a pipeline barrier that nothing completes, through the bounded wait every
+ * tensor-core kernel uses; the wait gives up (well under a second), ORs
+ * TC_DEV_WAIT_TIMEOUT into *dev_status and the kernel returns normally. */
+int tc_selftest_wait_timeout(int32_t* dev_status, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* post-ops                                                                  */
 /* ------------------------------------------------------------------------ */

@@ -94,6 +94,7 @@ SIGNATURES = {
     "tc_attn_fwd": [ctypes.POINTER(AttnArgs), ctypes.POINTER(Schedule), _c_vp],
     "tc_attn_bwd": [ctypes.POINTER(AttnArgs), ctypes.POINTER(Schedule), _c_vp],
     "tc_attn_bwd_noalloc": [ctypes.POINTER(AttnArgs), ctypes.POINTER(Schedule), _c_vp],
+    "tc_selftest_wait_timeout": [_c_vp, _c_vp],
     "tc_sink_fwd": [_c_i64, _c_i32, _c_i32, _c_i32, _c_vp, _c_vp, _c_i32, _c_vp, _c_vp, _c_vp],
     "tc_sink_bwd": [_c_i64, _c_i32, _c_i32, _c_i32, _c_vp, _c_vp, _c_i32, _c_vp, _c_vp, _c_vp,
                     _c_vp, _c_vp, _c_vp],

@@ -41,20 +41,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after kWaitLimit polls (well under a second), sets the CTA's
-// abort flag and the device status word, and returns false.  Once the abort
-// flag is set every later wait returns false immediately, so all roles drain
-// to the kernel's teardown instead of spinning.
-constexpr uint32_t kWaitLimit = 1u << 22;
+// Bounded wait: gives up after about a second of polling (device global
+// timer), sets the CTA's abort flag and the device status word, and returns
+// false.  Once the abort flag is set every later wait returns false
+// immediately, so all roles drain to the kernel's teardown instead of
+// spinning.
+constexpr uint64_t kWaitNs = 1000000000ull;
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatile int* abort_flag,
                                           int32_t* status) {
   uint32_t n = 0;
+  uint64_t t0 = 0;
   while (!mbar_try_wait(bar, phase)) {
     if (*abort_flag) return false;
-    if (++n > kWaitLimit) {
-      *abort_flag = 1;
-      if (status) atomicOr(status, TC_DEV_WAIT_TIMEOUT);
-      return false;
+    if ((++n & 255u) == 0u) {
+      const uint64_t now = global_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitNs) {
+        *abort_flag = 1;
+        if (status) atomicOr(status, TC_DEV_WAIT_TIMEOUT);
+        return false;
+      }
     }
     if (n > 1024) __nanosleep(64);
   }
