@@ -28,19 +28,23 @@ constexpr int T128 = 128 * 128 * 2;  // [128 rows x 128] 16-bit tile, two 64-col
 constexpr int T64 = 64 * 128 * 2;    // [64 rows x 128] tile
 constexpr int B128 = 128 * 128;      // one 64-col block of a 128-row tile
 constexpr int B64 = 64 * 128;        // one 64-col block of a 64-row tile
-constexpr int kSmemA = 2 * T128 + 4 * T64 + 128 * 128 + 1024 + 256;
+// dX tiles the accumulate MMAs read: double buffered (NX = 2) unless the
+// relative variant's staging leaves no room
+constexpr int nx_of(bool rel) { return rel ? 1 : 2; }
+constexpr int kSmemA = 2 * T128 + 4 * T64 + nx_of(false) * 128 * 128 + 1024 + 256;
 // relative Pass A: + an fp32 dX staging tile [128 x 66], per-row run info,
 // row totals and the double-buffered bias runs [2][128][kRunStride]
 constexpr int kDxfStride = 66;  // even: 8-byte column pairs; 16 rows per phase hit distinct banks
-constexpr int kSmemArel = kSmemA + 128 * kDxfStride * 4 + 128 * 3 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2 + 256;
+constexpr int kSmemArel = 2 * T128 + 4 * T64 + nx_of(true) * 128 * 128 + 1024 + 256 + 128 * kDxfStride * 4 + 128 * 3 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2 + 256;
 // Pass B: tiles + per-step query info [2][64] x {lo, hi, -lse2, -Delta} + the
 // per-warp interior flags [2][2] + bias offsets [2][64] (bytes) + barriers;
 // relative adds the staged bias columns [2][64][kColStride]
 constexpr int kColStride = 136;  // 272 B: the 16-byte aligned superset of a 128-node run
 constexpr int HC = 64 / kRowThreads;                     // tile columns per compute thread
 constexpr int kRowsPerWarp = 128 / (kComputeThreads / 32);  // drel write-out rows per compute warp
-constexpr int kSmemB = 2 * T128 + 4 * T64 + 2 * 128 * 128 + 2 * 64 * 16 + 16 + 2 * 64 + 256 + 1024;
-constexpr int kSmemBrel = kSmemB + 2 * 64 * kColStride * 2;
+constexpr int kSmemB = 2 * T128 + 4 * T64 + nx_of(false) * 2 * 128 * 128 + 2 * 64 * 16 + 16 + 2 * 64 + 256 + 1024;
+constexpr int kSmemBrel = 2 * T128 + 4 * T64 + nx_of(true) * 2 * 128 * 128 + 2 * 64 * 16 + 16 + 2 * 64 + 256 + 1024 +
+                          2 * 64 * kColStride * 2;
 
 struct BwdParams {
   int N, Hq, Hkv, E;
@@ -120,19 +124,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* g_s = q_s + T128;
   uint8_t* k_s = g_s + T128;   // [2] x T64
   uint8_t* v_s = k_s + 2 * T64;
-  uint8_t* x_s = v_s + 2 * T64;  // dX [128 x 64]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(x_s + 128 * 128);
+  constexpr int NX = nx_of(REL);
+  uint8_t* x_s = v_s + 2 * T64;  // [NX] dX [128 x 64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(x_s + NX * 128 * 128);
   uint64_t* qg_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = bars + 3;
   uint64_t* s_full = bars + 5;
   uint64_t* s_free = bars + 7;
-  uint64_t* x_full = bars + 9;
-  uint64_t* x_free = bars + 10;
-  uint64_t* dq_done = bars + 11;
-  uint64_t* run_full = bars + 12;   // relative: staged bias runs ready (warps 2-3)
-  uint64_t* run_empty = bars + 14;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* x_full = bars + 9;       // [NX]
+  uint64_t* x_free = x_full + NX;    // [NX]
+  uint64_t* dq_done = x_free + NX;
+  uint64_t* run_full = dq_done + 1;  // relative: staged bias runs ready (warps 2-3)
+  uint64_t* run_empty = run_full + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(run_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   // relative only: fp32 dX staging [128][65], run info [128][3], row totals
   // [128], bias runs [2][128][kRunStride]
@@ -158,8 +163,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&run_full[i], 64);
       mbar_init(&run_empty[i], kComputeThreads);
     }
-    mbar_init(x_full, kComputeThreads);
-    mbar_init(x_free, 1);
+    for (int i = 0; i < NX; ++i) {
+      mbar_init(&x_full[i], kComputeThreads);
+      mbar_init(&x_free[i], 1);
+    }
     mbar_init(dq_done, 1);
     *abort_flag = 0;
     mbar_fence_init();
@@ -199,12 +206,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t kIdQ = idesc_f16(128, 128, Pack2<T>::kFmt, 0, 1);
       const uint32_t qa = smem_addr(q_s), ga = smem_addr(g_s), xa = smem_addr(x_s);
       auto issue_dq = [&](int t) {
-        const uint32_t ka = smem_addr(k_s + (t & 1) * T64);
+        const uint32_t ka = smem_addr(k_s + (t & 1) * T64), xb = xa + (t % NX) * 128 * 128;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_f16(tmem + 256, sdesc_sw128(xa + kk * 32, 16, 1024), sdesc_sw128(ka + kk * 2048, B64, 1024), kIdQ,
+          mma_f16(tmem + 256, sdesc_sw128(xb + kk * 32, 16, 1024), sdesc_sw128(ka + kk * 2048, B64, 1024), kIdQ,
                   (t > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(x_free);
+        mma_commit(&x_free[t % NX]);
         mma_commit(&kv_empty[t & 1]);
       };
       bool alive = mbar_wait(qg_full, 0, abort_flag, status);
@@ -232,12 +239,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(&s_full[bb]);
         if (j >= 1) {
-          if (!mbar_wait(x_full, (j - 1) & 1, abort_flag, status)) { alive = false; break; }
+          const int t = j - 1;
+          if (!mbar_wait(&x_full[t % NX], (t / NX) & 1, abort_flag, status)) { alive = false; break; }
           tc_fence_after();
-          issue_dq(j - 1);
+          issue_dq(t);
         }
       }
-      if (alive && j >= 1 && mbar_wait(x_full, (j - 1) & 1, abort_flag, status)) {
+      if (alive && j >= 1 && mbar_wait(&x_full[(j - 1) % NX], ((j - 1) / NX) & 1, abort_flag, status)) {
         tc_fence_after();
         issue_dq(j - 1);
       }
@@ -288,8 +296,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[bb]);
-      if (j >= 1) {
-        alive = __all_sync(0xffffffffu, mbar_wait(x_free, (j - 1) & 1, abort_flag, status));
+      if (j >= NX) {  // dX buffer j % NX read by the dQ MMA of tile j - NX
+        alive = __all_sync(0xffffffffu, mbar_wait(&x_free[j % NX], ((j / NX) - 1) & 1, abort_flag, status));
         if (!alive) break;
       }
       const int jlo = lo - it.k0, jhi = hi - it.k0;
@@ -324,10 +332,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int cc8 = 0; cc8 < HC / 8; ++cc8)
-        *reinterpret_cast<uint4*>(x_s + sw128_offset(r, (ch * (HC / 8) + cc8) * 8, 128)) = pack8<T>(dx + cc8 * 8, 1.f);
+        *reinterpret_cast<uint4*>(x_s + (j % NX) * 128 * 128 + sw128_offset(r, (ch * (HC / 8) + cc8) * 8, 128)) =
+            pack8<T>(dx + cc8 * 8, 1.f);
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(x_full);
+      mbar_arrive(&x_full[j % NX]);
       if (want_drel) {
         // d rel_logits[q, h, dist] = dX (each (row, distance) once): this row's
         // valid columns [cs, ce) are distances base - k0 - c, one ascending run
@@ -412,10 +421,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* v_s = k_s + T128;
   uint8_t* q_s = v_s + T128;   // [2] x T64
   uint8_t* g_s = q_s + 2 * T64;
-  uint8_t* pt_s = g_s + 2 * T64;  // P^T  [128 x 64]
-  uint8_t* xt_s = pt_s + 128 * 128;  // dX^T [128 x 64]
+  constexpr int NX = nx_of(REL);
+  uint8_t* pt_s = g_s + 2 * T64;          // [NX] P^T  [128 x 64]
+  uint8_t* xt_s = pt_s + NX * 128 * 128;  // [NX] dX^T [128 x 64]
   // per step (double buffered), per query column: lo, hi, -lse * log2e, -Delta
-  int* lo_s = reinterpret_cast<int*>(xt_s + 128 * 128);  // [2][64]
+  int* lo_s = reinterpret_cast<int*>(xt_s + NX * 128 * 128);  // [2][64]
   int* hi_s = lo_s + 2 * 64;
   float* nl_s = reinterpret_cast<float*>(hi_s + 2 * 64);
   float* nd_s = nl_s + 2 * 64;
@@ -428,12 +438,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* q_empty = bars + 3;
   uint64_t* s_full = bars + 5;
   uint64_t* s_free = bars + 7;
-  uint64_t* x_full = bars + 9;
-  uint64_t* x_free = bars + 10;
-  uint64_t* kv_done = bars + 11;
-  uint64_t* info_full = bars + 12;   // warps 2-3: step info (and bias columns) ready
-  uint64_t* info_empty = bars + 14;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* x_full = bars + 9;        // [NX]
+  uint64_t* x_free = x_full + NX;     // [NX]
+  uint64_t* kv_done = x_free + NX;
+  uint64_t* info_full = kv_done + 1;  // warps 2-3: step info (and bias columns) ready
+  uint64_t* info_empty = info_full + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(info_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   // relative: bias column c of a step holds rl[row_c, pad + base_c - k0 - 127 - o_c ...]
   // (272 B from the 16-byte boundary below it); node r reads element o_c + 127 - r
@@ -460,8 +470,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&info_full[i], 64);
       mbar_init(&info_empty[i], kComputeThreads);
     }
-    mbar_init(x_full, kComputeThreads);
-    mbar_init(x_free, 1);
+    for (int i = 0; i < NX; ++i) {
+      mbar_init(&x_full[i], kComputeThreads);
+      mbar_init(&x_free[i], 1);
+    }
     mbar_init(kv_done, 1);
     *abort_flag = 0;
     mbar_fence_init();
@@ -504,13 +516,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ka = smem_addr(k_s), va = smem_addr(v_s), pa = smem_addr(pt_s), xa = smem_addr(xt_s);
       auto issue_acc = [&](int t) {
         const uint32_t qa = smem_addr(q_s + (t & 1) * T64), ga = smem_addr(g_s + (t & 1) * T64);
+        const uint32_t pb = pa + (t % NX) * 128 * 128, xb = xa + (t % NX) * 128 * 128;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-          mma_f16(tmem + 256, sdesc_sw128(pa + kk * 32, 16, 1024), sdesc_sw128(ga + kk * 2048, B64, 1024), kIdA, acc);
-          mma_f16(tmem + 384, sdesc_sw128(xa + kk * 32, 16, 1024), sdesc_sw128(qa + kk * 2048, B64, 1024), kIdA, acc);
+          mma_f16(tmem + 256, sdesc_sw128(pb + kk * 32, 16, 1024), sdesc_sw128(ga + kk * 2048, B64, 1024), kIdA, acc);
+          mma_f16(tmem + 384, sdesc_sw128(xb + kk * 32, 16, 1024), sdesc_sw128(qa + kk * 2048, B64, 1024), kIdA, acc);
         }
-        mma_commit(x_free);
+        mma_commit(&x_free[t % NX]);
         mma_commit(&q_empty[t & 1]);
       };
       QSteps w;
@@ -541,12 +554,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(&s_full[bb]);
         if (i >= 1) {
-          if (!mbar_wait(x_full, (i - 1) & 1, abort_flag, status)) { alive = false; break; }
+          const int t = i - 1;
+          if (!mbar_wait(&x_full[t % NX], (t / NX) & 1, abort_flag, status)) { alive = false; break; }
           tc_fence_after();
-          issue_acc(i - 1);
+          issue_acc(t);
         }
       }
-      if (alive && i >= 1 && mbar_wait(x_full, (i - 1) & 1, abort_flag, status)) {
+      if (alive && i >= 1 && mbar_wait(&x_full[(i - 1) % NX], ((i - 1) / NX) & 1, abort_flag, status)) {
         tc_fence_after();
         issue_acc(i - 1);
       }
@@ -624,8 +638,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[bb]);
-      if (i >= 1) {
-        alive = __all_sync(0xffffffffu, mbar_wait(x_free, (i - 1) & 1, abort_flag, status));
+      if (i >= NX) {  // P^T / dX^T buffer i % NX read by the MMAs of step i - NX
+        alive = __all_sync(0xffffffffu, mbar_wait(&x_free[i % NX], ((i / NX) - 1) & 1, abort_flag, status));
         if (!alive) break;
       }
       alive = __all_sync(0xffffffffu, mbar_wait(&info_full[bb], (i >> 1) & 1, abort_flag, status));
@@ -663,14 +677,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int cc8 = 0; cc8 < HC / 8; ++cc8) {
-        const uint32_t off = sw128_offset(r, (ch * (HC / 8) + cc8) * 8, 128);
+        const uint32_t off = (i % NX) * 128 * 128 + sw128_offset(r, (ch * (HC / 8) + cc8) * 8, 128);
         *reinterpret_cast<uint4*>(pt_s + off) = pack8<T>(pr + cc8 * 8, 1.f);
         *reinterpret_cast<uint4*>(xt_s + off) = pack8<T>(dx + cc8 * 8, 1.f);
       }
       mbar_arrive(&info_empty[bb]);
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(x_full);
+      mbar_arrive(&x_full[i % NX]);
     }
     if (alive && i >= 1) alive = __all_sync(0xffffffffu, mbar_wait(kv_done, 0, abort_flag, status));
     if (alive) {

@@ -291,14 +291,19 @@ __device__ __forceinline__ void store_row_part(uint32_t taddr, int ch, bool have
     }
     if (!store) continue;
     if (rope && have) {
-      const float* cr = cos_t + (int64_t)pos * (HD / 2) + (c0 & 63);
-      const float* sr = sin_t + (int64_t)pos * (HD / 2) + (c0 & 63);
+      const float4* cr = reinterpret_cast<const float4*>(cos_t + (int64_t)pos * (HD / 2) + (c0 & 63));
+      const float4* sr = reinterpret_cast<const float4*>(sin_t + (int64_t)pos * (HD / 2) + (c0 & 63));
       const bool first = c0 < 64;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float cc = __ldg(cr + i), ss = __ldg(sr + i);
-        // first half: x1 c + x2 s; second half: x2 c - x1 s (x1 = dims < 64)
-        a[i] = first ? (a[i] * cc + pb[i] * ss) * mul : (a[i] * cc - pb[i] * ss) * mul;
+      for (int i4 = 0; i4 < 8; ++i4) {
+        const float4 c4 = __ldg(cr + i4), s4 = __ldg(sr + i4);
+        const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv4[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int i = i4 * 4 + k;
+          // first half: x1 c + x2 s; second half: x2 c - x1 s (x1 = dims < 64)
+          a[i] = first ? (a[i] * cv[k] + pb[i] * sv4[k]) * mul : (a[i] * cv[k] - pb[i] * sv4[k]) * mul;
+        }
       }
     } else {
 #pragma unroll

@@ -46,6 +46,9 @@ def compute_linear_weights(x: torch.Tensor, w_proj: torch.Tensor) -> torch.Tenso
     Hkv, Ew = w_proj.shape
     assert E == Ew
     _lib.require_cuda(x, w_proj)
+    if x.dtype == w_proj.dtype:
+        # the reference's own op: one plain GEMM (cuBLAS through torch)
+        return x.matmul(w_proj.t()).unsqueeze(-1)
     x, w_proj = _contig(x), _contig(w_proj)
     out = torch.empty(B, N, Hkv, 1, device=x.device, dtype=torch.result_type(x, w_proj))
     _lib.check(_lib.lib().tc_linear_weights(
