@@ -413,6 +413,7 @@ int launch_fwd(const AttnParams& a, int dtype, cudaStream_t st) {
   p.rl_pad = a.rl_pad;
   p.s = a.s;
   constexpr int smem = FwdShape<BK>::SMEM + (REL ? 2 * 128 * kRunStride * 2 + 256 : 0);
+  static_assert(smem <= 227 * 1024, "forward shared memory layout exceeds the per-CTA limit");
   auto k = fwd_tc_kernel<T, BK, REL, CAP>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return TC_ERR_CUDA;
   k<<<dim3((a.N + BQ - 1) / BQ, a.Hq, a.B), kThreads, smem, st>>>(mq, mk, mv, p);

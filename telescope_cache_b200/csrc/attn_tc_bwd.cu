@@ -46,6 +46,10 @@ constexpr int kSmemB = 2 * T128 + 4 * T64 + nx_of(false) * 2 * 128 * 128 + 2 * 6
 constexpr int kSmemBrel = 2 * T128 + 4 * T64 + nx_of(true) * 2 * 128 * 128 + 2 * 64 * 16 + 16 + 2 * 64 + 256 + 1024 +
                           2 * 64 * kColStride * 2;
 
+constexpr int kMaxSmem = 227 * 1024;  // dynamic shared memory per CTA on sm_100
+static_assert(kSmemA <= kMaxSmem && kSmemArel <= kMaxSmem && kSmemB <= kMaxSmem && kSmemBrel <= kMaxSmem,
+              "backward shared memory layout exceeds the per-CTA limit");
+
 struct BwdParams {
   int N, Hq, Hkv, E;
   float scale, cap;
