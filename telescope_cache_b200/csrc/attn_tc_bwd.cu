@@ -35,13 +35,16 @@ constexpr int kSmemA = 2 * T128 + 4 * T64 + nx_of(false) * 128 * 128 + 1024 + 25
 // relative Pass A: + an fp32 dX staging tile [128 x 66], per-row run info,
 // row totals and the double-buffered bias runs [2][128][kRunStride]
 constexpr int kDxfStride = 66;  // even: 8-byte column pairs; 16 rows per phase hit distinct banks
-constexpr int kSmemArel = 2 * T128 + 4 * T64 + nx_of(true) * 128 * 128 + 1024 + 256 + 128 * kDxfStride * 4 + 128 * 3 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2 + 256;
+constexpr int kSmemArel = 2 * T128 + 4 * T64 + nx_of(true) * 128 * 128 + 1024 + 256 + 128 * kDxfStride * 4 + 128 * 4 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2 + 256;
 // Pass B: tiles + per-step query info [2][64] x {lo, hi, -lse2, -Delta} + the
 // per-warp interior flags [2][2] + bias offsets [2][64] (bytes) + barriers;
 // relative adds the staged bias columns [2][64][kColStride]
 constexpr int kColStride = 136;  // 272 B: the 16-byte aligned superset of a 128-node run
 constexpr int HC = 64 / kRowThreads;                     // tile columns per compute thread
-constexpr int kRowsPerWarp = 128 / (kComputeThreads / 32);  // drel write-out rows per compute warp
+// drel write-out: each compute warp writes kRowsPerWarp rows of its own TMEM
+// lane quadrant, whose dX columns the quadrant's four warps staged
+constexpr int kRowsPerWarp = 128 / (kComputeThreads / 32);
+constexpr int kQuadThreads = 128;  // the four compute warps of one lane quadrant
 constexpr int kSmemB = 2 * T128 + 4 * T64 + nx_of(false) * 2 * 128 * 128 + 2 * 64 * 16 + 16 + 2 * 64 + 256 + 1024;
 constexpr int kSmemBrel = 2 * T128 + 4 * T64 + nx_of(true) * 2 * 128 * 128 + 2 * 64 * 16 + 16 + 2 * 64 + 256 + 1024 +
                           2 * 64 * kColStride * 2;
@@ -143,11 +146,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* run_empty = run_full + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(run_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  // relative only: fp32 dX staging [128][65], run info [128][3], row totals
-  // [128], bias runs [2][128][kRunStride]
+  // relative only: fp32 dX staging [128][kDxfStride], run info [128] x
+  // {first distance, length, last staged column, -}, row totals [128], bias
+  // runs [2][128][kRunStride]
   float* dxf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
-  int* rinfo = reinterpret_cast<int*>(dxf + 128 * kDxfStride);
-  int* mtot = rinfo + 128 * 3;
+  int4* rinfo = reinterpret_cast<int4*>(dxf + 128 * kDxfStride);
+  int* mtot = reinterpret_cast<int*>(rinfo + 128);
   uint16_t* run_s = reinterpret_cast<uint16_t*>(mtot + 128);
   uint8_t* sh_s = reinterpret_cast<uint8_t*>(run_s + 2 * 128 * kRunStride);  // [2][128] run offsets
 
@@ -272,6 +276,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float dlt = row_ok ? p.delta[row] : 0.f;
     const bool want_drel = REL && p.drel != nullptr;
     if (want_drel && ch == 0) mtot[r] = row_ok ? visible_count(q, p.s) : 0;
+    // drel write-out rows of this warp: kRowsPerWarp rows of its lane quadrant;
+    // the quadrant's four warps synchronise on barrier 2 + quadrant
+    const int quad = warp & 3, wrow0 = quad * 32 + ch * kRowsPerWarp;
+    const int qbar = 2 + quad;
+    const int64_t drel_stride = (int64_t)p.Hq * p.bins;
+    float* drel_rows = want_drel ? p.drel + (((int64_t)b * p.N + q0 + wrow0) * p.Hq + hq) * p.bins : nullptr;
     int lo = 0, hi = 0, base = 0, cur = -1;
     TileWalk it{-1, 0, 0, q0, q1, 64};
     bool ok = it.start(p.s);
@@ -291,31 +301,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const int bb = j & 1;
-      alive = __all_sync(0xffffffffu, mbar_wait(&s_full[bb], (j >> 1) & 1, abort_flag, status));
-      if (!alive) break;
-      tc_fence_after();
+      // every wait result is warp-uniform; with drel staging the quadrant's
+      // four warps also agree on it, so that all four leave at the same tile
+      bool got = __all_sync(0xffffffffu, mbar_wait(&s_full[bb], (j >> 1) & 1, abort_flag, status));
       float sv[HC], dp[HC];
-      tmem_ld<HC>(tmem + lane_base + bb * 64 + ch * HC, sv);
-      tmem_ld<HC>(tmem + lane_base + 128 + bb * 64 + ch * HC, dp);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&s_free[bb]);
-      if (j >= NX) {  // dX buffer j % NX read by the dQ MMA of tile j - NX
-        alive = __all_sync(0xffffffffu, mbar_wait(&x_free[j % NX], ((j / NX) - 1) & 1, abort_flag, status));
-        if (!alive) break;
+      if (got) {
+        tc_fence_after();
+        tmem_ld<HC>(tmem + lane_base + bb * 64 + ch * HC, sv);
+        tmem_ld<HC>(tmem + lane_base + 128 + bb * 64 + ch * HC, dp);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&s_free[bb]);
       }
+      // dX buffer j % NX read by the dQ MMA of tile j - NX
+      if (got && j >= NX)
+        got = __all_sync(0xffffffffu, mbar_wait(&x_free[j % NX], ((j / NX) - 1) & 1, abort_flag, status));
       const int jlo = lo - it.k0, jhi = hi - it.k0;
       // column c = HC ch + cl has bin distance base - k0 - c: run element
       // 63 - c, i.e. element HC - 1 - cl of this thread's window
       uint32_t run[REL ? HC / 2 : 1];
       if constexpr (REL) {
-        alive = __all_sync(0xffffffffu, mbar_wait(&run_full[bb], (j >> 1) & 1, abort_flag, status));
-        if (!alive) break;
-        load_run_part<HC>(run_s + (bb * 128 + r) * kRunStride, sh_s[bb * 128 + r], ch, run);
-        mbar_arrive(&run_empty[bb]);
+        if (got) got = __all_sync(0xffffffffu, mbar_wait(&run_full[bb], (j >> 1) & 1, abort_flag, status));
+        if (got) {
+          load_run_part<HC>(run_s + (bb * 128 + r) * kRunStride, sh_s[bb * 128 + r], ch, run);
+          mbar_arrive(&run_empty[bb]);
+        }
       }
-      // the single dX staging tile is free once every warp wrote out the last one
-      if (want_drel && j >= 1) named_bar(1, kComputeThreads);
+      // the dX staging rows are free once the quadrant wrote out the last tile
+      if (want_drel) got = named_bar_and(qbar, kQuadThreads, got);
+      if (!got) {
+        alive = false;
+        break;
+      }
       const int ljlo = jlo - ch * HC, ljhi = jhi - ch * HC;  // this thread's columns
       const bool interior = __all_sync(0xffffffffu, ljlo <= 0 && ljhi >= HC);
       const float2 nl2 = make_float2(-lse2, -lse2), nd = make_float2(-dlt, -dlt);
@@ -344,37 +361,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (want_drel) {
         // d rel_logits[q, h, dist] = dX (each (row, distance) once): this row's
         // valid columns [cs, ce) are distances base - k0 - c, one ascending run
-        // in memory; the warp then writes its 32 rows' runs coalesced.
+        // in memory; each warp then writes its rows' runs coalesced, every
+        // load issued before the first store.
         const int cs = max(jlo, 0), ce = min(jhi, 64);
-        if (ch == 0) {
-          int* ri = rinfo + r * 3;
-          ri[0] = base - it.k0 - (ce - 1);
-          ri[1] = (row_ok && lo < hi && ce > cs) ? ce - cs : 0;
-          ri[2] = ce;
-        }
-        named_bar(1, kComputeThreads);
-        const int wc = warp - 4;  // kRowsPerWarp rows per compute warp
-        const float* src = dxf;
-        const int* inf = rinfo;
+        if (ch == 0)
+          rinfo[r] = make_int4(base - it.k0 - (ce - 1), (row_ok && lo < hi && ce > cs) ? ce - cs : 0, ce - 1, 0);
+        named_bar(qbar, kQuadThreads);
+        int4 inf[kRowsPerWarp];
+#pragma unroll
+        for (int k = 0; k < kRowsPerWarp; ++k) inf[k] = rinfo[wrow0 + k];
+        float lo_v[kRowsPerWarp], hi_v[kRowsPerWarp];
+#pragma unroll
         for (int k = 0; k < kRowsPerWarp; ++k) {
-          const int rr = wc * kRowsPerWarp + k;
-          const int n = inf[rr * 3 + 1];
-          if (n == 0) continue;
-          const int dmin = inf[rr * 3], cend = inf[rr * 3 + 2];
-          float* dst = p.drel + (((int64_t)b * p.N + q0 + rr) * p.Hq + hq) * p.bins + dmin;
-          for (int l = lane; l < n; l += 32) dst[l] = src[rr * kDxfStride + (cend - 1 - l)];
+          const float* src = dxf + (wrow0 + k) * kDxfStride + inf[k].z;
+          lo_v[k] = lane < inf[k].y ? src[-lane] : 0.f;
+          hi_v[k] = lane + 32 < inf[k].y ? src[-lane - 32] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < kRowsPerWarp; ++k) {
+          float* dst = drel_rows + k * drel_stride + inf[k].x;
+          if (lane < inf[k].y) dst[lane] = lo_v[k];
+          if (lane + 32 < inf[k].y) dst[lane + 32] = hi_v[k];
         }
       }
     }
-    if (want_drel) {  // every compute warp reaches this barrier, also after an abort
+    if (want_drel) {  // the quadrant's four warps all reach this barrier, also after an abort
       // distances at or beyond a row's visible count are never attended: zero them
-      named_bar(1, kComputeThreads);
-      const int wc = warp - 4;
+      named_bar(qbar, kQuadThreads);
       for (int k = 0; k < kRowsPerWarp; ++k) {
-        const int rr = wc * kRowsPerWarp + k;
-        if (q0 + rr >= p.N) break;
-        float* dst = p.drel + (((int64_t)b * p.N + q0 + rr) * p.Hq + hq) * p.bins;
-        for (int d = mtot[rr] + lane; d < p.bins; d += 32) dst[d] = 0.f;
+        if (q0 + wrow0 + k >= p.N) break;
+        float* dst = drel_rows + k * drel_stride;
+        for (int d = mtot[wrow0 + k] + lane; d < p.bins; d += 32) dst[d] = 0.f;
       }
     }
     if (alive && j >= 1) alive = __all_sync(0xffffffffu, mbar_wait(dq_done, 0, abort_flag, status));

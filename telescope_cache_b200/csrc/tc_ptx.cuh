@@ -103,6 +103,19 @@ __device__ __forceinline__ void fence_async_smem() {
 __device__ __forceinline__ void named_bar(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
+// Named barrier that also returns the AND of `v` over its n participants.
+__device__ __forceinline__ bool named_bar_and(int id, int n, bool v) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.b32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1 : 0), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
 
 // ---------------------------------------------------------------------------
 // tcgen05
