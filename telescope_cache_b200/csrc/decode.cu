@@ -37,11 +37,24 @@ template <int DM> struct DecShared {
   float w_new;
 };
 
+// What the advance alone needs (no attention state): a few KB, so every
+// (batch, KV head) CTA of a step is resident at once.
+template <int DM> struct AdvShared {
+  float kt[DM], vt[DM];
+  float qs[MAXE][DM];
+  float st[MAXE][32];
+  float wbuf[1][DM];
+  int lo_s[TC_MAX_LEVELS], hi_s[TC_MAX_LEVELS], base_s[TC_MAX_LEVELS], pre_s[TC_MAX_LEVELS + 1];
+  int roff_s[TC_MAX_LEVELS + 1], caps_s[TC_MAX_LEVELS];
+  float w_new;
+};
+
 // Steps 1-4 of the step (conv, merge weight, ruler-tick merge, level-0
 // write), then the visible ranges of query t and the query rows.  Returns
-// false when the mode does not attend (every thread agrees).
-template <typename T, int DM>
-__device__ bool decode_prologue(const DecParams& P, DecShared<DM>& S) {
+// false when the mode does not attend (every thread agrees).  SH is
+// DecShared<DM> or, for the advance alone, AdvShared<DM>.
+template <typename T, int DM, typename SH>
+__device__ bool decode_prologue(const DecParams& P, SH& S) {
   const tc_decode_args& a = P.a;
   const int b = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -87,11 +100,24 @@ __device__ bool decode_prologue(const DecParams& P, DecShared<DM>& S) {
     T* nout = static_cast<T*>(isk ? a.k_new : a.v_new);
     if (nout) nout[((int64_t)b * a.Hkv + h) * D + dd] = from_f<T>(y);
   }
-  // raw query rows of the group
+  // raw query rows of the group; with rope, the cos / sin of position t for
+  // the query rotation below are fetched in the same round trip
   const T* qt = static_cast<const T*>(a.q_t);
-  for (int i = tid; i < E * a.Dk; i += NT) {
-    const int e = i / a.Dk, d = i - e * a.Dk;
-    S.qs[e][d] = to_f(qt[((int64_t)b * a.Hq + h * E + e) * a.Dk + d]);
+  const bool rope_q = attend && a.position_mode == TC_POS_ROPE;
+  constexpr int kQPer = MAXE * DM / NT + 1;
+  float qc[kQPer], qsn[kQPer];
+  {
+    const int hd = a.Dk / 2;
+    int cnt = 0;
+    for (int i = tid; i < E * a.Dk; i += NT, ++cnt) {
+      const int e = i / a.Dk, d = i - e * a.Dk;
+      S.qs[e][d] = to_f(qt[((int64_t)b * a.Hq + h * E + e) * a.Dk + d]);
+      if (rope_q) {
+        const int ii = d < hd ? d : d - hd;
+        qc[cnt] = a.rope_cos[(int64_t)t * hd + ii];
+        qsn[cnt] = a.rope_sin[(int64_t)t * hd + ii];
+      }
+    }
   }
   if (a.position_mode == TC_POS_RELATIVE) {
     for (int i = tid; i < E * a.d_rel; i += NT) {
@@ -194,14 +220,14 @@ __device__ bool decode_prologue(const DecParams& P, DecShared<DM>& S) {
     S.roff_s[a.num_levels] = a.ring_off[a.num_levels];
   }
   __syncthreads();
-  if (a.position_mode == TC_POS_ROPE) {
+  if (rope_q) {
     const int hd = a.Dk / 2;
-    float rq[MAXE * DM / NT + 1];
+    float rq[kQPer];
     int cnt = 0;
     for (int i = tid; i < E * a.Dk; i += NT, ++cnt) {
       const int e = i / a.Dk, d = i - e * a.Dk;
       const int ii = d < hd ? d : d - hd;
-      const float c = a.rope_cos[(int64_t)t * hd + ii], s = a.rope_sin[(int64_t)t * hd + ii];
+      const float c = qc[cnt], s = qsn[cnt];
       const float x1 = S.qs[e][ii], x2 = S.qs[e][ii + hd];
       rq[cnt] = round_to<T>(d < hd ? x1 * c - x2 * s : x2 * c + x1 * s);
     }
@@ -290,6 +316,14 @@ __global__ void __launch_bounds__(NT) decode_combine_kernel(DecParams P, int spl
     }
     finish_elem<T>(a, b, h, e, d, mx, ls, o);
   }
+}
+
+// The advance alone (steps 1-4) for the split path: small shared memory and
+// registers, so a step's CTAs run as one wave.
+template <typename T>
+__global__ void __launch_bounds__(NT, 8) decode_advance_kernel(DecParams P) {
+  __shared__ AdvShared<128> S;
+  decode_prologue<T, 128>(P, S);
 }
 
 // Generic variant: any Dk, Dv <= DM, any element type; warp w takes entries
@@ -696,7 +730,8 @@ int launch_decode(const DecParams& P, int E, int d, dim3 grid, cudaStream_t st) 
       if (P.a.mode != TC_DECODE_ATTEND) {
         DecParams adv = P;
         adv.a.mode = TC_DECODE_ADVANCE;
-        if (int rc = launch128<T>(adv, E, grid, st)) return rc;
+        decode_advance_kernel<T><<<grid, NT, 0, st>>>(adv);
+        if (int rc = launch_status()) return rc;
       }
       if (P.a.mode != TC_DECODE_ADVANCE) {
         DecParams att = P;
