@@ -10,7 +10,7 @@
 //                             double buffered for 64-node tiles, so the
 //                             softmax only waits on a PV product before a
 //                             lazy O rescale or a P buffer reuse)
-//   warps 2, 3  relative bias staging: bulk copies of each row's bias run
+//   warps 2, 3  relative bias staging: 16-byte cp.async copies of each row's bias run
 //   warps 4..   softmax:      kRowThreads threads per query row (= TMEM
 //                             lane), each with a slice of the tile's
 //                             columns: exact per-row
@@ -110,8 +110,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_empty = p_full + NP;   // [NP] PV(j) done: buffer free, O up to date
   uint64_t* run_full = p_empty + NP; // relative: staged bias runs ready (warps 2-3)
   uint64_t* run_empty = run_full + 2;
-  uint64_t* xch = run_empty + 2;     // [2] row-maximum exchange, [2] final row sum
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xch + 3);
+  // per lane quadrant (the four warps that hold a row's threads): [2] row
+  // maximum exchange, [1] final row sum
+  uint64_t* xch = run_empty + 2;     // [3][4]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xch + 12);
+  static_assert((1 + 2 * NS + 2 + 2 + 2 * NP + 2 + 2 + 12) * 8 + 8 <= 256,
+                "forward barriers, TMEM address and abort flag exceed their 256-byte area");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* xs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [3][kRowThreads][128]
   uint16_t* run_s = reinterpret_cast<uint16_t*>(xs + 3 * kRowThreads * 128);     // [2][128][72]
@@ -134,7 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&run_full[i], 64);
       mbar_init(&run_empty[i], kComputeThreads);
     }
-    for (int i = 0; i < 3; ++i) mbar_init(&xch[i], kComputeThreads);
+    for (int i = 0; i < 12; ++i) mbar_init(&xch[i], kComputeThreads / 4);
     for (int i = 0; i < NP; ++i) {
       mbar_init(&p_full[i], kComputeThreads);
       mbar_init(&p_empty[i], 1);
@@ -229,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < 4) {
     // ---------------- relative bias staging (warps 2, 3) ----------------
     if constexpr (REL)
-      stage_runs(threadIdx.x - 64, q0, q1, p.N, p.Hq, hq, b, p.s, p.rl, p.rl_stride, p.rl_pad, run_s, sh_s,
+      stage_runs<true>(threadIdx.x - 64, q0, q1, p.N, p.Hq, hq, b, p.s, p.rl, p.rl_stride, p.rl_pad, run_s, sh_s,
                  run_full, run_empty, abort_flag, status);
   } else {
     // ---------------- softmax / epilogue: kRowThreads threads per query row ----------------
@@ -240,7 +244,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ch = (threadIdx.x - 128) >> 7;
     const int q = q0 + r;
     const bool row_ok = q < p.N;
-    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const int quad = warp & 3;  // TMEM lane quadrant: rows 32 quad .. 32 quad + 31
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     // logit2 = (S * scale + bias) * log2(e), softcapped: cap * tanh(. / cap) * log2(e)
     const float kq = p.has_cap ? p.scale / p.cap : p.scale * kLog2e;
     const float kb = p.has_cap ? 1.f / p.cap : kLog2e;
@@ -287,8 +292,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (CAP) mloc *= kc;  // log2 units (kc > 0 keeps the order; -inf stays -inf)
       // row maximum over the row's threads (bounded wait on the exchange barrier)
       xs[bb * XS + ch * 128 + r] = mloc;
-      mbar_arrive(&xch[bb]);
-      alive = __all_sync(0xffffffffu, mbar_wait(&xch[bb], (j >> 1) & 1, abort_flag, status));
+      mbar_arrive(&xch[bb * 4 + quad]);
+      alive = __all_sync(0xffffffffu, mbar_wait(&xch[bb * 4 + quad], (j >> 1) & 1, abort_flag, status));
       if (!alive) break;
       float mx = xs[bb * XS + r];
 #pragma unroll
@@ -359,8 +364,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (alive && j >= 1) {
       // the row sum over the row's threads
       xs[2 * XS + ch * 128 + r] = ell;
-      mbar_arrive(&xch[2]);
-      alive = __all_sync(0xffffffffu, mbar_wait(&xch[2], 0, abort_flag, status));
+      mbar_arrive(&xch[8 + quad]);
+      alive = __all_sync(0xffffffffu, mbar_wait(&xch[8 + quad], 0, abort_flag, status));
     }
     if (alive && j >= 1) {
       tc_fence_after();

@@ -31,11 +31,14 @@ constexpr int B64 = 64 * 128;        // one 64-col block of a 64-row tile
 // dX tiles the accumulate MMAs read: double buffered (NX = 2) unless the
 // relative variant's staging leaves no room
 constexpr int nx_of(bool rel) { return rel ? 1 : 2; }
-constexpr int kSmemA = 2 * T128 + 4 * T64 + nx_of(false) * 128 * 128 + 1024 + 256;
+// Pass A K/V stages: three, so a tile's TMA load starts two tiles before its
+// MMAs, unless the relative variant's staging leaves no room
+constexpr int nkv_of(bool rel) { return rel ? 2 : 3; }
+constexpr int kSmemA = 2 * T128 + 2 * nkv_of(false) * T64 + nx_of(false) * 128 * 128 + 1024 + 256;
 // relative Pass A: + an fp32 dX staging tile [128 x 66], per-row run info,
 // row totals and the double-buffered bias runs [2][128][kRunStride]
 constexpr int kDxfStride = 66;  // even: 8-byte column pairs; 16 rows per phase hit distinct banks
-constexpr int kSmemArel = 2 * T128 + 4 * T64 + nx_of(true) * 128 * 128 + 1024 + 256 + 128 * kDxfStride * 4 + 128 * 4 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2 + 256;
+constexpr int kSmemArel = 2 * T128 + 2 * nkv_of(true) * T64 + nx_of(true) * 128 * 128 + 1024 + 256 + 128 * kDxfStride * 4 + 128 * 4 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2 + 256;
 // Pass B: tiles + per-step query info [2][64] x {lo, hi, -lse2, -Delta} + the
 // per-warp interior flags [2][2] + bias offsets [2][64] (bytes) + barriers;
 // relative adds the staged bias columns [2][64][kColStride]
@@ -80,19 +83,6 @@ struct BwdScalars {
       : kq(p.has_cap ? p.scale / p.cap : p.scale * kLog2e),
         kb(p.has_cap ? 1.f / p.cap : kLog2e),
         kc(p.cap * kLog2e) {}
-  // s: raw accumulator S, bias: relative bias (natural units).  Returns the
-  // log2-domain logit and the softcap derivative 1 - tanh^2 (1 without cap).
-  __device__ __forceinline__ void logit(float s, float bias, int has_cap, float* l2, float* g) const {
-    const float x = fmaf(s, kq, bias * kb);
-    if (has_cap) {
-      const float t = tanh_fast(x);
-      *l2 = t * kc;
-      *g = 1.f - t * t;
-    } else {
-      *l2 = x;
-      *g = 1.f;
-    }
-  }
 };
 
 // dX = P (dP - Delta) softcap' for two columns, with P = exp2(logit2 - lse2):
@@ -129,17 +119,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_s = sm;
   uint8_t* g_s = q_s + T128;
-  uint8_t* k_s = g_s + T128;   // [2] x T64
-  uint8_t* v_s = k_s + 2 * T64;
-  constexpr int NX = nx_of(REL);
-  uint8_t* x_s = v_s + 2 * T64;  // [NX] dX [128 x 64]
+  constexpr int NX = nx_of(REL), NKV = nkv_of(REL);
+  uint8_t* k_s = g_s + T128;       // [NKV] x T64
+  uint8_t* v_s = k_s + NKV * T64;  // [NKV] x T64
+  uint8_t* x_s = v_s + NKV * T64;  // [NX] dX [128 x 64]
   uint64_t* bars = reinterpret_cast<uint64_t*>(x_s + NX * 128 * 128);
   uint64_t* qg_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 3;
-  uint64_t* s_full = bars + 5;
-  uint64_t* s_free = bars + 7;
-  uint64_t* x_full = bars + 9;       // [NX]
+  uint64_t* kv_full = bars + 1;         // [NKV]
+  uint64_t* kv_empty = kv_full + NKV;   // [NKV]
+  uint64_t* s_full = kv_empty + NKV;    // [2]
+  uint64_t* s_free = s_full + 2;        // [2]
+  uint64_t* x_full = s_free + 2;        // [NX]
   uint64_t* x_free = x_full + NX;    // [NX]
   uint64_t* dq_done = x_free + NX;
   uint64_t* run_full = dq_done + 1;  // relative: staged bias runs ready (warps 2-3)
@@ -164,12 +154,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(qg_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kComputeThreads);
       mbar_init(&run_full[i], 64);
       mbar_init(&run_empty[i], kComputeThreads);
+    }
+    for (int i = 0; i < NKV; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
     }
     for (int i = 0; i < NX; ++i) {
       mbar_init(&x_full[i], kComputeThreads);
@@ -198,8 +190,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       TileWalk it{-1, 0, 0, q0, q1, 64};
       bool ok = it.start(p.s);
       for (int j = 0; ok; ++j, ok = it.advance(p.s)) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1, abort_flag, status)) break;
+        const int st = j % NKV;
+        if (j >= NKV && !mbar_wait(&kv_empty[st], ((j / NKV) - 1) & 1, abort_flag, status)) break;
         mbar_expect_tx(&kv_full[st], 2 * T64);
         const int row = p.s.off[it.lev] + it.k0;
         tma_load_4d(k_s + st * T64, &tmk, 0, hkv, row, b, &kv_full[st]);
@@ -214,13 +206,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t kIdQ = idesc_f16(128, 128, Pack2<T>::kFmt, 0, 1);
       const uint32_t qa = smem_addr(q_s), ga = smem_addr(g_s), xa = smem_addr(x_s);
       auto issue_dq = [&](int t) {
-        const uint32_t ka = smem_addr(k_s + (t & 1) * T64), xb = xa + (t % NX) * 128 * 128;
+        const uint32_t ka = smem_addr(k_s + (t % NKV) * T64), xb = xa + (t % NX) * 128 * 128;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_f16(tmem + 256, sdesc_sw128(xb + kk * 32, 16, 1024), sdesc_sw128(ka + kk * 2048, B64, 1024), kIdQ,
                   (t > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&x_free[t % NX]);
-        mma_commit(&kv_empty[t & 1]);
+        mma_commit(&kv_empty[t % NKV]);
       };
       bool alive = mbar_wait(qg_full, 0, abort_flag, status);
       tc_fence_after();
@@ -228,8 +220,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = alive && it.start(p.s);
       int j = 0;
       for (; ok; ++j, ok = it.advance(p.s)) {
-        const int st = j & 1, bb = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, abort_flag, status)) { alive = false; break; }
+        const int st = j % NKV, bb = j & 1;
+        if (!mbar_wait(&kv_full[st], (j / NKV) & 1, abort_flag, status)) { alive = false; break; }
         if (j >= 2 && !mbar_wait(&s_free[bb], ((j >> 1) - 1) & 1, abort_flag, status)) { alive = false; break; }
         tc_fence_after();
         const uint32_t ka = smem_addr(k_s + st * T64), va = smem_addr(v_s + st * T64);
@@ -262,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < 4) {
     // relative bias staging (warps 2, 3)
     if constexpr (REL)
-      stage_runs(threadIdx.x - 64, q0, q1, p.N, p.Hq, hq, b, p.s, p.rl, p.rl_stride, p.rl_pad, run_s, sh_s,
+      stage_runs<false>(threadIdx.x - 64, q0, q1, p.N, p.Hq, hq, b, p.s, p.rl, p.rl_stride, p.rl_pad, run_s, sh_s,
                  run_full, run_empty, abort_flag, status);
   } else {
     const int r = (threadIdx.x - 128) & 127;  // query row = TMEM lane

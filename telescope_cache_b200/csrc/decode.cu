@@ -25,13 +25,15 @@ struct DecParams {
   float scale;
 };
 
-template <int DM> struct DecShared {
+// ME: query heads per KV head it holds; WB: rotation buffers (one per warp
+// for the generic variant, one for the merged key otherwise).
+template <int DM, int ME = MAXE, int WB = NW> struct DecShared {
   float kt[DM], vt[DM];
-  float qs[MAXE][DM];           // query rows of the group (rotated for rope)
-  float st[MAXE][32];           // relative states of the group
-  float wbuf[NW][DM];           // generic variant: one key per warp for the rotation
-  float part_m[NW][MAXE], part_l[NW][MAXE];
-  float part_acc[NW][MAXE][DM];
+  float qs[ME][DM];             // query rows of the group (rotated for rope)
+  float st[ME][32];             // relative states of the group
+  float wbuf[WB][DM];           // generic variant: one key per warp for the rotation
+  float part_m[NW][ME], part_l[NW][ME];
+  float part_acc[NW][ME][DM];
   int lo_s[TC_MAX_LEVELS], hi_s[TC_MAX_LEVELS], base_s[TC_MAX_LEVELS], pre_s[TC_MAX_LEVELS + 1];
   int roff_s[TC_MAX_LEVELS + 1], caps_s[TC_MAX_LEVELS];
   float w_new;
@@ -266,8 +268,8 @@ __device__ __forceinline__ void finish_elem(const tc_decode_args& a, int b, int 
 // Merge the warps' partial softmax states (part_m / part_l / part_acc).  With
 // one CTA per (batch, KV head) it finishes the outputs; a split CTA writes
 // its merged state {m, l, acc[Dv]} to the workspace slot (b, h, split, e).
-template <typename T, int DM>
-__device__ void decode_epilogue(const DecParams& P, DecShared<DM>& S) {
+template <typename T, int DM, typename SH>
+__device__ void decode_epilogue(const DecParams& P, SH& S) {
   const tc_decode_args& a = P.a;
   const int b = blockIdx.x, h = blockIdx.y;
   const int E = a.Hq / a.Hkv;
@@ -465,11 +467,6 @@ __device__ __forceinline__ float2 round2(float2 v) {
   } else {
     return __half22float2(__floats2half2_rn(v.x, v.y));
   }
-}
-
-__device__ __forceinline__ uint4 shfl_xor4(const uint4& v, int m) {
-  return make_uint4(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m),
-                    __shfl_xor_sync(0xffffffffu, v.z, m), __shfl_xor_sync(0xffffffffu, v.w, m));
 }
 
 // Dk = Dv = 128, 16-bit rings, E query heads per KV head.  Group g0 covers
@@ -701,13 +698,15 @@ inline int sm_count() {
   return n;
 }
 
-// Splits of each (batch, KV head)'s entries: enough CTAs for ~16 per SM,
-// at least 256 entries per split, at most kMaxSplits and what the workspace holds.
+// Splits of each (batch, KV head)'s entries: enough CTAs for ~4 per SM (a
+// split costs a prologue, a workspace round trip and the extra advance and
+// combine launches, so enough units run unsplit), at least 256 entries per
+// split, at most kMaxSplits and what the workspace holds.
 constexpr int kMaxSplits = 8;
 inline int decode_splits(const tc_decode_args& a, int E) {
   if (!a.workspace) return 1;
   const int64_t units = (int64_t)a.B * a.Hkv;
-  int s = (int)((16LL * sm_count() + units - 1) / units);
+  int s = (int)((4LL * sm_count() + units - 1) / units);
   s = s < 1 ? 1 : (s > kMaxSplits ? kMaxSplits : s);
   const int by_entries = a.cache_size / 256;
   if (s > by_entries) s = by_entries < 1 ? 1 : by_entries;

@@ -179,10 +179,14 @@ constexpr int kRunStride = 72;  // elements per staged row (144 B: 16-B accesses
 // walk and every query row r of the block, the bias run of the row
 // (rl[row, pad + base_r - k0 - 63 + i], i < 64) lands in run_s[buf][r] as its
 // 16-byte aligned 144-byte superset: run element i is raw element
-// sh_s[buf][r] + i.  Thread t (0..63 of warps 2-3) owns rows t and t + 64 and
-// issues one bulk copy per visible row; completion is counted on
-// run_full[buf] (one arrival per thread plus the copied bytes).  Rows without
-// a visible node in the tile are not copied: their columns are masked.
+// sh_s[buf][r] + i.  Thread t (0..63 of warps 2-3) owns rows t and t + 64.
+// LSU: each visible row is copied in nine 16-byte cp.async pieces through the
+// load/store path (the forward, where 128 short bulk copies a tile would queue
+// in the TMA unit); otherwise one bulk copy per row (Pass A, whose load/store
+// path is busy with its own drel stores).  run_full[buf] completes when every
+// thread arrived and its copies landed.  Rows without a visible node in the
+// tile are not copied: their columns are masked.
+template <bool LSU>
 __device__ __forceinline__ void stage_runs(int t, int q0, int q1, int N, int Hq, int hq, int b, const Sched& s,
                                            const uint16_t* rl, int64_t stride, int pad, uint16_t* run_s,
                                            uint8_t* sh_s, uint64_t* run_full, uint64_t* run_empty,
@@ -213,21 +217,34 @@ __device__ __forceinline__ void stage_runs(int t, int q0, int q1, int N, int Hq,
     }
     bool vis[2];
     int64_t src[2];
-    uint32_t bytes = 0;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       vis[h] = lo[h] < hi[h] && lo[h] - it.k0 < 64 && hi[h] - it.k0 > 0;
       const int64_t e0 = roff[h] + base[h] - it.k0 - 63;
       src[h] = e0 & ~int64_t(7);
       sh_s[buf * 128 + t + 64 * h] = (uint8_t)(e0 - src[h]);
-      if (vis[h]) bytes += kRunStride * 2;
     }
-    if (bytes) ptx::mbar_expect_tx(&run_full[buf], bytes);  // this thread's arrival + its bytes
-    else ptx::mbar_arrive(&run_full[buf]);
+    if constexpr (LSU) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
-      if (vis[h])
-        ptx::bulk_load(run_s + (buf * 128 + t + 64 * h) * kRunStride, rl + src[h], kRunStride * 2, &run_full[buf]);
+      for (int h = 0; h < 2; ++h) {
+        if (vis[h]) {
+          const uint4* g = reinterpret_cast<const uint4*>(rl + src[h]);
+          uint4* d = reinterpret_cast<uint4*>(run_s + (buf * 128 + t + 64 * h) * kRunStride);
+#pragma unroll
+          for (int k = 0; k < kRunStride / 8; ++k) ptx::cp_async16(d + k, g + k);
+        }
+      }
+      ptx::cp_async_track(&run_full[buf]);
+      ptx::mbar_arrive(&run_full[buf]);
+    } else {
+      const uint32_t bytes = (vis[0] ? kRunStride * 2 : 0) + (vis[1] ? kRunStride * 2 : 0);
+      if (bytes) ptx::mbar_expect_tx(&run_full[buf], bytes);  // this thread's arrival + its bytes
+      else ptx::mbar_arrive(&run_full[buf]);
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        if (vis[h])
+          ptx::bulk_load(run_s + (buf * 128 + t + 64 * h) * kRunStride, rl + src[h], kRunStride * 2, &run_full[buf]);
+    }
   }
 }
 

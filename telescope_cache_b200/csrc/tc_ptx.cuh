@@ -93,6 +93,19 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
 }
+// 16 bytes global -> shared through the load/store path (not the TMA unit):
+// dst and src 16-byte aligned.  Completion is tracked by cp_async_track.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)),
+               "l"(reinterpret_cast<uint64_t>(src))
+               : "memory");
+}
+// Hold `bar`'s current phase open until every cp_async16 this thread issued
+// so far has landed (one more pending arrival, made when they complete); the
+// thread's own arrival is separate (mbar_arrive).
+__device__ __forceinline__ void cp_async_track(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
