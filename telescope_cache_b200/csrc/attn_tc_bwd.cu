@@ -657,42 +657,57 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       alive = __all_sync(0xffffffffu, mbar_wait(&info_full[bb], (i >> 1) & 1, abort_flag, status));
       if (!alive) break;
-      const uint8_t* bo = bo_s + bb * 64;
       const uint16_t* bcol = bias_s + bb * 64 * kColStride + 127 - r;
       const bool interior = in_s[bb * 2 + ((ch * HC) >> 5)] != 0;
-      float pr[HC], dx[HC];
+      // eight query columns at a time: their step info (and bias offsets) with
+      // vector loads, every bias load issued before the math, P^T and dX^T
+      // packed and stored as soon as the eight are done
 #pragma unroll
-      for (int cl = 0; cl < HC; cl += 2) {
-        const int c = ch * HC + cl;
-        float2 bias = make_float2(0.f, 0.f);
+      for (int c8 = 0; c8 < HC / 8; ++c8) {
+        const int c0 = ch * HC + c8 * 8;
+        float bias[8];
         if constexpr (REL) {
           // lanes hold consecutive nodes: consecutive (descending) halves
-          bias.x = bits_to_float<T>(bcol[c * kColStride + bo[c]]);
-          bias.y = bits_to_float<T>(bcol[(c + 1) * kColStride + bo[c + 1]]);
-        }
-        const float2 nl2 = *reinterpret_cast<const float2*>(nl_s + bb * 64 + c);
-        const float2 nd = *reinterpret_cast<const float2*>(nd_s + bb * 64 + c);
-        float2 p2;
-        float2 v = dx_pair<REL, CAP>(make_float2(sv[cl], sv[cl + 1]), bias, make_float2(dp[cl], dp[cl + 1]), nl2,
-                                     nd, sc.kq, sc.kb, sc.kc, &p2);
-        if (!interior) {
-          const bool v0 = node_ok && jn >= lo_s[bb * 64 + c] && jn < hi_s[bb * 64 + c];
-          const bool v1 = node_ok && jn >= lo_s[bb * 64 + c + 1] && jn < hi_s[bb * 64 + c + 1];
-          p2.x = v0 ? p2.x : 0.f;
-          p2.y = v1 ? p2.y : 0.f;
-          v.x = v0 ? v.x : 0.f;
-          v.y = v1 ? v.y : 0.f;
-        }
-        pr[cl] = p2.x;
-        pr[cl + 1] = p2.y;
-        dx[cl] = v.x;
-        dx[cl + 1] = v.y;
-      }
+          const uint2 o8 = *reinterpret_cast<const uint2*>(bo_s + bb * 64 + c0);
 #pragma unroll
-      for (int cc8 = 0; cc8 < HC / 8; ++cc8) {
-        const uint32_t off = (i % NX) * 128 * 128 + sw128_offset(r, (ch * (HC / 8) + cc8) * 8, 128);
-        *reinterpret_cast<uint4*>(pt_s + off) = pack8<T>(pr + cc8 * 8, 1.f);
-        *reinterpret_cast<uint4*>(xt_s + off) = pack8<T>(dx + cc8 * 8, 1.f);
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t o = ((k < 4 ? o8.x : o8.y) >> (8 * (k & 3))) & 0xffu;
+            bias[k] = bits_to_float<T>(bcol[(c0 + k) * kColStride + o]);
+          }
+        }
+        float nl[8], nd[8];
+#pragma unroll
+        for (int k = 0; k < 8; k += 4) {
+          const float4 a4 = *reinterpret_cast<const float4*>(nl_s + bb * 64 + c0 + k);
+          const float4 d4 = *reinterpret_cast<const float4*>(nd_s + bb * 64 + c0 + k);
+          nl[k] = a4.x, nl[k + 1] = a4.y, nl[k + 2] = a4.z, nl[k + 3] = a4.w;
+          nd[k] = d4.x, nd[k + 1] = d4.y, nd[k + 2] = d4.z, nd[k + 3] = d4.w;
+        }
+        float pr[8], dx[8];
+#pragma unroll
+        for (int k = 0; k < 8; k += 2) {
+          const int cl = c8 * 8 + k, c = c0 + k;
+          float2 p2;
+          float2 v = dx_pair<REL, CAP>(make_float2(sv[cl], sv[cl + 1]),
+                                       REL ? make_float2(bias[k], bias[k + 1]) : make_float2(0.f, 0.f),
+                                       make_float2(dp[cl], dp[cl + 1]), make_float2(nl[k], nl[k + 1]),
+                                       make_float2(nd[k], nd[k + 1]), sc.kq, sc.kb, sc.kc, &p2);
+          if (!interior) {
+            const bool v0 = node_ok && jn >= lo_s[bb * 64 + c] && jn < hi_s[bb * 64 + c];
+            const bool v1 = node_ok && jn >= lo_s[bb * 64 + c + 1] && jn < hi_s[bb * 64 + c + 1];
+            p2.x = v0 ? p2.x : 0.f;
+            p2.y = v1 ? p2.y : 0.f;
+            v.x = v0 ? v.x : 0.f;
+            v.y = v1 ? v.y : 0.f;
+          }
+          pr[k] = p2.x;
+          pr[k + 1] = p2.y;
+          dx[k] = v.x;
+          dx[k + 1] = v.y;
+        }
+        const uint32_t off = (i % NX) * 128 * 128 + sw128_offset(r, (ch * (HC / 8) + c8) * 8, 128);
+        *reinterpret_cast<uint4*>(pt_s + off) = pack8<T>(pr, 1.f);
+        *reinterpret_cast<uint4*>(xt_s + off) = pack8<T>(dx, 1.f);
       }
       mbar_arrive(&info_empty[bb]);
       fence_async_smem();
