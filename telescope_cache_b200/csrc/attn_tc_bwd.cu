@@ -39,18 +39,23 @@ constexpr int kSmemA = 2 * T128 + 2 * nkv_of(false) * T64 + nx_of(false) * 128 *
 // row totals and the double-buffered bias runs [2][128][kRunStride]
 constexpr int kDxfStride = 66;  // even: 8-byte column pairs; 16 rows per phase hit distinct banks
 constexpr int kSmemArel = 2 * T128 + 2 * nkv_of(true) * T64 + nx_of(true) * 128 * 128 + 1024 + 256 + 128 * kDxfStride * 4 + 128 * 4 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2 + 256;
-// Pass B: tiles + per-step query info [2][64] x {lo, hi, -lse2, -Delta} + the
-// per-warp interior flags [2][2] + bias offsets [2][64] (bytes) + barriers;
-// relative adds the staged bias columns [2][64][kColStride]
+// Pass B: tiles (NQ Q/dO stages: three, so a step's TMA load starts two
+// steps before its MMAs, unless the relative variant's staging leaves no
+// room) + per-step query info [2][64] x {-lse2, -Delta} (fp32) and {lo, hi}
+// (bytes, relative to the tile) + the per-warp interior flags [2][2] + bias
+// offsets [2][64] (bytes) + barriers; relative adds the staged bias columns
+// [2][64][kColStride]
 constexpr int kColStride = 136;  // 272 B: the 16-byte aligned superset of a 128-node run
 constexpr int HC = 64 / kRowThreads;                     // tile columns per compute thread
 // drel write-out: each compute warp writes kRowsPerWarp rows of its own TMEM
 // lane quadrant, whose dX columns the quadrant's four warps staged
 constexpr int kRowsPerWarp = 128 / (kComputeThreads / 32);
 constexpr int kQuadThreads = 128;  // the four compute warps of one lane quadrant
-constexpr int kSmemB = 2 * T128 + 4 * T64 + nx_of(false) * 2 * 128 * 128 + 2 * 64 * 16 + 16 + 2 * 64 + 256 + 1024;
-constexpr int kSmemBrel = 2 * T128 + 4 * T64 + nx_of(true) * 2 * 128 * 128 + 2 * 64 * 16 + 16 + 2 * 64 + 256 + 1024 +
-                          2 * 64 * kColStride * 2;
+constexpr int nq_of(bool rel) { return rel ? 2 : 3; }
+constexpr int kSmemB = 2 * T128 + 2 * nq_of(false) * T64 + nx_of(false) * 2 * 128 * 128 + 2 * 64 * 8 + 16 +
+                       3 * 2 * 64 + 256 + 1024;
+constexpr int kSmemBrel = 2 * T128 + 2 * nq_of(true) * T64 + nx_of(true) * 2 * 128 * 128 + 2 * 64 * 8 + 16 +
+                          3 * 2 * 64 + 256 + 1024 + 2 * 64 * kColStride * 2;
 
 constexpr int kMaxSmem = 227 * 1024;  // dynamic shared memory per CTA on sm_100
 static_assert(kSmemA <= kMaxSmem && kSmemArel <= kMaxSmem && kSmemB <= kMaxSmem && kSmemBrel <= kMaxSmem,
@@ -432,32 +437,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* k_s = sm;
   uint8_t* v_s = k_s + T128;
-  uint8_t* q_s = v_s + T128;   // [2] x T64
-  uint8_t* g_s = q_s + 2 * T64;
-  constexpr int NX = nx_of(REL);
-  uint8_t* pt_s = g_s + 2 * T64;          // [NX] P^T  [128 x 64]
+  constexpr int NX = nx_of(REL), NQ = nq_of(REL);
+  uint8_t* q_s = v_s + T128;              // [NQ] x T64
+  uint8_t* g_s = q_s + NQ * T64;          // [NQ] x T64
+  uint8_t* pt_s = g_s + NQ * T64;         // [NX] P^T  [128 x 64]
   uint8_t* xt_s = pt_s + NX * 128 * 128;  // [NX] dX^T [128 x 64]
-  // per step (double buffered), per query column: lo, hi, -lse * log2e, -Delta
-  int* lo_s = reinterpret_cast<int*>(xt_s + NX * 128 * 128);  // [2][64]
-  int* hi_s = lo_s + 2 * 64;
-  float* nl_s = reinterpret_cast<float*>(hi_s + 2 * 64);
+  // per step (double buffered), per query column: -lse * log2e, -Delta, and
+  // the visible nodes [lo, hi) clamped to the tile's [0, 128]
+  float* nl_s = reinterpret_cast<float*>(xt_s + NX * 128 * 128);  // [2][64]
   float* nd_s = nl_s + 2 * 64;
-  int* in_s = reinterpret_cast<int*>(nd_s + 2 * 64);         // [2][2]: every node of the tile visible to every
-                                                             // query of staging warp 2 / 3's 32 columns
-  uint8_t* bo_s = reinterpret_cast<uint8_t*>(in_s + 4);      // [2][64] relative: run offset - 127
+  int* in_s = reinterpret_cast<int*>(nd_s + 2 * 64);  // [2][2]: every node of the tile visible to every
+                                                      // query of staging warp 2 / 3's 32 columns
+  uint8_t* lo_s = reinterpret_cast<uint8_t*>(in_s + 4);  // [2][64]
+  uint8_t* hi_s = lo_s + 2 * 64;                         // [2][64]
+  uint8_t* bo_s = hi_s + 2 * 64;                         // [2][64] relative: run offset - 127
   uint64_t* bars = reinterpret_cast<uint64_t*>(bo_s + 2 * 64);
   uint64_t* kv_full = bars;
-  uint64_t* q_full = bars + 1;
-  uint64_t* q_empty = bars + 3;
-  uint64_t* s_full = bars + 5;
-  uint64_t* s_free = bars + 7;
-  uint64_t* x_full = bars + 9;        // [NX]
+  uint64_t* q_full = bars + 1;        // [NQ]
+  uint64_t* q_empty = q_full + NQ;    // [NQ]
+  uint64_t* s_full = q_empty + NQ;    // [2]
+  uint64_t* s_free = s_full + 2;      // [2]
+  uint64_t* x_full = s_free + 2;      // [NX]
   uint64_t* x_free = x_full + NX;     // [NX]
   uint64_t* kv_done = x_free + NX;
   uint64_t* info_full = kv_done + 1;  // warps 2-3: step info (and bias columns) ready
   uint64_t* info_empty = info_full + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(info_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  static_assert((1 + 2 * NQ + 2 + 2 + 2 * NX + 1 + 2 + 2) * 8 + 8 <= 256,
+                "Pass B barriers, TMEM address and abort flag exceed their 256-byte area");
   // relative: bias column c of a step holds rl[row_c, pad + base_c - k0 - 127 - o_c ...]
   // (272 B from the 16-byte boundary below it); node r reads element o_c + 127 - r
   uint16_t* bias_s = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(bars) + 256);
@@ -475,9 +483,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NQ; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kComputeThreads);
       mbar_init(&info_full[i], 64);
@@ -512,8 +522,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_4d(v_s + B128, &tmv, 64, hkv, row0, b, kv_full);
       }
       for (int i = 0; ok; ++i, ok = w.advance()) {
-        const int st = i & 1;
-        if (i >= 2 && !mbar_wait(&q_empty[st], ((i >> 1) - 1) & 1, abort_flag, status)) break;
+        const int st = i % NQ;
+        if (i >= NQ && !mbar_wait(&q_empty[st], ((i / NQ) - 1) & 1, abort_flag, status)) break;
         const int hq = hkv * p.E + w.e;
         mbar_expect_tx(&q_full[st], 2 * T64);
         tma_load_4d(q_s + st * T64, &tmq, 0, hq, w.qb, b, &q_full[st]);
@@ -528,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t kIdA = idesc_f16(128, 128, Pack2<T>::kFmt, 0, 1);
       const uint32_t ka = smem_addr(k_s), va = smem_addr(v_s), pa = smem_addr(pt_s), xa = smem_addr(xt_s);
       auto issue_acc = [&](int t) {
-        const uint32_t qa = smem_addr(q_s + (t & 1) * T64), ga = smem_addr(g_s + (t & 1) * T64);
+        const uint32_t qa = smem_addr(q_s + (t % NQ) * T64), ga = smem_addr(g_s + (t % NQ) * T64);
         const uint32_t pb = pa + (t % NX) * 128 * 128, xb = xa + (t % NX) * 128 * 128;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
@@ -537,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_f16(tmem + 384, sdesc_sw128(xb + kk * 32, 16, 1024), sdesc_sw128(qa + kk * 2048, B64, 1024), kIdA, acc);
         }
         mma_commit(&x_free[t % NX]);
-        mma_commit(&q_empty[t & 1]);
+        mma_commit(&q_empty[t % NQ]);
       };
       QSteps w;
       bool ok = w.start(qlo, qhi, p.E);
@@ -548,8 +558,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = alive;
       }
       for (; ok; ++i, ok = w.advance()) {
-        const int st = i & 1, bb = i & 1;
-        if (!mbar_wait(&q_full[st], (i >> 1) & 1, abort_flag, status)) { alive = false; break; }
+        const int st = i % NQ, bb = i & 1;
+        if (!mbar_wait(&q_full[st], (i / NQ) & 1, abort_flag, status)) { alive = false; break; }
         if (i >= 2 && !mbar_wait(&s_free[bb], ((i >> 1) - 1) & 1, abort_flag, status)) { alive = false; break; }
         tc_fence_after();
         const uint32_t qa = smem_addr(q_s + st * T64), ga = smem_addr(g_s + st * T64);
@@ -604,8 +614,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         dl = p.delta[row];
       }
       const int ci = buf * 64 + t;
-      lo_s[ci] = lo;
-      hi_s[ci] = hi;
+      lo_s[ci] = (uint8_t)min(max(lo - k0, 0), 128);
+      hi_s[ci] = (uint8_t)min(max(hi - k0, 0), 128);
       nl_s[ci] = -l2;
       nd_s[ci] = -dl;
       const bool all_in = __all_sync(0xffffffffu, nk == 128 && lo <= k0 && hi >= k0 + 128);
@@ -693,8 +703,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                        make_float2(dp[cl], dp[cl + 1]), make_float2(nl[k], nl[k + 1]),
                                        make_float2(nd[k], nd[k + 1]), sc.kq, sc.kb, sc.kc, &p2);
           if (!interior) {
-            const bool v0 = node_ok && jn >= lo_s[bb * 64 + c] && jn < hi_s[bb * 64 + c];
-            const bool v1 = node_ok && jn >= lo_s[bb * 64 + c + 1] && jn < hi_s[bb * 64 + c + 1];
+            const bool v0 = node_ok && r >= lo_s[bb * 64 + c] && r < hi_s[bb * 64 + c];
+            const bool v1 = node_ok && r >= lo_s[bb * 64 + c + 1] && r < hi_s[bb * 64 + c + 1];
             p2.x = v0 ? p2.x : 0.f;
             p2.y = v1 ? p2.y : 0.f;
             v.x = v0 ? v.x : 0.f;
