@@ -552,70 +552,83 @@ __global__ void __launch_bounds__(NT) decode_kernel128(DecParams P) {
       lc[i] = ln[i];
     }
     if (g0 + 64 < M) fetch(g0 + 64);  // next group's rows in flight during this group's math
-    float x[E][4];
+    // per entry: this lane's share of the logit over its 8 dims (and its
+    // d_rel dims of the relative bias), z = dot * k_in + bias * k_bias;
+    // a reduce-scatter over the half-warp then leaves each lane with the
+    // whole logit of one entry, so the tanh / exp2 run once per entry per
+    // lane instead of four times
+    const int own = ((l16 >> 3) & 1) * 2 + ((l16 >> 2) & 1);  // entry 2 own + half of the group
+    const bool up8 = (l16 & 8) != 0, up4 = (l16 & 4) != 0;
+    const bool own_ok = (own == 0 ? jc[0] : own == 1 ? jc[1] : own == 2 ? jc[2] : jc[3]) >= 0;
+    float2 kf[4][4];
+    float pr0[4], pr1[4];  // relative: proj[r, dist] for r = l16, l16 + 16
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const bool ok = jc[i] >= 0;
       const uint32_t kw[4] = {kc[i].x, kc[i].y, kc[i].z, kc[i].w};
-      float2 kf[4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) kf[c] = unpack2<T>(kw[c]);
-      float pr0 = 0.f, pr1 = 0.f;  // relative: proj[r, dist] for r = l16, l16 + 16
-      if (rel && ok) {
+      for (int c = 0; c < 4; ++c) kf[i][c] = unpack2<T>(kw[c]);
+      pr0[i] = pr1[i] = 0.f;
+      if (rel && jc[i] >= 0) {
         const int dist = S.base_s[lc[i]] - jc[i];
-        if (l16 < a.d_rel) pr0 = load_any(a.rel_proj, (int64_t)l16 * a.rel_bins + dist, a.rel_dtype);
-        if (l16 + 16 < a.d_rel) pr1 = load_any(a.rel_proj, (int64_t)(l16 + 16) * a.rel_bins + dist, a.rel_dtype);
-      }
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        float2 d2 = fmul2(q[e][0], kf[0]);
-#pragma unroll
-        for (int c = 1; c < 4; ++c) d2 = ffma2(q[e][c], kf[c], d2);
-        float dot = d2.x + d2.y;
-#pragma unroll
-        for (int o = 8; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-        float bias = 0.f;
-        if (rel) {
-          bias = (l16 < a.d_rel ? S.st[e][l16] * pr0 : 0.f) + (l16 + 16 < a.d_rel ? S.st[e][l16 + 16] * pr1 : 0.f);
-#pragma unroll
-          for (int o = 8; o; o >>= 1) bias += __shfl_xor_sync(0xffffffffu, bias, o);
-        }
-        float y = fmaf(dot, k_in, bias * k_bias);
-        if (cap) y = tanh_approx(y) * k_out;
-        x[e][i] = ok ? y : -INFINITY;
+        if (l16 < a.d_rel) pr0[i] = load_any(a.rel_proj, (int64_t)l16 * a.rel_bins + dist, a.rel_dtype);
+        if (l16 + 16 < a.d_rel) pr1[i] = load_any(a.rel_proj, (int64_t)(l16 + 16) * a.rel_bins + dist, a.rel_dtype);
       }
     }
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      float gm = fmaxf(fmaxf(x[e][0], x[e][1]), fmaxf(x[e][2], x[e][3]));
+      float z[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 d2 = fmul2(q[e][0], kf[i][0]);
+#pragma unroll
+        for (int c = 1; c < 4; ++c) d2 = ffma2(q[e][c], kf[i][c], d2);
+        z[i] = (d2.x + d2.y) * k_in;
+        if (rel)
+          z[i] += ((l16 < a.d_rel ? S.st[e][l16] * pr0[i] : 0.f) +
+                   (l16 + 16 < a.d_rel ? S.st[e][l16 + 16] * pr1[i] : 0.f)) * k_bias;
+      }
+      // lanes 0-7 keep entries {0, 1}, 8-15 {2, 3}; then 0-3 / 8-11 the first
+      float k0 = up8 ? z[2] : z[0], k1 = up8 ? z[3] : z[1];
+      k0 += __shfl_xor_sync(0xffffffffu, up8 ? z[0] : z[2], 8);
+      k1 += __shfl_xor_sync(0xffffffffu, up8 ? z[1] : z[3], 8);
+      float y = up4 ? k1 : k0;
+      y += __shfl_xor_sync(0xffffffffu, up4 ? k0 : k1, 4);
+      y += __shfl_xor_sync(0xffffffffu, y, 2);
+      y += __shfl_xor_sync(0xffffffffu, y, 1);
+      if (cap) y = tanh_approx(y) * k_out;
+      const float x = own_ok ? y : -INFINITY;
+      // the group maximum over the warp's eight entries
+      float gm = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
+      gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 8));
       gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 16));
       const float mn = fmaxf(m[e], gm);
       if (mn == -INFINITY) continue;  // warp-uniform: no visible entry yet
       const float corr = ex2_approx(m[e] - mn);
       const float2 c2 = make_float2(corr, corr);
-      float p[4], ps = 0.f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        p[i] = ex2_approx(x[e][i] - mn);
-        ps += p[i];
-      }
-      l[e] = fmaf(l[e], corr, ps);
+      const float p_own = ex2_approx(x - mn);
+      // this lane's share of the row sum: its own entry slot (each slot is
+      // held by four lanes; the epilogue divides by four)
+      l[e] = fmaf(l[e], corr, p_own);
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc[e][c] = fmul2(acc[e][c], c2);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
+        const float pi = __shfl_sync(0xffffffffu, p_own, (lane & 16) | ((i >> 1) << 3) | ((i & 1) << 2));
         const uint32_t vw[4] = {vc[i].x, vc[i].y, vc[i].z, vc[i].w};
-        const float2 p2 = make_float2(p[i], p[i]);
+        const float2 p2 = make_float2(pi, pi);
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[e][c] = ffma2(p2, unpack2<T>(vw[c]), acc[e][c]);
       }
       m[e] = mn;
     }
   }
-  // the two halves hold different entries of the same dims: add them
+  // the two halves hold different entries of the same dims: add them; the
+  // row sum is spread over all lanes, each entry slot four times
 #pragma unroll
   for (int e = 0; e < E; ++e) {
-    l[e] += __shfl_xor_sync(0xffffffffu, l[e], 16);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) l[e] += __shfl_xor_sync(0xffffffffu, l[e], o);
+    l[e] *= 0.25f;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       acc[e][c].x += __shfl_xor_sync(0xffffffffu, acc[e][c].x, 16);
