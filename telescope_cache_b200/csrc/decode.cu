@@ -475,7 +475,7 @@ __device__ __forceinline__ float2 round2(float2 v) {
 // (exp2 / tanh instructions); the partial maxima go to the epilogue in
 // natural units.
 template <typename T, int E>
-__global__ void __launch_bounds__(NT) decode_kernel128(DecParams P) {
+__global__ void __launch_bounds__(NT, E == 1 ? 2 : 1) decode_kernel128(DecParams P) {
   __shared__ DecShared<128> S;
   __shared__ int r0_s[TC_MAX_LEVELS];  // lo % cap: ring position of each level's first visible node
   if (!decode_prologue<T, 128>(P, S)) return;
@@ -513,114 +513,115 @@ __global__ void __launch_bounds__(NT) decode_kernel128(DecParams P) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[e][i] = make_float2(0.f, 0.f);
   }
-  // this CTA's entries [e_lo, e_hi) of the visible set (all of it unsplit)
+  // this CTA's entries [e_lo, M) of the visible set (all of it unsplit)
   const int M_all = S.pre_s[nl];
   const int e_lo = (int)((int64_t)M_all * blockIdx.z / gridDim.z);
   const int M = (int)((int64_t)M_all * (blockIdx.z + 1) / gridDim.z);
-  int lev = 0;  // entries of a lane only move forward through the levels
-  uint4 kn[4], vn[4];
-  int jn[4], ln[4];
-  auto fetch = [&](int g0) {
+  // this (batch, KV head)'s ring rows: slot s at 16-byte offset s * Hkv * 16
+  const uint4* kbase = rk + row0 * 16 + l16;
+  const uint4* vbase = rv + row0 * 16 + l16;
+  const int sstride = a.Hkv * 16;
+  int lev_f = 0, lev_c = 0;  // a lane's entries only move forward through the levels
+  // a group's row slices (entries g0 + 8 warp + 2 i + half); entries past the
+  // end re-read the last one (masked in the math), so no lane branches
+  struct Grp {
+    uint4 k[4], v[4];
+  };
+  auto fetch = [&](Grp& G, int g0) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int idx = g0 + warp * 8 + 2 * i + half;
-      jn[i] = -1;
-      ln[i] = 0;
-      kn[i] = vn[i] = make_uint4(0u, 0u, 0u, 0u);
-      if (idx < M) {
-        while (idx >= S.pre_s[lev + 1]) ++lev;
-        // slot = off + j % cap with j = lo + d and d < cap: one conditional subtract
-        const int d = idx - S.pre_s[lev], cp = S.caps_s[lev];
-        const int rr = r0_s[lev] + d;
-        const int64_t row = row0 + (int64_t)(S.roff_s[lev] + (rr >= cp ? rr - cp : rr)) * a.Hkv;
-        kn[i] = __ldg(rk + row * 16 + l16);
-        vn[i] = __ldg(rv + row * 16 + l16);
-        jn[i] = S.lo_s[lev] + d;
-        ln[i] = lev;
-      }
+      const int idx = min(g0 + warp * 8 + 2 * i + half, M - 1);
+      while (idx >= S.pre_s[lev_f + 1]) ++lev_f;
+      // slot = off + j % cap with j = lo + d and d < cap: one conditional subtract
+      const int d = idx - S.pre_s[lev_f], cp = S.caps_s[lev_f];
+      const int rr = r0_s[lev_f] + d;
+      const int off = (S.roff_s[lev_f] + (rr >= cp ? rr - cp : rr)) * sstride;
+      G.k[i] = __ldg(kbase + off);
+      G.v[i] = __ldg(vbase + off);
     }
   };
-  if (e_lo < M) fetch(e_lo);
-  for (int g0 = e_lo; g0 < M; g0 += 64) {
-    uint4 kc[4], vc[4];
-    int jc[4], lc[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      kc[i] = kn[i];
-      vc[i] = vn[i];
-      jc[i] = jn[i];
-      lc[i] = ln[i];
-    }
-    if (g0 + 64 < M) fetch(g0 + 64);  // next group's rows in flight during this group's math
-    // per entry: this lane's share of the logit over its 8 dims (and its
-    // d_rel dims of the relative bias), z = dot * k_in + bias * k_bias;
-    // a reduce-scatter over the half-warp then leaves each lane with the
-    // whole logit of one entry, so the tanh / exp2 run once per entry per
-    // lane instead of four times
-    const int own = ((l16 >> 3) & 1) * 2 + ((l16 >> 2) & 1);  // entry 2 own + half of the group
-    const bool up8 = (l16 & 8) != 0, up4 = (l16 & 4) != 0;
-    const bool own_ok = (own == 0 ? jc[0] : own == 1 ? jc[1] : own == 2 ? jc[2] : jc[3]) >= 0;
-    float2 kf[4][4];
-    float pr0[4], pr1[4];  // relative: proj[r, dist] for r = l16, l16 + 16
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t kw[4] = {kc[i].x, kc[i].y, kc[i].z, kc[i].w};
-#pragma unroll
-      for (int c = 0; c < 4; ++c) kf[i][c] = unpack2<T>(kw[c]);
-      pr0[i] = pr1[i] = 0.f;
-      if (rel && jc[i] >= 0) {
-        const int dist = S.base_s[lc[i]] - jc[i];
-        if (l16 < a.d_rel) pr0[i] = load_any(a.rel_proj, (int64_t)l16 * a.rel_bins + dist, a.rel_dtype);
-        if (l16 + 16 < a.d_rel) pr1[i] = load_any(a.rel_proj, (int64_t)(l16 + 16) * a.rel_bins + dist, a.rel_dtype);
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      float z[4];
+  auto consume = [&](const Grp& G, int g0) {
+      // per entry: this lane's share of the logit over its 8 dims (and its
+      // d_rel dims of the relative bias), z = dot * k_in + bias * k_bias;
+      // a reduce-scatter over the half-warp then leaves each lane with the
+      // whole logit of one entry, so the tanh / exp2 run once per entry per
+      // lane instead of four times
+      const int own = ((l16 >> 3) & 1) * 2 + ((l16 >> 2) & 1);  // entry 2 own + half of the group
+      const bool up8 = (l16 & 8) != 0, up4 = (l16 & 4) != 0;
+      const bool own_ok = g0 + warp * 8 + 2 * own + half < M;
+      float2 kf[4][4];
+      float pr0[4], pr1[4];  // relative: proj[r, dist] for r = l16, l16 + 16
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        float2 d2 = fmul2(q[e][0], kf[i][0]);
+        const uint32_t kw[4] = {G.k[i].x, G.k[i].y, G.k[i].z, G.k[i].w};
 #pragma unroll
-        for (int c = 1; c < 4; ++c) d2 = ffma2(q[e][c], kf[i][c], d2);
-        z[i] = (d2.x + d2.y) * k_in;
-        if (rel)
-          z[i] += ((l16 < a.d_rel ? S.st[e][l16] * pr0[i] : 0.f) +
-                   (l16 + 16 < a.d_rel ? S.st[e][l16 + 16] * pr1[i] : 0.f)) * k_bias;
+        for (int c = 0; c < 4; ++c) kf[i][c] = unpack2<T>(kw[c]);
+        pr0[i] = pr1[i] = 0.f;
+        const int idx = g0 + warp * 8 + 2 * i + half;
+        if (rel && idx < M) {
+          while (idx >= S.pre_s[lev_c + 1]) ++lev_c;
+          const int dist = S.base_s[lev_c] - (S.lo_s[lev_c] + idx - S.pre_s[lev_c]);
+          if (l16 < a.d_rel) pr0[i] = load_any(a.rel_proj, (int64_t)l16 * a.rel_bins + dist, a.rel_dtype);
+          if (l16 + 16 < a.d_rel) pr1[i] = load_any(a.rel_proj, (int64_t)(l16 + 16) * a.rel_bins + dist, a.rel_dtype);
+        }
       }
-      // lanes 0-7 keep entries {0, 1}, 8-15 {2, 3}; then 0-3 / 8-11 the first
-      float k0 = up8 ? z[2] : z[0], k1 = up8 ? z[3] : z[1];
-      k0 += __shfl_xor_sync(0xffffffffu, up8 ? z[0] : z[2], 8);
-      k1 += __shfl_xor_sync(0xffffffffu, up8 ? z[1] : z[3], 8);
-      float y = up4 ? k1 : k0;
-      y += __shfl_xor_sync(0xffffffffu, up4 ? k0 : k1, 4);
-      y += __shfl_xor_sync(0xffffffffu, y, 2);
-      y += __shfl_xor_sync(0xffffffffu, y, 1);
-      if (cap) y = tanh_approx(y) * k_out;
-      const float x = own_ok ? y : -INFINITY;
-      // the group maximum over the warp's eight entries
-      float gm = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
-      gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 8));
-      gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 16));
-      const float mn = fmaxf(m[e], gm);
-      if (mn == -INFINITY) continue;  // warp-uniform: no visible entry yet
-      const float corr = ex2_approx(m[e] - mn);
-      const float2 c2 = make_float2(corr, corr);
-      const float p_own = ex2_approx(x - mn);
-      // this lane's share of the row sum: its own entry slot (each slot is
-      // held by four lanes; the epilogue divides by four)
-      l[e] = fmaf(l[e], corr, p_own);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) acc[e][c] = fmul2(acc[e][c], c2);
+      for (int e = 0; e < E; ++e) {
+        float z[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float pi = __shfl_sync(0xffffffffu, p_own, (lane & 16) | ((i >> 1) << 3) | ((i & 1) << 2));
-        const uint32_t vw[4] = {vc[i].x, vc[i].y, vc[i].z, vc[i].w};
-        const float2 p2 = make_float2(pi, pi);
+        for (int i = 0; i < 4; ++i) {
+          float2 d2 = fmul2(q[e][0], kf[i][0]);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) acc[e][c] = ffma2(p2, unpack2<T>(vw[c]), acc[e][c]);
+          for (int c = 1; c < 4; ++c) d2 = ffma2(q[e][c], kf[i][c], d2);
+          z[i] = (d2.x + d2.y) * k_in;
+          if (rel)
+            z[i] += ((l16 < a.d_rel ? S.st[e][l16] * pr0[i] : 0.f) +
+                     (l16 + 16 < a.d_rel ? S.st[e][l16 + 16] * pr1[i] : 0.f)) * k_bias;
+        }
+        // lanes 0-7 keep entries {0, 1}, 8-15 {2, 3}; then 0-3 / 8-11 the first
+        float k0 = up8 ? z[2] : z[0], k1 = up8 ? z[3] : z[1];
+        k0 += __shfl_xor_sync(0xffffffffu, up8 ? z[0] : z[2], 8);
+        k1 += __shfl_xor_sync(0xffffffffu, up8 ? z[1] : z[3], 8);
+        float y = up4 ? k1 : k0;
+        y += __shfl_xor_sync(0xffffffffu, up4 ? k0 : k1, 4);
+        y += __shfl_xor_sync(0xffffffffu, y, 2);
+        y += __shfl_xor_sync(0xffffffffu, y, 1);
+        if (cap) y = tanh_approx(y) * k_out;
+        const float x = own_ok ? y : -INFINITY;
+        // the group maximum over the warp's eight entries
+        float gm = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
+        gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 8));
+        gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 16));
+        const float mn = fmaxf(m[e], gm);
+        if (mn == -INFINITY) continue;  // warp-uniform: no visible entry yet
+        const float corr = ex2_approx(m[e] - mn);
+        const float2 c2 = make_float2(corr, corr);
+        const float p_own = ex2_approx(x - mn);
+        // this lane's share of the row sum: its own entry slot (each slot is
+        // held by four lanes; the epilogue divides by four)
+        l[e] = fmaf(l[e], corr, p_own);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[e][c] = fmul2(acc[e][c], c2);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float pi = __shfl_sync(0xffffffffu, p_own, (lane & 16) | ((i >> 1) << 3) | ((i & 1) << 2));
+          const uint32_t vw[4] = {G.v[i].x, G.v[i].y, G.v[i].z, G.v[i].w};
+          const float2 p2 = make_float2(pi, pi);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[e][c] = ffma2(p2, unpack2<T>(vw[c]), acc[e][c]);
+        }
+        m[e] = mn;
       }
-      m[e] = mn;
-    }
+  };
+  // two register groups in turn: one in flight while the other is used
+  Grp ga, gb;
+  if (e_lo < M) fetch(ga, e_lo);
+  for (int g0 = e_lo; g0 < M; g0 += 128) {
+    if (g0 + 64 < M) fetch(gb, g0 + 64);
+    consume(ga, g0);
+    if (g0 + 64 >= M) break;
+    if (g0 + 128 < M) fetch(ga, g0 + 128);
+    consume(gb, g0 + 64);
   }
   // the two halves hold different entries of the same dims: add them; the
   // row sum is spread over all lanes, each entry slot four times
