@@ -596,48 +596,51 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = w.start(qlo, qhi, p.E);
     for (int i = 0; ok; ++i, ok = w.advance()) {
       const int buf = i & 1;
-      if (i >= 2 && !__all_sync(0xffffffffu, mbar_wait(&info_empty[buf], ((i >> 1) - 1) & 1, abort_flag, status)))
-        break;
       const int hq = hkv * p.E + w.e;
       const int q = w.qb + t;
+      const bool q_ok = q < p.N;
       const int64_t row = ((int64_t)b * p.N + q) * p.Hq + hq;
-      int lo = 0, hi = 0, base = 0;
+      // the step's lse / Delta loads and bounds are independent of the buffer:
+      // in flight during the wait for it
       float l2 = 0.f, dl = 0.f;
-      if (q < p.N) {
+      int lo = 0, hi = 0, base = 0;
+      if (q_ok) {
+        l2 = p.lse[row];
+        dl = p.delta[row];
         if (REL) {
           level_info(q, lev, p.s, &lo, &hi, &base);
         } else {
           level_bounds_raw(q, lev, p.s, &lo, &hi);
           if (lo >= hi) lo = hi = 0;
         }
-        l2 = p.lse[row] * kLog2e;
-        dl = p.delta[row];
       }
+      if (i >= 2 && !__all_sync(0xffffffffu, mbar_wait(&info_empty[buf], ((i >> 1) - 1) & 1, abort_flag, status)))
+        break;
       const int ci = buf * 64 + t;
-      lo_s[ci] = (uint8_t)min(max(lo - k0, 0), 128);
-      hi_s[ci] = (uint8_t)min(max(hi - k0, 0), 128);
-      nl_s[ci] = -l2;
-      nd_s[ci] = -dl;
-      const bool all_in = __all_sync(0xffffffffu, nk == 128 && lo <= k0 && hi >= k0 + 128);
-      if (lane == 0) in_s[buf * 2 + (t >> 5)] = all_in;
       if constexpr (REL) {
         // nodes k0 + r see distance base - k0 - r: one descending run of 128
         // elements ending at rl[row, pad + base - k0]; some node of the tile
         // is visible, so base >= k0 and the 16-byte superset stays inside the
-        // row's padding (pad >= 136)
+        // row's padding (pad >= 136).  The copy goes out first (its bytes
+        // declared without arriving); the thread arrives once the step info
+        // below is written.
         if (lo < hi && lo < k0 + nk && hi > k0) {
           const int64_t e0 = row * p.rl_stride + p.rl_pad + base - k0 - 127;
           const int64_t a = e0 & ~int64_t(7);
           bo_s[ci] = (uint8_t)(e0 - a);
-          mbar_expect_tx(&info_full[buf], kColStride * 2);
+          mbar_expect_tx_only(&info_full[buf], kColStride * 2);
           bulk_load(bias_s + ci * kColStride, p.rl + a, kColStride * 2, &info_full[buf]);
         } else {
           bo_s[ci] = 0;
-          mbar_arrive(&info_full[buf]);
         }
-      } else {
-        mbar_arrive(&info_full[buf]);
       }
+      lo_s[ci] = (uint8_t)min(max(lo - k0, 0), 128);
+      hi_s[ci] = (uint8_t)min(max(hi - k0, 0), 128);
+      nl_s[ci] = -l2 * kLog2e;
+      nd_s[ci] = -dl;
+      const bool all_in = __all_sync(0xffffffffu, nk == 128 && lo <= k0 && hi >= k0 + 128);
+      if (lane == 0) in_s[buf * 2 + (t >> 5)] = all_in;
+      mbar_arrive(&info_full[buf]);
     }
   } else {
     const int r = (threadIdx.x - 128) & 127;  // node row = TMEM lane
