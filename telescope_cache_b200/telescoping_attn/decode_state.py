@@ -16,7 +16,8 @@ from typing import Dict, List, Optional, Tuple
 import torch
 
 from .. import _lib
-from ..range_spec import RangeSpec, activation_times_from_fmap, range_bounds
+from ..range_spec import (RangeSpec, activation_times_from_fmap, level_row_bounds, normalize_empty,
+                          range_bounds)
 from .position import compute_relative_states, positional_args, check_relative_bins
 from .summaries import _check_conv_weight, compute_linear_weights, short_conv
 
@@ -190,7 +191,9 @@ def init_decode_state(
 def _check_tick(state: DecodeState, t: int):
     """The schedule invariants the reference asserts at every step
     (reference.py:2036-2082): at most one level fires, its children are live
-    at t-1, and no level exceeds its ring capacity at t."""
+    at t-1, and no level exceeds its ring capacity at t.  Every level's range
+    of a row comes from one pass of the closed forms (level_row_bounds), so a
+    step costs two such passes, not one per level."""
     a = state.activation_times
     fired = None
     for level in range(1, len(a)):
@@ -200,18 +203,32 @@ def _check_tick(state: DecodeState, t: int):
                     f"levels {fired} and {level} both activate at t={t}; the schedule is not "
                     f"dyadically aligned")
             fired = level
-            j = (t - a[level]) >> level
-            lo_c, hi_c = range_bounds(state.spec(t), t - 1, level - 1)
-            if not (lo_c <= 2 * j and 2 * j + 1 < hi_c):
-                raise AssertionError(
-                    f"children of node ({level}, {j}) not live at t-1={t - 1}: level-{level - 1} "
-                    f"range [{lo_c},{hi_c})")
-    spec_next = state.spec(t + 1)
-    for level in range(len(a)):
-        lo, hi = range_bounds(spec_next, t, level)
+    if fired is not None:
+        j = (t - a[fired]) >> fired
+        lo_c, hi_c = _checked_bounds(state, t - 1, t)[fired - 1]
+        if not (lo_c <= 2 * j and 2 * j + 1 < hi_c):
+            raise AssertionError(
+                f"children of node ({fired}, {j}) not live at t-1={t - 1}: level-{fired - 1} "
+                f"range [{lo_c},{hi_c})")
+    for level, (lo, hi) in enumerate(_checked_bounds(state, t, t + 1)):
         if hi - lo > state.caps[level]:
             raise AssertionError(
                 f"level {level} needs {hi - lo} live slots > cap {state.caps[level]} at t={t}")
+
+
+def _checked_bounds(state: DecodeState, q: int, seq_len: int):
+    """range_bounds(spec(seq_len), q, level) for every level at once: the
+    normalised ranges of query q with the reference's level-length check."""
+    if not 0 <= q < seq_len:
+        raise ValueError(f"q={q} out of range [0, {seq_len})")
+    out = []
+    for level, (lo, hi) in enumerate(level_row_bounds(q, state.activation_times, state.cache_size)):
+        lo, hi = normalize_empty((lo, hi))
+        if hi > seq_len >> level:
+            raise AssertionError(
+                f"range [{lo},{hi}) exceeds level_len={seq_len >> level} at q={q}, level={level}")
+        out.append((lo, hi))
+    return out
 
 
 DECODE_MAX_SPLITS = 8
