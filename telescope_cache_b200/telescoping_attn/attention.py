@@ -14,6 +14,7 @@ the kernel from relative_states and relative_proj and is never materialised.
 
 import ctypes
 import math
+import weakref
 from typing import Dict, Optional
 
 import torch
@@ -70,13 +71,43 @@ def _relative_band(st, pj, max_visible, dtype):
     return band.contiguous(), width
 
 
+# The relative band of a forward, kept for the backward of the same call:
+# id(lse) -> (weak lse, weak states, weak proj, their versions and shapes,
+# band, width).  An entry lives as long as the forward's lse output; it is
+# reused only for the same states / proj objects, unmodified (version
+# counters), so a backward with other or changed tensors recomputes the band.
+_BANDS: Dict[int, tuple] = {}
+
+
+def _band_key(states, proj, reach, dtype):
+    return (states._version, tuple(states.shape), states.dtype, proj._version, tuple(proj.shape), proj.dtype,
+            reach, dtype)
+
+
+def _cached_band(lse, states, proj, reach, dtype):
+    e = _BANDS.get(id(lse)) if lse is not None else None
+    if e is None or e[0]() is not lse or e[1]() is not states or e[2]() is not proj:
+        return None
+    if e[3] != _band_key(states, proj, reach, dtype):
+        return None
+    return e[4], e[5]
+
+
+def _keep_band(lse, states, proj, reach, dtype, band, width):
+    k = id(lse)
+    _BANDS[k] = (weakref.ref(lse, lambda _r, k=k: _BANDS.pop(k, None)), weakref.ref(states), weakref.ref(proj),
+                 _band_key(states, proj, reach, dtype), band, width)
+
+
 def _tensor_core_shape(dtype, Dk, Dv):
     return dtype in (torch.bfloat16, torch.float16) and Dk == 128 and Dv == 128
 
 
 def _prepare(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope_sin,
-             relative_states, relative_proj, impl=None):
-    """Shared validation + operand preparation of forward and backward."""
+             relative_states, relative_proj, impl=None, band_of=None):
+    """Shared validation + operand preparation of forward and backward.
+    band_of: the forward's lse in a backward, whose relative band is reused
+    when it was kept for the same, unmodified states and proj."""
     B, N, Hq, Dk = q.shape
     Hkv = packed.k.shape[2]
     Dv = packed.v.shape[-1]
@@ -125,11 +156,14 @@ def _prepare(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope
         dev_status=device_status(q.device).data_ptr())
     band = None
     if position_mode == "relative" and impl != "simt" and _tensor_core_shape(dtype, Dk, Dv):
-        band, width = _relative_band(st, pj, mx, dtype)
+        hit = _cached_band(band_of, relative_states, relative_proj, mx, dtype)
+        band, width = hit if hit is not None else _relative_band(st, pj, mx, dtype)
         args.rel_logits = band.data_ptr()
         args.rel_logits_stride = width
         args.rel_logits_pad = REL_PAD
     keep = (qc, kc, vc, cos, sin, st, pj, band)
+    if band is not None:
+        args._band = (mx, band, width)  # for _keep_band after the forward
     return args, sched, spec, keep, (B, N, Hq, Hkv, Dk, Dv, dtype)
 
 
@@ -146,6 +180,9 @@ def _forward(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope
     args.impl = _impl_code(impl)
     _lib.check(_lib.lib().tc_attn_fwd(ctypes.byref(args), ctypes.byref(sched), _lib.stream_of(q)),
                "tc_attn_fwd")
+    band = getattr(args, "_band", None)
+    if band is not None:
+        _keep_band(lse, relative_states, relative_proj, band[0], dims[-1], band[1], band[2])
     del keep
     return out, lse
 
@@ -269,7 +306,7 @@ def multilevel_attention_backward(
             raise ValueError("dlse must have floating dtype")
     args, sched, spec, keep, dims = _prepare(q, packed, fmap, cache_size, softcap, position_mode,
                                              rope_cos, rope_sin, relative_states, relative_proj,
-                                             impl)
+                                             impl, band_of=lse)
     dtype = dims[-1]
     _lib.require_cuda(out, lse, dout, dlse)
     oc = out.to(dtype).contiguous()
