@@ -3,11 +3,13 @@
 // on tcgen05 with fp32 accumulators in TMEM and operands staged by TMA.
 //
 // Pass A (Q-owned dQ): CTA = 128 query rows of one query head walking every
-//   level's hull in 64-node tiles.  Per tile: S = Q K^T and dP = dO V^T into
-//   double-buffered TMEM; one thread per query row rebuilds P from the saved
-//   lse with the exact level mask, forms dX = P (dP - Delta) softcap' into
-//   shared memory, and the MMA warp accumulates dQ += dX K in TMEM.  The
-//   epilogue scales, rotates back (RoPE) and stores dQ.
+//   level's hull in 64-node tiles.  Q and dO stay in TMEM for the whole walk
+//   (the A operands of S and dP: no shared-memory operand traffic for them).
+//   Per tile: S = Q K^T and dP = dO V^T into double-buffered TMEM; four
+//   threads per query row rebuild P from the saved lse with the exact level
+//   mask, form dX = P (dP - Delta) softcap' into shared memory, and the MMA
+//   warp accumulates dQ += dX K in TMEM.  The epilogue scales, rotates back
+//   (RoPE) and stores dQ.
 // Pass B (KV-owned dK/dV): CTA = 128 nodes of one level of one KV head walking
 //   the nodes' query hull (bwd_hull) in 64-query steps, every query head of
 //   the GQA group.  Per step: S^T = K Q^T, dP^T = V dO^T; one thread per node
@@ -28,17 +30,17 @@ constexpr int T128 = 128 * 128 * 2;  // [128 rows x 128] 16-bit tile, two 64-col
 constexpr int T64 = 64 * 128 * 2;    // [64 rows x 128] tile
 constexpr int B128 = 128 * 128;      // one 64-col block of a 128-row tile
 constexpr int B64 = 64 * 128;        // one 64-col block of a 64-row tile
-// dX tiles the accumulate MMAs read: double buffered (NX = 2) unless the
-// relative variant's staging leaves no room
+// Pass B dX^T / P^T tiles the accumulate MMAs read: double buffered (NX = 2)
+// unless the relative variant's staging leaves no room
 constexpr int nx_of(bool rel) { return rel ? 1 : 2; }
-// Pass A K/V stages: three, so a tile's TMA load starts two tiles before its
-// MMAs, unless the relative variant's staging leaves no room
-constexpr int nkv_of(bool rel) { return rel ? 2 : 3; }
-constexpr int kSmemA = 2 * T128 + 2 * nkv_of(false) * T64 + nx_of(false) * 128 * 128 + 1024 + 256;
+// Pass A (Q and dO in TMEM): three K/V stages, so a tile's TMA load starts two
+// tiles before its MMAs, and two dX tiles
+constexpr int kNkvA = 3, kNxA = 2;
+constexpr int kSmemA = 2 * kNkvA * T64 + kNxA * 128 * 128 + 1024 + 256;
 // relative Pass A: + an fp32 dX staging tile [128 x 66], per-row run info,
 // row totals and the double-buffered bias runs [2][128][kRunStride]
 constexpr int kDxfStride = 66;  // even: 8-byte column pairs; 16 rows per phase hit distinct banks
-constexpr int kSmemArel = 2 * T128 + 2 * nkv_of(true) * T64 + nx_of(true) * 128 * 128 + 1024 + 256 + 128 * kDxfStride * 4 + 128 * 4 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2 + 256;
+constexpr int kSmemArel = 2 * kNkvA * T64 + kNxA * 128 * 128 + 1024 + 256 + 128 * kDxfStride * 4 + 128 * 4 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2 + 256;
 // Pass B: tiles (NQ Q/dO stages: three, so a step's TMA load starts two
 // steps before its MMAs, unless the relative variant's staging leaves no
 // room) + per-step query info [2][64] x {-lse2, -Delta} (fp32) and {lo, hi}
@@ -78,6 +80,8 @@ struct BwdParams {
   int64_t rl_stride;
   int rl_pad;
   int32_t* status;
+  const void* q;                 // Pass A: q (rotated for RoPE) and dO, [B, N, Hq, 128]
+  const void* dout;
   Sched s;
   int tiles[TC_MAX_LEVELS + 1];  // Pass B: prefix count of 128-node tiles per level
 };
@@ -116,20 +120,21 @@ __device__ __forceinline__ float2 dx_pair(float2 s, float2 bias, float2 dp, floa
 // ---------------------------------------------------------------------------
 // Pass A
 // ---------------------------------------------------------------------------
+// TMEM columns of Pass A: S [0, 128) and dP [128, 256) (double buffered),
+// dQ [256, 384), Q [384, 448) and dO [448, 512) (two 16-bit elements per column)
+constexpr uint32_t kColQ = 384, kColG = 448;
+
 template <typename T, bool REL, bool CAP>
 __global__ void __launch_bounds__(kThreads, 1)
-    bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmg,
-                     const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, BwdParams p) {
+    bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* q_s = sm;
-  uint8_t* g_s = q_s + T128;
-  constexpr int NX = nx_of(REL), NKV = nkv_of(REL);
-  uint8_t* k_s = g_s + T128;       // [NKV] x T64
+  constexpr int NX = kNxA, NKV = kNkvA;
+  uint8_t* k_s = sm;               // [NKV] x T64
   uint8_t* v_s = k_s + NKV * T64;  // [NKV] x T64
   uint8_t* x_s = v_s + NKV * T64;  // [NX] dX [128 x 64]
   uint64_t* bars = reinterpret_cast<uint64_t*>(x_s + NX * 128 * 128);
-  uint64_t* qg_full = bars;
+  uint64_t* qg_full = bars;  // Q and dO written to TMEM by the compute warps
   uint64_t* kv_full = bars + 1;         // [NKV]
   uint64_t* kv_empty = kv_full + NKV;   // [NKV]
   uint64_t* s_full = kv_empty + NKV;    // [2]
@@ -157,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   int32_t* status = p.status;
 
   if (threadIdx.x == 0) {
-    mbar_init(qg_full, 1);
+    mbar_init(qg_full, kComputeThreads);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kComputeThreads);
@@ -187,11 +192,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(qg_full, 2 * T128);
-      tma_load_4d(q_s, &tmq, 0, hq, q0, b, qg_full);
-      tma_load_4d(q_s + B128, &tmq, 64, hq, q0, b, qg_full);
-      tma_load_4d(g_s, &tmg, 0, hq, q0, b, qg_full);
-      tma_load_4d(g_s + B128, &tmg, 64, hq, q0, b, qg_full);
       TileWalk it{-1, 0, 0, q0, q1, 64};
       bool ok = it.start(p.s);
       for (int j = 0; ok; ++j, ok = it.advance(p.s)) {
@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t kIdS = idesc_f16(128, 64, Pack2<T>::kFmt, 0, 0);
       constexpr uint32_t kIdQ = idesc_f16(128, 128, Pack2<T>::kFmt, 0, 1);
-      const uint32_t qa = smem_addr(q_s), ga = smem_addr(g_s), xa = smem_addr(x_s);
+      const uint32_t xa = smem_addr(x_s);
       auto issue_dq = [&](int t) {
         const uint32_t ka = smem_addr(k_s + (t % NKV) * T64), xb = xa + (t % NX) * 128 * 128;
 #pragma unroll
@@ -230,17 +230,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j >= 2 && !mbar_wait(&s_free[bb], ((j >> 1) - 1) & 1, abort_flag, status)) { alive = false; break; }
         tc_fence_after();
         const uint32_t ka = smem_addr(k_s + st * T64), va = smem_addr(v_s + st * T64);
+        // A = Q / dO from TMEM (8 columns = 16 head dims per K step)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t ao = (kk >> 2) * B128 + (kk & 3) * 32, bo = (kk >> 2) * B64 + (kk & 3) * 32;
-          mma_f16(tmem + bb * 64, sdesc_sw128(qa + ao, 16, 1024), sdesc_sw128(ka + bo, 16, 1024), kIdS,
-                  kk > 0 ? 1u : 0u);
+          const uint32_t bo = (kk >> 2) * B64 + (kk & 3) * 32;
+          mma_f16_ta(tmem + bb * 64, tmem + kColQ + 8 * kk, sdesc_sw128(ka + bo, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t ao = (kk >> 2) * B128 + (kk & 3) * 32, bo = (kk >> 2) * B64 + (kk & 3) * 32;
-          mma_f16(tmem + 128 + bb * 64, sdesc_sw128(ga + ao, 16, 1024), sdesc_sw128(va + bo, 16, 1024), kIdS,
-                  kk > 0 ? 1u : 0u);
+          const uint32_t bo = (kk >> 2) * B64 + (kk & 3) * 32;
+          mma_f16_ta(tmem + 128 + bb * 64, tmem + kColG + 8 * kk, sdesc_sw128(va + bo, 16, 1024), kIdS,
+                     kk > 0 ? 1u : 0u);
         }
         mma_commit(&s_full[bb]);
         if (j >= 1) {
@@ -271,6 +271,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t row = ((int64_t)b * p.N + q) * p.Hq + hq;
     const float lse2 = row_ok ? p.lse[row] * kLog2e : 0.f;
     const float dlt = row_ok ? p.delta[row] : 0.f;
+    // this row's Q and dO, head dims [32 ch, 32 ch + 32), into TMEM (the A
+    // operands of S and dP for the whole walk); rows past N are zero
+    {
+      uint32_t wq[16], wg[16];
+      const uint4* qsrc = reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + row * HD + 32 * ch);
+      const uint4* gsrc = reinterpret_cast<const uint4*>(static_cast<const T*>(p.dout) + row * HD + 32 * ch);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 a = row_ok ? __ldg(qsrc + i) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 g = row_ok ? __ldg(gsrc + i) : make_uint4(0u, 0u, 0u, 0u);
+        wq[4 * i] = a.x, wq[4 * i + 1] = a.y, wq[4 * i + 2] = a.z, wq[4 * i + 3] = a.w;
+        wg[4 * i] = g.x, wg[4 * i + 1] = g.y, wg[4 * i + 2] = g.z, wg[4 * i + 3] = g.w;
+      }
+      tmem_st16u(tmem + lane_base + kColQ + 16 * ch, wq);
+      tmem_st16u(tmem + lane_base + kColG + 16 * ch, wg);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(qg_full);
+    }
     const bool want_drel = REL && p.drel != nullptr;
     if (want_drel && ch == 0) mtot[r] = row_ok ? visible_count(q, p.s) : 0;
     // drel write-out rows of this warp: kRowsPerWarp rows of its lane quadrant;
@@ -748,9 +767,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <typename T, bool REL, bool CAP>
 int launch_bwd(const AttnParams& a, int dtype, cudaStream_t st) {
-  CUtensorMap mq128, mg128, mk64, mv64, mq64, mg64, mk128, mv128;
-  if (int rc = make_map(&mq128, a.q, dtype, a.B, a.N, a.Hq, 128)) return rc;
-  if (int rc = make_map(&mg128, a.dout, dtype, a.B, a.N, a.Hq, 128)) return rc;
+  CUtensorMap mk64, mv64, mq64, mg64, mk128, mv128;
   if (int rc = make_map(&mk64, a.k, dtype, a.B, a.total, a.Hkv, 64)) return rc;
   if (int rc = make_map(&mv64, a.v, dtype, a.B, a.total, a.Hkv, 64)) return rc;
   if (int rc = make_map(&mq64, a.q, dtype, a.B, a.N, a.Hq, 64)) return rc;
@@ -779,6 +796,8 @@ int launch_bwd(const AttnParams& a, int dtype, cudaStream_t st) {
   p.rl_stride = a.rl_stride;
   p.rl_pad = a.rl_pad;
   p.status = a.status;
+  p.q = a.q;
+  p.dout = a.dout;
   p.s = a.s;
   p.tiles[0] = 0;
   for (int l = 0; l < TC_MAX_LEVELS; ++l)
@@ -787,7 +806,7 @@ int launch_bwd(const AttnParams& a, int dtype, cudaStream_t st) {
   auto ka = bwd_dq_tc_kernel<T, REL, CAP>;
   constexpr int smem_a = REL ? kSmemArel : kSmemA;
   if (cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_a) != cudaSuccess) return TC_ERR_CUDA;
-  ka<<<dim3((a.N + 127) / 128, a.Hq, a.B), kThreads, smem_a, st>>>(mq128, mg128, mk64, mv64, p);
+  ka<<<dim3((a.N + 127) / 128, a.Hq, a.B), kThreads, smem_a, st>>>(mk64, mv64, p);
   if (int rc = launch_status()) return rc;
   const int ntiles = p.tiles[a.s.nl];
   if (ntiles > 0) {
