@@ -65,7 +65,7 @@ DECODE = dict(B=64, T=32768, H=16, D=128, levels=8, W=256, conv=4, softcap=20.0,
 # the ncu capture of the c3_small case (profiles/attn_kernels_c3_small_full.txt)
 # scaled by the 16x (batch, head) units of config 3; traffic is proportional to
 # the units.  None where no capture covers the workload.
-TRAFFIC = {"c3": 16 * (0.412925e9 + 1.044257e9 + 0.407912e9 + 0.064190e9)}
+TRAFFIC = {"c3": 16 * (0.411784e9 + 1.043806e9 + 0.407769e9 + 0.063763e9)}
 
 
 def schedule(wl):
