@@ -146,6 +146,46 @@ typedef struct tc_tree_args {
  * build_dyadic_summaries and pack_levels (reference.py:117-211, :465-640). */
 int tc_build_tree(const tc_tree_args* a, void* stream);
 
+/* Phase-1 VJP (the backward of build_dyadic_summaries, reference.py:465-584,
+ * which the reference takes through torch autograd).  On entry gk / gv / gw
+ * hold the upstream gradients of the packed levels in fp32 (zeros where
+ * none); from the coarsest level down every parent's gradient is propagated
+ * to its two children (alpha = softmax(w0, w1), parent = sum alpha child,
+ * w_parent = logsumexp), so on return level 0 of gk / gv / gw holds the
+ * gradients of the post-conv keys, values and level-0 merge weights.  In qk
+ * weight mode (q non-NULL, detach 0) dw0 then goes through w =
+ * logsumexp_e(q_e . k / sqrt(Dk)): dq is written and the k part added to
+ * level 0 of gk; with q NULL (linear weights) or detach 1, dq is not touched
+ * and dw0 is left for the caller (x @ w_proj^T's two GEMMs). */
+typedef struct tc_tree_bwd_args {
+  int32_t B, N, Hq, Hkv, Dk, Dv;
+  int32_t num_summary_levels;  /* L (tree has L + 1 levels)                 */
+  int32_t dtype;               /* q and the packed k / v element type       */
+  int32_t w_dtype;             /* packed w element type                     */
+  const void* q;               /* [B, N, Hq, Dk] (qk mode) or NULL          */
+  const void* k_packed;        /* [B, total, Hkv, Dk] forward levels        */
+  const void* v_packed;        /* [B, total, Hkv, Dv]                       */
+  const void* w_packed;        /* [B, total, Hkv]                           */
+  float* gk;                   /* [B, total, Hkv, Dk] fp32, in/out          */
+  float* gv;                   /* [B, total, Hkv, Dv] fp32, in/out          */
+  float* gw;                   /* [B, total, Hkv] fp32, in/out              */
+  void* dq;                    /* [B, N, Hq, Dk] out (qk mode)              */
+  int32_t dq_dtype;
+  int32_t detach;              /* detach_weights: no gradient through w     */
+  int64_t total;               /* sum_l (N >> l)                            */
+} tc_tree_bwd_args;
+int tc_build_tree_bwd(const tc_tree_bwd_args* a, void* stream);
+
+/* VJP of short_conv (reference.py:167-211) for one tensor x [B, N, C] with
+ * conv weight w [C, K]: dx[t] = dy[t] + sum_j w[c, j] dy[t + K - 1 - j] and
+ * dw[c, j] = sum_{b, t} dy[t, c] x[t - K + 1 + j, c].  dy is fp32; dx is
+ * written in dtype, dw in fp32.  The dw reduction runs in a fixed order
+ * (per-chunk partials, then their sum): partial_floats must be at least
+ * B * ceil(N / 256) * C * K. */
+int tc_short_conv_bwd(int32_t B, int32_t N, int32_t C, int32_t dtype, const void* x, int32_t K,
+                      int32_t w_dtype, const void* w, const float* dy, void* dx, float* dw, float* partials,
+                      int64_t partial_floats, void* stream);
+
 /* w[b, t, h] = x[b, t, :] . w_proj[h, :] (compute_linear_weights,
  * reference.py:148-164).  x [rows, E], w_proj [H, E], out [rows, H]. */
 int tc_linear_weights(int64_t rows, int32_t E, int32_t H, int32_t x_dtype, const void* x,

@@ -104,6 +104,105 @@ def build_tree(k, v, w, num_summary_levels, store=identity):
     return kl, vl, wl
 
 
+def short_conv_vjp(x, weight, dy):
+    """VJP of short_conv: dx[s] = dy[s] + sum_j weight[c,j] dy[s+K-1-j] and
+    dweight[c,j] = sum_{b,t} dy[t,c] x[t-K+1+j,c] (zero padding)."""
+    x = np.asarray(x, np.float64)
+    w = np.asarray(weight, np.float64)
+    dy = np.asarray(dy, np.float64)
+    n, kk = x.shape[1], w.shape[1]
+    dx = dy.copy()
+    dw = np.zeros_like(w)
+    for j in range(kk):
+        back = kk - 1 - j
+        if back < n:
+            dx[:, : n - back, :] += w[:, j] * dy[:, back:, :]
+            dw[:, j] = np.einsum("btc,btc->c", dy[:, back:, :], x[:, : n - back, :])
+    return dx, dw
+
+
+def build_tree_vjp(q, k, v, num_summary_levels, dk_packed, dv_packed, dw_packed, x=None, w_proj=None,
+                   k_conv_weight=None, v_conv_weight=None, detach_weights=False):
+    """VJP of build_dyadic_summaries (reference.py:465-584) in float64 for
+    upstream gradients of the packed levels dk_packed [B, total, Hkv, Dk],
+    dv_packed [B, total, Hkv, Dv] and dw_packed [B, total, Hkv].
+
+    Forward as the reference: optional short conv of k and v, merge weights
+    (qk logsumexp over the GQA group, or x @ w_proj^T), then per level
+    alpha = softmax(w0, w1), parent = alpha0 child0 + alpha1 child1,
+    w_parent = logsumexp(w0, w1).  Backward from the coarsest level down:
+      dchild_i += alpha_i dparent                       (k and v)
+      dalpha_i  = dk_parent . k_child_i + dv_parent . v_child_i
+      dw_i     += alpha_i (dalpha_i - sum_j alpha_j dalpha_j) + alpha_i dw_parent
+    then level 0's dw through the weights (cut by detach_weights) and dk, dv
+    through the conv.  Returns a dict of dq, dk, dv and, when present, dx,
+    dw_proj, dkcw, dvcw (float64)."""
+    q = np.asarray(q, np.float64)
+    k_pre = np.asarray(k, np.float64)
+    v_pre = np.asarray(v, np.float64)
+    B, N, Hkv, Dk = k_pre.shape
+    Dv = v_pre.shape[-1]
+    k0, v0 = k_pre, v_pre
+    if k_conv_weight is not None:
+        k0 = short_conv(k_pre.reshape(B, N, Hkv * Dk), k_conv_weight).reshape(B, N, Hkv, Dk)
+        v0 = short_conv(v_pre.reshape(B, N, Hkv * Dv), v_conv_weight).reshape(B, N, Hkv, Dv)
+    w0 = linear_weights(x, w_proj) if x is not None else qk_weights(q, k0)
+    kl, vl, wl = build_tree(k0, v0, w0, num_summary_levels)
+    offs = np.cumsum([0] + [a.shape[1] for a in kl])
+    gk = [np.array(dk_packed[:, offs[l]:offs[l + 1]], np.float64) for l in range(len(kl))]
+    gv = [np.array(dv_packed[:, offs[l]:offs[l + 1]], np.float64) for l in range(len(kl))]
+    gw = [np.array(dw_packed[:, offs[l]:offs[l + 1]], np.float64) for l in range(len(kl))]
+    for l in range(len(kl) - 1, 0, -1):
+        npar = kl[l].shape[1]
+        if npar == 0:
+            continue
+        c0, c1 = slice(0, 2 * npar, 2), slice(1, 2 * npar, 2)
+        wc0, wc1 = wl[l - 1][:, c0], wl[l - 1][:, c1]
+        m = np.maximum(wc0, wc1)
+        e0, e1 = np.exp(wc0 - m), np.exp(wc1 - m)
+        a0, a1 = e0 / (e0 + e1), e1 / (e0 + e1)
+        dkp, dvp, dwp = gk[l], gv[l], gw[l]
+        gk[l - 1][:, c0] += a0[..., None] * dkp
+        gk[l - 1][:, c1] += a1[..., None] * dkp
+        gv[l - 1][:, c0] += a0[..., None] * dvp
+        gv[l - 1][:, c1] += a1[..., None] * dvp
+        da0 = (dkp * kl[l - 1][:, c0]).sum(-1) + (dvp * vl[l - 1][:, c0]).sum(-1)
+        da1 = (dkp * kl[l - 1][:, c1]).sum(-1) + (dvp * vl[l - 1][:, c1]).sum(-1)
+        sa = a0 * da0 + a1 * da1
+        gw[l - 1][:, c0] += a0 * (da0 - sa) + a0 * dwp
+        gw[l - 1][:, c1] += a1 * (da1 - sa) + a1 * dwp
+    dk0, dv0, dw0 = gk[0], gv[0], gw[0]
+    out = {"dq": np.zeros_like(q)}
+    if not detach_weights:
+        if x is not None:
+            xx = np.asarray(x, np.float64)
+            out["dx"] = dw0 @ np.asarray(w_proj, np.float64)
+            out["dw_proj"] = np.einsum("bnh,bne->he", dw0, xx)
+        else:
+            Hq = q.shape[2]
+            E = Hq // Hkv
+            qg = q.reshape(B, N, Hkv, E, Dk)
+            sc = 1.0 / math.sqrt(Dk)
+            s_ = np.einsum("bnhed,bnhd->bnhe", qg, k0) * sc
+            p = np.exp(s_ - s_.max(-1, keepdims=True))
+            p /= p.sum(-1, keepdims=True)
+            ds = dw0[..., None] * p
+            out["dq"] = (ds[..., None] * k0[:, :, :, None, :] * sc).reshape(B, N, Hq, Dk)
+            dk0 = dk0 + np.einsum("bnhe,bnhed->bnhd", ds, qg) * sc
+    elif x is not None:
+        out["dx"] = np.zeros(np.shape(x))
+        out["dw_proj"] = np.zeros(np.shape(w_proj))
+    if k_conv_weight is not None:
+        dk, out["dkcw"] = short_conv_vjp(k_pre.reshape(B, N, Hkv * Dk), k_conv_weight,
+                                         dk0.reshape(B, N, Hkv * Dk))
+        dv, out["dvcw"] = short_conv_vjp(v_pre.reshape(B, N, Hkv * Dv), v_conv_weight,
+                                         dv0.reshape(B, N, Hkv * Dv))
+        out["dk"], out["dv"] = dk.reshape(B, N, Hkv, Dk), dv.reshape(B, N, Hkv, Dv)
+    else:
+        out["dk"], out["dv"] = dk0, dv0
+    return out
+
+
 def pack(levels):
     """Level-major concatenation [L0 | L1 | ...] along the sequence axis
     (reference.py:604-640)."""

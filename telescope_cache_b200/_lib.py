@@ -41,6 +41,16 @@ class TreeArgs(ctypes.Structure):
     ]
 
 
+class TreeBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("B", _c_i32), ("N", _c_i32), ("Hq", _c_i32), ("Hkv", _c_i32), ("Dk", _c_i32),
+        ("Dv", _c_i32), ("num_summary_levels", _c_i32), ("dtype", _c_i32), ("w_dtype", _c_i32),
+        ("q", _c_vp), ("k_packed", _c_vp), ("v_packed", _c_vp), ("w_packed", _c_vp), ("gk", _c_vp),
+        ("gv", _c_vp), ("gw", _c_vp), ("dq", _c_vp), ("dq_dtype", _c_i32), ("detach", _c_i32),
+        ("total", _c_i64),
+    ]
+
+
 class AttnArgs(ctypes.Structure):
     _fields_ = [
         ("B", _c_i32), ("N", _c_i32), ("Hq", _c_i32), ("Hkv", _c_i32), ("Dk", _c_i32),
@@ -85,6 +95,9 @@ SIGNATURES = {
     "tc_hulls_host": [ctypes.POINTER(Schedule), _c_i32, _c_i32, _c_vp, _c_vp, _c_i32, _c_vp],
     "tc_range_bounds_device": [ctypes.POINTER(Schedule), _c_vp, _c_i32, _c_vp, _c_vp],
     "tc_build_tree": [ctypes.POINTER(TreeArgs), _c_vp],
+    "tc_build_tree_bwd": [ctypes.POINTER(TreeBwdArgs), _c_vp],
+    "tc_short_conv_bwd": [_c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_i32, _c_i32, _c_vp, _c_vp, _c_vp, _c_vp,
+                          _c_vp, _c_i64, _c_vp],
     "tc_linear_weights": [_c_i64, _c_i32, _c_i32, _c_i32, _c_vp, _c_i32, _c_vp, _c_i32, _c_vp, _c_vp],
     "tc_qk_weights": [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_vp, _c_i32, _c_vp,
                       _c_vp],

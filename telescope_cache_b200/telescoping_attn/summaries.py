@@ -5,8 +5,12 @@ The builder is one fused CUDA launch (``tc_build_tree``) that writes every
 level straight into a level-major packed buffer; the per-level tensors it
 returns are views of that buffer, so ``pack_levels`` on them copies nothing.
 
-The returned tensors are not attached to autograd (the Phase-1 VJP of the
-reference is left to torch autograd; here it is not provided yet).
+When an input requires gradients the packed buffers come from a
+``torch.autograd.Function`` whose backward is the Phase-1 VJP in CUDA
+(``tc_build_tree_bwd``: the pair merges from the coarsest level down and the
+qk merge weights; ``tc_short_conv_bwd``: the conv), with the linear merge
+weights' two GEMMs through cuBLAS -- the gradients the reference obtains from
+torch autograd on ``build_dyadic_summaries``.
 """
 
 import ctypes
@@ -82,30 +86,8 @@ def short_conv(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     return y
 
 
-def build_dyadic_summaries(
-    q: torch.Tensor,
-    k: torch.Tensor,
-    v: torch.Tensor,
-    num_summary_levels: int,
-    detach_weights: bool = False,
-    x: Optional[torch.Tensor] = None,
-    w_proj: Optional[torch.Tensor] = None,
-    k_conv_weight: Optional[torch.Tensor] = None,
-    v_conv_weight: Optional[torch.Tensor] = None,
-):
-    """The canonical dyadic K/V tree, levels 0..L (reference.py:465-584).
-
-    Level 0 is k/v after the optional short conv; parent j of level l merges
-    children (2j, 2j+1) with alpha = softmax(w0, w1) and takes
-    w = logsumexp(w0, w1); odd trailing nodes are dropped.  Merge weights are
-    qk-logsumexp (x and w_proj None) or x @ w_proj^T (both given).
-
-    Returns (k_levels, v_levels, w_levels): lists of L + 1 views
-    [B, N >> l, Hkv, D] / [B, N >> l, Hkv, 1] of one level-major packed
-    buffer per tensor.  ``detach_weights`` only affects gradients in the
-    reference; these outputs carry none, so it is accepted and ignored.
-    """
-    del detach_weights
+def _build_packed(q, k, v, num_summary_levels, x, w_proj, k_conv_weight, v_conv_weight):
+    """The forward builder: (k_packed, v_packed, w_packed, level offsets)."""
     if (k_conv_weight is None) != (v_conv_weight is None):
         raise ValueError(
             "k_conv_weight and v_conv_weight must both be provided or both be None")
@@ -163,6 +145,118 @@ def build_dyadic_summaries(
             conv_dtype=_lib.dtype_code(kcw.dtype) if conv_k else 0, conv_k=conv_k,
             k_packed=kp.data_ptr(), v_packed=vp.data_ptr(), w_packed=wp.data_ptr(), total=total)
         _lib.check(_lib.lib().tc_build_tree(ctypes.byref(args), _lib.stream_of(k)), "tc_build_tree")
+    return kp, vp, wp, offs
+
+
+class _DyadicTree(torch.autograd.Function):
+    """Packed tree with the Phase-1 VJP as its backward."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, x, w_proj, k_conv_weight, v_conv_weight, num_summary_levels, detach):
+        kp, vp, wp, offs = _build_packed(q, k, v, num_summary_levels, x, w_proj, k_conv_weight,
+                                         v_conv_weight)
+        ctx.save_for_backward(q, k, v, x, w_proj, k_conv_weight, v_conv_weight, kp, vp, wp)
+        ctx.cfg = (int(num_summary_levels), bool(detach), tuple(offs))
+        return kp, vp, wp
+
+    @staticmethod
+    def backward(ctx, gkp, gvp, gwp):
+        q, k, v, x, w_proj, kcw, vcw, kp, vp, wp = ctx.saved_tensors
+        L, detach, offs = ctx.cfg
+        B, N, Hkv, Dk = k.shape
+        Dv, Hq = v.shape[-1], q.shape[2]
+        dtype = v.dtype
+        total = kp.shape[1]
+        f32 = dict(device=k.device, dtype=torch.float32)
+        gk = torch.zeros(B, total, Hkv, Dk, **f32) if gkp is None else gkp.float().contiguous().clone()
+        gv = torch.zeros(B, total, Hkv, Dv, **f32) if gvp is None else gvp.float().contiguous().clone()
+        gw = torch.zeros(B, total, Hkv, **f32) if gwp is None else gwp.float().contiguous().clone()
+        linear = x is not None
+        qc = dq = None
+        if not linear and not detach:
+            qc = _contig(q.to(dtype))
+            dq = torch.empty(qc.shape, device=q.device, dtype=dtype)
+        args = _lib.TreeBwdArgs(
+            B=B, N=N, Hq=Hq, Hkv=Hkv, Dk=Dk, Dv=Dv, num_summary_levels=L, dtype=_lib.dtype_code(dtype),
+            w_dtype=_lib.dtype_code(wp.dtype), q=None if qc is None else qc.data_ptr(),
+            k_packed=kp.data_ptr(), v_packed=vp.data_ptr(), w_packed=wp.data_ptr(), gk=gk.data_ptr(),
+            gv=gv.data_ptr(), gw=gw.data_ptr(), dq=None if dq is None else dq.data_ptr(),
+            dq_dtype=_lib.dtype_code(dtype), detach=int(detach), total=total)
+        _lib.check(_lib.lib().tc_build_tree_bwd(ctypes.byref(args), _lib.stream_of(k)),
+                   "tc_build_tree_bwd")
+        dq_out = torch.zeros_like(q) if dq is None else dq.to(q.dtype)
+        dx = dwp = None
+        if linear and not detach:
+            # w0 = x @ w_proj^T: two plain GEMMs (cuBLAS through torch)
+            dw0 = gw[:, :N]
+            dx = dw0.matmul(w_proj.float()).to(x.dtype)
+            dwp = dw0.reshape(-1, Hkv).t().matmul(x.reshape(-1, x.shape[-1]).float()).to(w_proj.dtype)
+        dk0 = gk[:, :N].contiguous()
+        dv0 = gv[:, :N].contiguous()
+        dkcw = dvcw = None
+        if kcw is not None:
+            dk, dkcw = _short_conv_vjp(k, kcw, dk0)
+            dv, dvcw = _short_conv_vjp(v, vcw, dv0)
+        else:
+            dk, dv = dk0.to(k.dtype), dv0.to(v.dtype)
+        return dq_out, dk, dv, dx, dwp, dkcw, dvcw, None, None
+
+
+def _short_conv_vjp(x_pre, weight, dy):
+    """dx (x_pre's dtype) and dweight (weight's dtype) of short_conv for fp32
+    dy [B, N, H, D] (tc_short_conv_bwd)."""
+    B, N = x_pre.shape[:2]
+    C = x_pre[0, 0].numel()
+    K = weight.shape[1]
+    xc = _contig(x_pre)
+    wc = _contig(weight)
+    dx = torch.empty_like(xc)
+    dw = torch.empty(C, K, device=x_pre.device, dtype=torch.float32)
+    parts = torch.empty(max(1, B * ((N + 255) // 256) * C * K), device=x_pre.device, dtype=torch.float32)
+    _lib.check(_lib.lib().tc_short_conv_bwd(
+        B, N, C, _lib.dtype_code(xc.dtype), _lib.ptr(xc), K, _lib.dtype_code(wc.dtype), _lib.ptr(wc),
+        _lib.ptr(dy), _lib.ptr(dx), _lib.ptr(dw), _lib.ptr(parts), parts.numel(), _lib.stream_of(xc)),
+        "tc_short_conv_bwd")
+    return dx.reshape(x_pre.shape), dw.to(weight.dtype)
+
+
+def build_dyadic_summaries(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    num_summary_levels: int,
+    detach_weights: bool = False,
+    x: Optional[torch.Tensor] = None,
+    w_proj: Optional[torch.Tensor] = None,
+    k_conv_weight: Optional[torch.Tensor] = None,
+    v_conv_weight: Optional[torch.Tensor] = None,
+):
+    """The canonical dyadic K/V tree, levels 0..L (reference.py:465-584).
+
+    Level 0 is k/v after the optional short conv; parent j of level l merges
+    children (2j, 2j+1) with alpha = softmax(w0, w1) and takes
+    w = logsumexp(w0, w1); odd trailing nodes are dropped.  Merge weights are
+    qk-logsumexp (x and w_proj None) or x @ w_proj^T (both given).
+
+    Returns (k_levels, v_levels, w_levels): lists of L + 1 views
+    [B, N >> l, Hkv, D] / [B, N >> l, Hkv, 1] of one level-major packed
+    buffer per tensor.  With grad mode on and any input requiring gradients,
+    the buffers carry the Phase-1 VJP; ``detach_weights`` then cuts the
+    gradient through the merge weights (q / k in qk mode, x / w_proj in
+    linear mode), as in the reference.
+    """
+    inputs = (q, k, v, x, w_proj, k_conv_weight, v_conv_weight)
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in inputs):
+        kp, vp, wp = _DyadicTree.apply(q, k, v, x, w_proj, k_conv_weight, v_conv_weight,
+                                       int(num_summary_levels), bool(detach_weights))
+        N = k.shape[1]
+        offs = [0]
+        for lv in range(int(num_summary_levels) + 1):
+            offs.append(offs[-1] + (N >> lv))
+    else:
+        kp, vp, wp, offs = _build_packed(q, k, v, num_summary_levels, x, w_proj, k_conv_weight,
+                                         v_conv_weight)
+    L = int(num_summary_levels)
     k_levels, v_levels, w_levels = [], [], []
     for lv in range(L + 1):
         kl = kp[:, offs[lv]:offs[lv + 1]]

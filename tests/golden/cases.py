@@ -141,6 +141,17 @@ CASES = [
          sink=True, gate=True, tail=40, seed=515),
     case("dec_rel_split_bf16", "decode", "d128_dec", dtype="bf16", position="relative",
          tail=24, seed=516),
+    # Phase-1 VJP (tree / merge weights / short conv backward): the gradients
+    # of q, k, v (and x, w_proj, the conv weights) for seeded upstream
+    # gradients of the packed k, v and w levels (make_tree_grads)
+    case("vjp_qk_tiny", "treevjp", "tiny", seed=30),
+    case("vjp_lin_odd", "treevjp", "odd_n", weights="linear", seed=31),
+    case("vjp_conv_four", "treevjp", "four_levels", conv=3, seed=32),
+    case("vjp_conv_lin_odd", "treevjp", "odd_n", conv=4, weights="linear", seed=33),
+    dict(case("vjp_detach_four", "treevjp", "four_levels", conv=2, seed=34), detach=True),
+    case("vjp_bf16_d128", "treevjp", "d128", dtype="bf16", conv=4, seed=35),
+    case("vjp_bf16_d128_lin_odd", "treevjp", "d128_odd", dtype="bf16", weights="linear", seed=36),
+    case("vjp_bf16_d128_deep", "treevjp", "d128_deep", dtype="bf16", conv=4, seed=37),
 ]
 
 CASE_BY_NAME = {c["name"]: c for c in CASES}
@@ -183,6 +194,27 @@ def make_inputs(c):
     if c["dtype"] == "bf16":
         inp = {k: bf16_round(v) for k, v in inp.items()}
     return inp
+
+
+def tree_total(c):
+    """Packed length of case `c`'s tree (levels 0 .. len(fmap))."""
+    g = GEOS[c["geo"]]
+    return sum(g["N"] >> l for l in range(len(g["fmap"]) + 1))
+
+
+def make_tree_grads(c):
+    """Seeded upstream gradients of the packed k, v and w levels of a
+    treevjp case: dk [B, total, Hkv, Dk], dv [B, total, Hkv, Dv],
+    dw [B, total, Hkv] (bf16-rounded for bf16 cases)."""
+    g = GEOS[c["geo"]]
+    B, Hkv, Dk, Dv = (g[k] for k in ("B", "Hkv", "Dk", "Dv"))
+    total = tree_total(c)
+    r = _rng(c["seed"] + 1000)
+    f = lambda *s: r.standard_normal(s).astype(np.float32)  # noqa: E731
+    out = dict(dk=f(B, total, Hkv, Dk), dv=f(B, total, Hkv, Dv), dw=f(B, total, Hkv))
+    if c["dtype"] == "bf16":
+        out = {k: bf16_round(v) for k, v in out.items()}
+    return out
 
 
 def case_json(c):

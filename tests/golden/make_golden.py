@@ -71,8 +71,38 @@ def positional(ref, c, inp, g, n_pos):
     return {}
 
 
+def gen_tree_vjp(ref, c):
+    """Phase-1 VJP: the reference's forward tree under autograd (float32),
+    reduced against the seeded upstream gradients of the packed k, v, w."""
+    import torch
+    g = C.GEOS[c["geo"]]
+    inp = C.make_inputs(c)
+    up = C.make_tree_grads(c)
+    leaves = {k_: t(inp[k_]).requires_grad_(True) for k_ in ("q", "k", "v")}
+    kw = {}
+    if c["conv"]:
+        leaves["kcw"] = t(inp["kcw"]).requires_grad_(True)
+        leaves["vcw"] = t(inp["vcw"]).requires_grad_(True)
+        kw.update(k_conv_weight=leaves["kcw"], v_conv_weight=leaves["vcw"])
+    if c["weights"] == "linear":
+        leaves["x"] = t(inp["x"]).requires_grad_(True)
+        leaves["w_proj"] = t(inp["w_proj"]).requires_grad_(True)
+        kw.update(x=leaves["x"], w_proj=leaves["w_proj"])
+    kl, vl, wl = ref.build_dyadic_summaries(leaves["q"], leaves["k"], leaves["v"], len(g["fmap"]),
+                                            detach_weights=c.get("detach", False), **kw)
+    kp, vp, wp = torch.cat(kl, 1), torch.cat(vl, 1), torch.cat(wl, 1)[..., 0]
+    loss = (kp * t(up["dk"])).sum() + (vp * t(up["dv"])).sum() + (wp * t(up["dw"])).sum()
+    loss.backward()
+    out = {}
+    for k_, leaf in leaves.items():
+        out["d" + k_] = n(leaf.grad) if leaf.grad is not None else np.zeros(leaf.shape, np.float32)
+    return out
+
+
 def gen_case(rs, ref, c):
     import torch
+    if c["kind"] == "treevjp":
+        return gen_tree_vjp(ref, c)
     g = C.GEOS[c["geo"]]
     inp = C.make_inputs(c)
     out = {}

@@ -50,7 +50,24 @@ def positional(c, inp, g, n_pos):
     return O.Positional()
 
 
+def oracle_tree_vjp(c, inp=None):
+    """The float64 Phase-1 VJP of a treevjp case (upstream gradients from
+    make_tree_grads)."""
+    g = C.GEOS[c["geo"]]
+    inp = C.make_inputs(c) if inp is None else inp
+    up = C.make_tree_grads(c)
+    kw = {}
+    if c["conv"]:
+        kw.update(k_conv_weight=inp["kcw"], v_conv_weight=inp["vcw"])
+    if c["weights"] == "linear":
+        kw.update(x=inp["x"], w_proj=inp["w_proj"])
+    return O.build_tree_vjp(inp["q"], inp["k"], inp["v"], len(g["fmap"]), up["dk"], up["dv"], up["dw"],
+                            detach_weights=c.get("detach", False), **kw)
+
+
 def oracle_case(c, inp=None, store=O.identity):
+    if c["kind"] == "treevjp":
+        return oracle_tree_vjp(c, inp)
     g = C.GEOS[c["geo"]]
     inp = C.make_inputs(c) if inp is None else inp
     res = {}

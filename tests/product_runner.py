@@ -40,7 +40,35 @@ def f64(x):
     return x.detach().double().cpu().numpy()
 
 
+def product_tree_vjp(c, inp=None):
+    """Phase-1 VJP through the product's autograd path: the packed levels of
+    build_dyadic_summaries reduced against the seeded upstream gradients."""
+    g = C.GEOS[c["geo"]]
+    inp = C.make_inputs(c) if inp is None else inp
+    dt = DT[c["dtype"]]
+    t = to_dev(inp, dt)
+    up = to_dev(C.make_tree_grads(c), dt)
+    names = ["q", "k", "v"] + (["kcw", "vcw"] if c["conv"] else []) + \
+        (["x", "w_proj"] if c["weights"] == "linear" else [])
+    leaves = {n_: t[n_].clone().requires_grad_(True) for n_ in names}
+    kw = {}
+    if c["conv"]:
+        kw.update(k_conv_weight=leaves["kcw"], v_conv_weight=leaves["vcw"])
+    if c["weights"] == "linear":
+        kw.update(x=leaves["x"], w_proj=leaves["w_proj"])
+    kl, vl, wl = T.build_dyadic_summaries(leaves["q"], leaves["k"], leaves["v"], len(g["fmap"]),
+                                          detach_weights=c.get("detach", False), **kw)
+    kp, vp, wp = torch.cat(kl, 1), torch.cat(vl, 1), torch.cat(wl, 1)[..., 0]
+    loss = ((kp.float() * up["dk"].float()).sum() + (vp.float() * up["dv"].float()).sum()
+            + (wp.float() * up["dw"].float()).sum())
+    loss.backward()
+    return {"d" + n_: (f64(x_.grad) if x_.grad is not None else np.zeros(tuple(x_.shape)))
+            for n_, x_ in leaves.items()}
+
+
 def product_case(c, inp=None, impl=None):
+    if c["kind"] == "treevjp":
+        return product_tree_vjp(c, inp)
     g = C.GEOS[c["geo"]]
     inp = C.make_inputs(c) if inp is None else inp
     t = to_dev(inp, DT[c["dtype"]])

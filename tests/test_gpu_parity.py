@@ -1,7 +1,8 @@
 """CUDA path vs the reference (golden fixtures) and the CPU oracle, on every
 golden case: builder, forward (none / rope / relative, softcap on/off, sink,
 gate, GQA, odd lengths, eviction), backward at the packed boundary with the
-sink dlse seam, and incremental decode.
+sink dlse seam, incremental decode, and the Phase-1 VJP (tree, merge
+weights, conv) through autograd.
 
 Tolerances: fp32 cases use the reference suite's own (1e-5 forward, 1e-4
 gradients, test_reference.py:118-119); bf16 cases must be within 2e-2
@@ -17,7 +18,8 @@ from oracle_runner import load_golden, oracle_case
 
 pytestmark = pytest.mark.gpu
 
-GRAD_KEYS = {"dq", "dk_packed", "dv_packed", "dpos", "dsinks", "dlse", "dout_pre"}
+GRAD_KEYS = {"dq", "dk_packed", "dv_packed", "dpos", "dsinks", "dlse", "dout_pre", "dk", "dv", "dx",
+             "dw_proj", "dkcw", "dvcw"}
 BF16_REL = 2e-2
 
 
@@ -64,7 +66,7 @@ def test_cuda_matches_reference_golden(cuda, name):
     check_against(name, c, got, gold, gold.get("ring_live"))
 
 
-@pytest.mark.parametrize("name", [c["name"] for c in C.CASES if c["kind"] in ("fwd", "bwd")])
+@pytest.mark.parametrize("name", [c["name"] for c in C.CASES if c["kind"] in ("fwd", "bwd", "treevjp")])
 def test_cuda_matches_oracle(cuda, name):
     from product_runner import product_case
     c = C.CASE_BY_NAME[name]

@@ -14,7 +14,8 @@ from oracle_runner import load_golden, oracle_case
 RTOL = ATOL = 1e-5          # reference suite's forward tolerance (test_reference.py:118)
 GRAD_RTOL = GRAD_ATOL = 1e-4  # reference suite's gradient tolerance (test_reference.py:119)
 
-GRAD_KEYS = {"dq", "dk_packed", "dv_packed", "dpos", "dsinks", "dlse", "dout_pre"}
+GRAD_KEYS = {"dq", "dk_packed", "dv_packed", "dpos", "dsinks", "dlse", "dout_pre", "dk", "dv", "dx",
+             "dw_proj", "dkcw", "dvcw"}
 
 
 @pytest.mark.parametrize("name", [c["name"] for c in C.CASES])
