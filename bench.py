@@ -202,6 +202,68 @@ def run_step(T, wl, inp, fmap, cache, tables, timers=None):
     return dq, dk, dv, dpos, out
 
 
+def vjp_bench(T, wl, inp, grads, args, hbm, flush):
+    """Phase-1 VJP (the backward of build_dyadic_summaries) at the workload's
+    shapes: the explicit backward from the Phase-2 step's packed dK / dV
+    (no weight-level upstream gradient), W warm-up and K timed calls with
+    CUDA events, L2 flushed before each.  Algorithmic bytes: the upstream
+    gradients and the forward rows every merge reads (children of levels
+    0..L-1), q and dq in qk mode, x and dx in linear mode, the level-0
+    gradients written once."""
+    import torch
+
+    from telescope_cache_b200 import _lib
+    from telescope_cache_b200.telescoping_attn import summaries as S
+    L = wl["levels"] - 1
+    kw = {}
+    if wl["weights"] == "linear":
+        kw.update(x=inp["x"], w_proj=inp["w_proj"])
+    if wl["conv"]:
+        kw.update(k_conv_weight=inp["kcw"], v_conv_weight=inp["vcw"])
+    kl, vl, wls = T.build_dyadic_summaries(inp["q"], inp["k"], inp["v"], L, **kw)
+    packed = T.pack_levels(kl, vl)
+    wp = torch.cat(wls, 1)[..., 0]
+    dk, dv = grads
+
+    def call():
+        return S.build_dyadic_summaries_backward(inp["q"], inp["k"], inp["v"], L, packed.k, packed.v, wp,
+                                                 dk, dv, None, **kw)
+
+    for _ in range(max(args.warmup, 1)):
+        call()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    n0 = _lib.launch_count()
+    for a, b in ev:
+        flush.zero_()
+        a.record(st)
+        call()
+        b.record(st)
+    torch.cuda.synchronize()
+    launches = (_lib.launch_count() - n0) // args.steps
+    ms = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
+    B, N, H, D = wl["B"], wl["T"], wl["H"], wl["D"]
+    total = sum(N >> lv for lv in range(L + 1))
+    el = 2  # bf16
+    rows = B * H
+    nbytes = rows * total * 2 * D * el                   # upstream dK, dV (packed)
+    nbytes += rows * (total - (N >> L)) * (2 * D * el + wp.element_size())  # children k, v, w
+    nbytes += rows * N * 2 * D * el                      # dk, dv written
+    if wl["weights"] == "qk":
+        nbytes += 2 * rows * N * D * el                  # q read, dq written
+    else:
+        nbytes += 2 * B * N * inp["x"].shape[-1] * el    # x read (dw_proj), dx written
+    if wl["conv"]:
+        nbytes += rows * N * 2 * D * (4 + 4 + el)        # fp32 dk0 / dv0 written and read, pre-conv rows
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    return {"what": "build_dyadic_summaries_backward (Phase-1 VJP: tree, merge weights"
+                    + (", conv" if wl["conv"] else "") + ")",
+            "ms": ms, "launches": launches, "bytes": nbytes, "achieved_gbs": achieved, "peak_gbs": hbm,
+            "frac": achieved / hbm, "upstream": "the step's packed dK, dV (bf16); no dw upstream"}
+
+
 def decode_visible(spec, t0, n):
     """Visible entries of the newest query at t0 .. t0 + n - 1."""
     from telescope_cache_b200 import range_spec as R
@@ -448,6 +510,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode", action="store_true",
                     help="skip the config-4 decode measurement added to the c3 line")
+    ap.add_argument("--no-vjp", action="store_true",
+                    help="skip the Phase-1 VJP measurement added to the line")
     args = ap.parse_args()
     if args.workload == "c4":
         return decode_main(args)
@@ -585,6 +649,11 @@ def main():
                 "forward_tflops": fwd_flops / (fms * 1e-3) / 1e12,
                 "backward_tflops": bwd_flops / (bms * 1e-3) / 1e12,
                 "forward_ms": fms, "backward_ms": bms}
+    vjp = None
+    if not args.no_vjp:
+        _, dk_s, dv_s, _, _ = run_step(T, wl, inp, fmap, cache, tables)
+        vjp = vjp_bench(T, wl, inp, (dk_s, dv_s), args, hbm, flush)
+        del dk_s, dv_s
     dec = None
     if args.workload == "c3" and not args.no_decode:
         # before the CPU baseline, whose worker threads can linger on the host
@@ -612,6 +681,8 @@ def main():
             "clocks": clocks.summary(),
             "gpu_launches": launches,
         }
+    if vjp is not None and rank == 0:
+        line["phase1_vjp"] = vjp
     if dec is not None and rank == 0:
         line["decode"] = dec
     if rank == 0:

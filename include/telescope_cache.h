@@ -146,34 +146,48 @@ typedef struct tc_tree_args {
  * build_dyadic_summaries and pack_levels (reference.py:117-211, :465-640). */
 int tc_build_tree(const tc_tree_args* a, void* stream);
 
-/* Phase-1 VJP (the backward of build_dyadic_summaries, reference.py:465-584,
- * which the reference takes through torch autograd).  On entry gk / gv / gw
- * hold the upstream gradients of the packed levels in fp32 (zeros where
- * none); from the coarsest level down every parent's gradient is propagated
- * to its two children (alpha = softmax(w0, w1), parent = sum alpha child,
- * w_parent = logsumexp), so on return level 0 of gk / gv / gw holds the
- * gradients of the post-conv keys, values and level-0 merge weights.  In qk
- * weight mode (q non-NULL, detach 0) dw0 then goes through w =
- * logsumexp_e(q_e . k / sqrt(Dk)): dq is written and the k part added to
- * level 0 of gk; with q NULL (linear weights) or detach 1, dq is not touched
- * and dw0 is left for the caller (x @ w_proj^T's two GEMMs). */
+/* Phase-1 VJP: the backward of build_dyadic_summaries (reference.py:465-584,
+ * which the reference takes through torch autograd), from the upstream
+ * gradients of the packed levels to the gradients of the level-0 (post-conv)
+ * keys, values and merge weights, and of q.
+ *
+ * From the coarsest level down every parent's gradient goes to its two
+ * children (alpha = softmax(w0, w1), parent = sum alpha child, w_parent =
+ * logsumexp(w0, w1)).  In qk weight mode (q non-NULL, detach 0) the level-0
+ * weight gradient then goes through w = logsumexp_e(q_e . k / sqrt(Dk)):
+ * dq is written and its k part is in dk0.  With q NULL (linear weights) or
+ * detach 1 dq is not touched; dw0, when non-NULL, receives the level-0
+ * weight gradient (for the caller's x @ w_proj^T GEMMs).
+ *
+ * Upstream gradients have the element type of what they are the gradient
+ * of (gk / gv: dtype, gw: w_dtype); a NULL one counts as zeros.  dq has
+ * dtype; dk0 / dv0 have d0_dtype (dtype, or TC_F32 for a following conv
+ * VJP).  Levels above the 64-leaf tiles (L > 6) need device scratch of
+ * tc_tree_bwd_scratch_bytes(a) bytes (0 otherwise). */
 typedef struct tc_tree_bwd_args {
   int32_t B, N, Hq, Hkv, Dk, Dv;
   int32_t num_summary_levels;  /* L (tree has L + 1 levels)                 */
-  int32_t dtype;               /* q and the packed k / v element type       */
-  int32_t w_dtype;             /* packed w element type                     */
+  int32_t dtype;               /* q, packed k / v, gk / gv element type     */
+  int32_t w_dtype;             /* packed w and gw element type              */
+  int32_t detach;              /* detach_weights: no gradient through w     */
   const void* q;               /* [B, N, Hq, Dk] (qk mode) or NULL          */
   const void* k_packed;        /* [B, total, Hkv, Dk] forward levels        */
   const void* v_packed;        /* [B, total, Hkv, Dv]                       */
   const void* w_packed;        /* [B, total, Hkv]                           */
-  float* gk;                   /* [B, total, Hkv, Dk] fp32, in/out          */
-  float* gv;                   /* [B, total, Hkv, Dv] fp32, in/out          */
-  float* gw;                   /* [B, total, Hkv] fp32, in/out              */
+  const void* gk_packed;       /* [B, total, Hkv, Dk] upstream, or NULL     */
+  const void* gv_packed;       /* [B, total, Hkv, Dv] upstream, or NULL     */
+  const void* gw_packed;       /* [B, total, Hkv] upstream, or NULL         */
   void* dq;                    /* [B, N, Hq, Dk] out (qk mode)              */
-  int32_t dq_dtype;
-  int32_t detach;              /* detach_weights: no gradient through w     */
+  int32_t dq_dtype;            /* must equal dtype                          */
+  int32_t d0_dtype;            /* dtype or TC_F32                           */
+  void* dk0;                   /* [B, N, Hkv, Dk] out                       */
+  void* dv0;                   /* [B, N, Hkv, Dv] out                       */
+  float* dw0;                  /* [B, N, Hkv] out, or NULL                  */
+  void* scratch;               /* device scratch                            */
+  int64_t scratch_bytes;
   int64_t total;               /* sum_l (N >> l)                            */
 } tc_tree_bwd_args;
+int64_t tc_tree_bwd_scratch_bytes(const tc_tree_bwd_args* a);  /* -1 on bad arguments */
 int tc_build_tree_bwd(const tc_tree_bwd_args* a, void* stream);
 
 /* VJP of short_conv (reference.py:167-211) for one tensor x [B, N, C] with

@@ -45,9 +45,10 @@ class TreeBwdArgs(ctypes.Structure):
     _fields_ = [
         ("B", _c_i32), ("N", _c_i32), ("Hq", _c_i32), ("Hkv", _c_i32), ("Dk", _c_i32),
         ("Dv", _c_i32), ("num_summary_levels", _c_i32), ("dtype", _c_i32), ("w_dtype", _c_i32),
-        ("q", _c_vp), ("k_packed", _c_vp), ("v_packed", _c_vp), ("w_packed", _c_vp), ("gk", _c_vp),
-        ("gv", _c_vp), ("gw", _c_vp), ("dq", _c_vp), ("dq_dtype", _c_i32), ("detach", _c_i32),
-        ("total", _c_i64),
+        ("detach", _c_i32), ("q", _c_vp), ("k_packed", _c_vp), ("v_packed", _c_vp), ("w_packed", _c_vp),
+        ("gk_packed", _c_vp), ("gv_packed", _c_vp), ("gw_packed", _c_vp), ("dq", _c_vp),
+        ("dq_dtype", _c_i32), ("d0_dtype", _c_i32), ("dk0", _c_vp), ("dv0", _c_vp), ("dw0", _c_vp),
+        ("scratch", _c_vp), ("scratch_bytes", _c_i64), ("total", _c_i64),
     ]
 
 
@@ -96,6 +97,7 @@ SIGNATURES = {
     "tc_range_bounds_device": [ctypes.POINTER(Schedule), _c_vp, _c_i32, _c_vp, _c_vp],
     "tc_build_tree": [ctypes.POINTER(TreeArgs), _c_vp],
     "tc_build_tree_bwd": [ctypes.POINTER(TreeBwdArgs), _c_vp],
+    "tc_tree_bwd_scratch_bytes": [ctypes.POINTER(TreeBwdArgs)],
     "tc_short_conv_bwd": [_c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_i32, _c_i32, _c_vp, _c_vp, _c_vp, _c_vp,
                           _c_vp, _c_i64, _c_vp],
     "tc_linear_weights": [_c_i64, _c_i32, _c_i32, _c_i32, _c_vp, _c_i32, _c_vp, _c_i32, _c_vp, _c_vp],
@@ -133,6 +135,7 @@ def lib():
             fn.restype = ctypes.c_int
         handle.tc_launch_count.argtypes = []
         handle.tc_launch_count.restype = ctypes.c_int64
+        handle.tc_tree_bwd_scratch_bytes.restype = ctypes.c_int64
         _LIB = handle
     return _LIB
 

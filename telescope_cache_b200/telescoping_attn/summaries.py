@@ -10,7 +10,8 @@ When an input requires gradients the packed buffers come from a
 (``tc_build_tree_bwd``: the pair merges from the coarsest level down and the
 qk merge weights; ``tc_short_conv_bwd``: the conv), with the linear merge
 weights' two GEMMs through cuBLAS -- the gradients the reference obtains from
-torch autograd on ``build_dyadic_summaries``.
+torch autograd on ``build_dyadic_summaries``.  The same VJP is the explicit
+call ``build_dyadic_summaries_backward``.
 """
 
 import ctypes
@@ -162,44 +163,88 @@ class _DyadicTree(torch.autograd.Function):
     @staticmethod
     def backward(ctx, gkp, gvp, gwp):
         q, k, v, x, w_proj, kcw, vcw, kp, vp, wp = ctx.saved_tensors
-        L, detach, offs = ctx.cfg
-        B, N, Hkv, Dk = k.shape
-        Dv, Hq = v.shape[-1], q.shape[2]
-        dtype = v.dtype
-        total = kp.shape[1]
-        f32 = dict(device=k.device, dtype=torch.float32)
-        gk = torch.zeros(B, total, Hkv, Dk, **f32) if gkp is None else gkp.float().contiguous().clone()
-        gv = torch.zeros(B, total, Hkv, Dv, **f32) if gvp is None else gvp.float().contiguous().clone()
-        gw = torch.zeros(B, total, Hkv, **f32) if gwp is None else gwp.float().contiguous().clone()
-        linear = x is not None
-        qc = dq = None
-        if not linear and not detach:
-            qc = _contig(q.to(dtype))
-            dq = torch.empty(qc.shape, device=q.device, dtype=dtype)
-        args = _lib.TreeBwdArgs(
-            B=B, N=N, Hq=Hq, Hkv=Hkv, Dk=Dk, Dv=Dv, num_summary_levels=L, dtype=_lib.dtype_code(dtype),
-            w_dtype=_lib.dtype_code(wp.dtype), q=None if qc is None else qc.data_ptr(),
-            k_packed=kp.data_ptr(), v_packed=vp.data_ptr(), w_packed=wp.data_ptr(), gk=gk.data_ptr(),
-            gv=gv.data_ptr(), gw=gw.data_ptr(), dq=None if dq is None else dq.data_ptr(),
-            dq_dtype=_lib.dtype_code(dtype), detach=int(detach), total=total)
-        _lib.check(_lib.lib().tc_build_tree_bwd(ctypes.byref(args), _lib.stream_of(k)),
-                   "tc_build_tree_bwd")
-        dq_out = torch.zeros_like(q) if dq is None else dq.to(q.dtype)
-        dx = dwp = None
-        if linear and not detach:
-            # w0 = x @ w_proj^T: two plain GEMMs (cuBLAS through torch)
-            dw0 = gw[:, :N]
-            dx = dw0.matmul(w_proj.float()).to(x.dtype)
-            dwp = dw0.reshape(-1, Hkv).t().matmul(x.reshape(-1, x.shape[-1]).float()).to(w_proj.dtype)
-        dk0 = gk[:, :N].contiguous()
-        dv0 = gv[:, :N].contiguous()
-        dkcw = dvcw = None
-        if kcw is not None:
-            dk, dkcw = _short_conv_vjp(k, kcw, dk0)
-            dv, dvcw = _short_conv_vjp(v, vcw, dv0)
-        else:
-            dk, dv = dk0.to(k.dtype), dv0.to(v.dtype)
-        return dq_out, dk, dv, dx, dwp, dkcw, dvcw, None, None
+        L, detach, _ = ctx.cfg
+        return (*build_dyadic_summaries_backward(
+            q, k, v, L, kp, vp, wp, gkp, gvp, gwp, detach_weights=detach, x=x, w_proj=w_proj,
+            k_conv_weight=kcw, v_conv_weight=vcw), None, None)
+
+
+def build_dyadic_summaries_backward(q, k, v, num_summary_levels, k_packed, v_packed, w_packed,
+                                    dk_packed, dv_packed, dw_packed, detach_weights=False, x=None,
+                                    w_proj=None, k_conv_weight=None, v_conv_weight=None):
+    """Explicit Phase-1 VJP: gradients of build_dyadic_summaries' inputs from
+    the upstream gradients of its packed outputs (the backward the reference
+    gets from torch autograd through reference.py:117-211, 465-584).
+
+    k_packed / v_packed / w_packed are the forward's packed buffers
+    ([B, total, Hkv, D] and [B, total, Hkv] or [..., 1]); dk_packed /
+    dv_packed / dw_packed the upstream gradients in the same shapes and
+    element types, any of them None for zero.  Returns (dq, dk, dv, dx,
+    dw_proj, dk_conv_weight, dv_conv_weight), None where the input is absent
+    (dq is zeros in linear mode or with detach_weights, dx / dw_proj None
+    with detach_weights)."""
+    L, detach = int(num_summary_levels), bool(detach_weights)
+    kp, vp = k_packed, v_packed
+    wp = w_packed[..., 0] if w_packed.dim() == 4 else w_packed
+    kcw, vcw = k_conv_weight, v_conv_weight
+    B, N, Hkv, Dk = k.shape
+    Dv, Hq = v.shape[-1], q.shape[2]
+    dtype = kp.dtype
+    total = kp.shape[1]
+    linear = x is not None
+    conv = kcw is not None
+    dev = k.device
+    if dw_packed is not None and dw_packed.dim() == 4:
+        dw_packed = dw_packed[..., 0]
+    ups = [None if g is None else _contig(g) for g in (dk_packed, dv_packed, dw_packed)]
+    for g, ref in zip(ups, (kp, vp, wp)):
+        if g is not None and (g.shape != ref.shape or g.dtype != ref.dtype):
+            raise ValueError(f"upstream gradient {tuple(g.shape)} {g.dtype} does not match the packed "
+                             f"output {tuple(ref.shape)} {ref.dtype}")
+    kp, vp, wp = _contig(kp), _contig(vp), _contig(wp)
+    qc = dq = dw0 = None
+    if not linear and not detach:
+        qc = _contig(q.to(dtype))
+        dq = torch.empty(qc.shape, device=dev, dtype=dtype)
+    if linear and not detach:
+        dw0 = torch.empty(B, N, Hkv, device=dev, dtype=torch.float32)
+    d0 = torch.float32 if conv else dtype  # the conv VJP takes fp32 gradients
+    dk0 = torch.empty(B, N, Hkv, Dk, device=dev, dtype=d0)
+    dv0 = torch.empty(B, N, Hkv, Dv, device=dev, dtype=d0)
+
+    def addr(t):
+        return None if t is None else t.data_ptr()
+
+    args = _lib.TreeBwdArgs(
+        B=B, N=N, Hq=Hq, Hkv=Hkv, Dk=Dk, Dv=Dv, num_summary_levels=L, dtype=_lib.dtype_code(dtype),
+        w_dtype=_lib.dtype_code(wp.dtype), detach=int(detach), q=addr(qc),
+        k_packed=kp.data_ptr(), v_packed=vp.data_ptr(), w_packed=wp.data_ptr(),
+        gk_packed=addr(ups[0]), gv_packed=addr(ups[1]), gw_packed=addr(ups[2]),
+        dq=addr(dq), dq_dtype=_lib.dtype_code(dtype), d0_dtype=_lib.dtype_code(d0),
+        dk0=dk0.data_ptr(), dv0=dv0.data_ptr(), dw0=addr(dw0), total=total)
+    nbytes = _lib.lib().tc_tree_bwd_scratch_bytes(ctypes.byref(args))
+    if nbytes < 0:
+        raise ValueError("tc_tree_bwd_scratch_bytes: invalid arguments")
+    scratch = torch.empty(max(int(nbytes), 1), device=dev, dtype=torch.uint8)
+    args.scratch, args.scratch_bytes = scratch.data_ptr(), int(nbytes)
+    _lib.check(_lib.lib().tc_build_tree_bwd(ctypes.byref(args), _lib.stream_of(k)), "tc_build_tree_bwd")
+    dq_out = torch.zeros_like(q) if dq is None else dq.to(q.dtype)
+    dx = dwp = None
+    if dw0 is not None:
+        # w0 = x @ w_proj^T: two plain GEMMs (cuBLAS through torch, fp32
+        # accumulation) in the inputs' precision, as autograd runs them on
+        # the reference's x @ w_proj^T; dw0 is rounded to that precision first
+        ct = torch.promote_types(x.dtype, w_proj.dtype)
+        g = dw0.to(ct)
+        dx = g.matmul(w_proj.to(ct)).to(x.dtype)
+        dwp = g.reshape(-1, Hkv).t().matmul(x.reshape(-1, x.shape[-1]).to(ct)).to(w_proj.dtype)
+    dkcw = dvcw = None
+    if conv:
+        dk, dkcw = _short_conv_vjp(k, kcw, dk0)
+        dv, dvcw = _short_conv_vjp(v, vcw, dv0)
+    else:
+        dk, dv = dk0.to(k.dtype), dv0.to(v.dtype)
+    return dq_out, dk, dv, dx, dwp, dkcw, dvcw
 
 
 def _short_conv_vjp(x_pre, weight, dy):
@@ -270,4 +315,4 @@ def build_dyadic_summaries(
 
 
 __all__ = ["compute_summary_weights", "compute_linear_weights", "short_conv",
-           "build_dyadic_summaries"]
+           "build_dyadic_summaries", "build_dyadic_summaries_backward"]
