@@ -59,6 +59,8 @@ EMB = 2048
 DECODE = dict(B=64, T=32768, H=16, D=128, levels=8, W=256, conv=4, softcap=20.0,
               desc="BASELINE config 4: decode_step after a 32768-token prefill, rope, conv 4, "
                    "sink, gate")
+# the same decode schedule and features at B=8, for ncu captures (a few GB on the device)
+DECODE_SMALL = dict(DECODE, B=8, desc="config 4 schedule and features at B=8 (profiling case)")
 
 
 # DRAM bytes per launch of the dominant op (the backward: Pass A + Pass B), from
@@ -271,6 +273,54 @@ def decode_visible(spec, t0, n):
             for t in range(t0, t0 + n)]
 
 
+def handoff_bench(T, args, kl, vl, wl, fmap, cache, k_pre, v_pre, conv):
+    """The prefill hand-off at config 4: init_decode_state (one tc_decode_init
+    launch places every ring slot; the conv history is two small copies),
+    W warm-up and K timed public calls with CUDA events.  Its inputs and the
+    2 GB of rings it writes exceed L2, so no flush is needed.  Algorithmic
+    bytes: every ring slot written once (k, v, w) and every live node read
+    once."""
+    import torch
+
+    from telescope_cache_b200 import _lib
+    from telescope_cache_b200 import range_spec as R
+
+    def call():
+        return T.init_decode_state(kl, vl, wl, fmap, cache, k_pre_conv=k_pre, v_pre_conv=v_pre,
+                                   conv_kernel_size=conv)
+
+    for _ in range(max(args.warmup, 1)):
+        st = call()
+    del st
+    torch.cuda.synchronize()
+    cur = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    n0 = _lib.launch_count()
+    for a, b in ev:
+        a.record(cur)
+        st = call()
+        b.record(cur)
+        del st
+    torch.cuda.synchronize()
+    launches = (_lib.launch_count() - n0) // args.steps
+    ms = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
+    B, N, H, Dk = kl[0].shape
+    Dv = vl[0].shape[-1]
+    el, wel = kl[0].element_size(), wl[0].element_size()
+    caps = T.decode_capacities(R.activation_times_from_fmap(fmap), cache)
+    spec = R.RangeSpec.from_fmap(fmap, cache, N)
+    live = sum(hi - lo for lo, hi in (R.range_bounds(spec, N - 1, lv) for lv in range(len(caps))))
+    row = H * ((Dk + Dv) * el + wel)
+    nbytes = B * (sum(caps) + live) * row
+    _, _, hbm, src = peaks()
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    return {"what": "init_decode_state (prefill hand-off: tc_decode_init ring placement + conv history)",
+            "ms": ms, "launches_per_call": launches, "bytes": nbytes, "ring_slots": sum(caps),
+            "live_nodes": live, "achieved_gbs": achieved, "peak_gbs": hbm,
+            "peak_source": f"{src} hbm_gbs", "frac": achieved / hbm}
+
+
 def decode_bench(args, dev, world, with_e2e=True):
     """Config 4: prefill (builder + init_decode_state) untimed, then W warm-up
     and K timed decode_step calls through the public API.  Returns a dict
@@ -282,7 +332,7 @@ def decode_bench(args, dev, world, with_e2e=True):
     import telescope_cache_b200 as T
     from telescope_cache_b200 import range_spec as R
 
-    c = DECODE
+    c = DECODE_SMALL if args.workload == "c4_small" else DECODE
     B, N, H, D = c["B"], c["T"], c["H"], c["D"]
     fmap, cache = {l: l * c["W"] for l in range(1, c["levels"])}, c["levels"] * c["W"]
     bf = torch.bfloat16
@@ -298,6 +348,7 @@ def decode_bench(args, dev, world, with_e2e=True):
     k = torch.randn(B, N, H, D, generator=g, device=dev, dtype=bf)
     v = torch.randn(B, N, H, D, generator=g, device=dev, dtype=bf)
     kl, vl, wl = T.build_dyadic_summaries(q, k, v, c["levels"] - 1, k_conv_weight=kcw, v_conv_weight=vcw)
+    handoff = handoff_bench(T, args, kl, vl, wl, fmap, cache, k, v, c["conv"])
     state = T.init_decode_state(kl, vl, wl, fmap, cache, k_pre_conv=k, v_pre_conv=v,
                                 conv_kernel_size=c["conv"])
     del q, k, v, kl, vl, wl
@@ -339,13 +390,14 @@ def decode_bench(args, dev, world, with_e2e=True):
     gbs = ring_bytes / (ms * 1e-3) / 1e9
     res = {"metric": "decode tokens/s", "value": B * world / (ms * 1e-3), "unit": "tokens/s",
            "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
-           "config": {"workload": "c4", "desc": c["desc"], "B_per_rank": B, "prefill": N, "H": H,
+           "config": {"workload": args.workload if args.workload.startswith("c4") else "c4", "desc": c["desc"], "B_per_rank": B, "prefill": N, "H": H,
                       "D": D, "fmap": fmap, "cache_size": cache, "caps": list(state.caps),
                       "softcap": c["softcap"], "visible_per_step": sum(vis) / len(vis)},
            "roofline": {"bound": "hbm", "kernel": "decode_step (whole public call)",
                         "achieved": gbs, "peak": hbm, "peak_source": f"{src} hbm_gbs", "unit": "GB/s",
                         "frac": gbs / hbm, "algorithmic_bytes_per_step": ring_bytes,
-                        "traffic": None}}
+                        "traffic": None},
+           "handoff": handoff}
     if with_e2e:
         # every step copies its token inputs from pinned host memory and reads
         # its output back; the next step's inputs are copied on a side stream
@@ -505,7 +557,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS) + ["c4"])
+    ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS) + ["c4", "c4_small"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode", action="store_true",
@@ -513,7 +565,7 @@ def main():
     ap.add_argument("--no-vjp", action="store_true",
                     help="skip the Phase-1 VJP measurement added to the line")
     args = ap.parse_args()
-    if args.workload == "c4":
+    if args.workload in ("c4", "c4_small"):
         return decode_main(args)
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":

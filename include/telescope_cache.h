@@ -406,6 +406,35 @@ typedef struct tc_decode_args {
  *  apply_attention_sink + apply_output_gate, reference.py:1948-2317). */
 int tc_decode_step(const tc_decode_args* a, void* stream);
 
+typedef struct tc_decode_init_args {
+  int32_t B, Hkv, Dk, Dv;
+  int32_t dtype;                          /* level / ring k and v element type  */
+  int32_t w_dtype;                        /* level / ring w element type        */
+  int32_t num_levels;
+  int32_t caps[TC_MAX_LEVELS];
+  int32_t ring_off[TC_MAX_LEVELS + 1];
+  int32_t lo[TC_MAX_LEVELS];              /* live range [lo, hi) of query N-1   */
+  int32_t hi[TC_MAX_LEVELS];              /* per level (hi - lo <= caps[l])     */
+  const void* k_lv[TC_MAX_LEVELS];        /* level l keys [B, >= hi, Hkv, Dk]   */
+  const void* v_lv[TC_MAX_LEVELS];        /* level l values [B, >= hi, Hkv, Dv] */
+  const void* w_lv[TC_MAX_LEVELS];        /* level l weights [B, >= hi, Hkv]    */
+  /* batch and token strides of each level tensor, in elements; the
+   * (Hkv, D) block of a token (the Hkv weights for w) is dense. */
+  int64_t k_stride_b[TC_MAX_LEVELS], k_stride_n[TC_MAX_LEVELS];
+  int64_t v_stride_b[TC_MAX_LEVELS], v_stride_n[TC_MAX_LEVELS];
+  int64_t w_stride_b[TC_MAX_LEVELS], w_stride_n[TC_MAX_LEVELS];
+  void* ring_k;                           /* [B, sum(caps), Hkv, Dk] written whole */
+  void* ring_v;                           /* [B, sum(caps), Hkv, Dv]            */
+  void* ring_w;                           /* [B, sum(caps), Hkv]                */
+} tc_decode_init_args;
+
+/* Prefill hand-off on the device: every ring slot of every level receives
+ * the node of that level live at query N-1 that maps to it
+ * (slot = ring_off[l] + j % caps[l]), or zeros when none does, in one launch
+ * (the ring placement of init_decode_state, reference.py:1848-1930; the conv
+ * history rows stay with the caller). */
+int tc_decode_init(const tc_decode_init_args* a, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

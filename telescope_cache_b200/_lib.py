@@ -84,6 +84,19 @@ class DecodeArgs(ctypes.Structure):
     ]
 
 
+class DecodeInitArgs(ctypes.Structure):
+    _fields_ = [
+        ("B", _c_i32), ("Hkv", _c_i32), ("Dk", _c_i32), ("Dv", _c_i32), ("dtype", _c_i32),
+        ("w_dtype", _c_i32), ("num_levels", _c_i32), ("caps", _c_i32 * MAX_LEVELS),
+        ("ring_off", _c_i32 * (MAX_LEVELS + 1)), ("lo", _c_i32 * MAX_LEVELS),
+        ("hi", _c_i32 * MAX_LEVELS), ("k_lv", _c_vp * MAX_LEVELS), ("v_lv", _c_vp * MAX_LEVELS),
+        ("w_lv", _c_vp * MAX_LEVELS), ("k_stride_b", _c_i64 * MAX_LEVELS),
+        ("k_stride_n", _c_i64 * MAX_LEVELS), ("v_stride_b", _c_i64 * MAX_LEVELS),
+        ("v_stride_n", _c_i64 * MAX_LEVELS), ("w_stride_b", _c_i64 * MAX_LEVELS),
+        ("w_stride_n", _c_i64 * MAX_LEVELS), ("ring_k", _c_vp), ("ring_v", _c_vp), ("ring_w", _c_vp),
+    ]
+
+
 # (name, argtypes) of every exported symbol; the CPU test checks that each one
 # exists and that this list matches include/telescope_cache.h.
 SIGNATURES = {
@@ -115,6 +128,7 @@ SIGNATURES = {
                     _c_vp, _c_vp, _c_vp],
     "tc_gate_apply": [_c_i64, _c_i32, _c_vp, _c_i32, _c_vp, _c_i32, _c_vp, _c_vp],
     "tc_decode_step": [ctypes.POINTER(DecodeArgs), _c_vp],
+    "tc_decode_init": [ctypes.POINTER(DecodeInitArgs), _c_vp],
 }
 
 _LIB = None

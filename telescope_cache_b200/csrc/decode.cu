@@ -796,3 +796,110 @@ extern "C" int tc_decode_step(const tc_decode_args* a, void* stream) {
   TC_DISPATCH(a->dtype, T, { return launch_decode<T>(P, E, d, grid, st); });
   return TC_ERR_ARG;
 }
+
+// ---------------------------------------------------------------------------
+// Prefill hand-off (the ring placement of init_decode_state,
+// reference.py:1848-1930).  One warp per (batch row, ring slot): it finds the
+// slot's level, the one node j in [lo, hi) with j % cap == slot - ring_off[l]
+// (hi - lo <= cap, so at most one), and copies that node's [Hkv, D] key and
+// value rows and its Hkv weights, or writes zeros.  The whole ring is written,
+// so the caller allocates it uninitialised.  V is the widest vector type that
+// every row pointer, stride and row size of the call is aligned to.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kInitWarps = 8;
+
+template <typename V>
+__device__ __forceinline__ void init_copy_row(V* __restrict__ dst, const V* __restrict__ src, int n,
+                                              int lane) {
+  constexpr int U = 8;  // loads in flight per lane before the stores
+  for (int base = 0; base < n; base += 32 * U) {
+    V r[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * 32 + lane;
+      if (i < n) r[u] = src ? __ldg(src + i) : V{};
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * 32 + lane;
+      if (i < n) dst[i] = r[u];
+    }
+  }
+}
+
+template <typename V>
+__global__ void __launch_bounds__(32 * kInitWarps) decode_init_kernel(tc_decode_init_args a, int total,
+                                                                      int es, int w_es) {
+  const int lane = threadIdx.x & 31;
+  const int s = blockIdx.x * kInitWarps + (threadIdx.x >> 5);
+  const int b = blockIdx.y;
+  if (s >= total) return;
+  int l = 0;
+  while (l + 1 < a.num_levels && s >= a.ring_off[l + 1]) ++l;
+  const int cap = a.caps[l], r = s - a.ring_off[l], lo = a.lo[l], hi = a.hi[l];
+  int64_t j = -1;
+  if (lo < hi) {
+    const int jj = lo + ((r - lo % cap) % cap + cap) % cap;
+    if (jj < hi) j = jj;
+  }
+  const int64_t row = (int64_t)b * total + s;
+  const int kb = a.Hkv * a.Dk * es, vb = a.Hkv * a.Dv * es;
+  const char* ks = j < 0 ? nullptr
+                         : (const char*)a.k_lv[l] + ((int64_t)b * a.k_stride_b[l] + j * a.k_stride_n[l]) * es;
+  const char* vs = j < 0 ? nullptr
+                         : (const char*)a.v_lv[l] + ((int64_t)b * a.v_stride_b[l] + j * a.v_stride_n[l]) * es;
+  init_copy_row<V>((V*)((char*)a.ring_k + row * kb), (const V*)ks, kb / (int)sizeof(V), lane);
+  init_copy_row<V>((V*)((char*)a.ring_v + row * vb), (const V*)vs, vb / (int)sizeof(V), lane);
+  const char* ws = j < 0 ? nullptr
+                         : (const char*)a.w_lv[l] + ((int64_t)b * a.w_stride_b[l] + j * a.w_stride_n[l]) * w_es;
+  char* wd = (char*)a.ring_w + row * a.Hkv * w_es;
+  for (int h = lane; h < a.Hkv; h += 32) {
+    if (w_es == 4) ((uint32_t*)wd)[h] = ws ? __ldg((const uint32_t*)ws + h) : 0u;
+    else ((uint16_t*)wd)[h] = ws ? __ldg((const unsigned short*)ws + h) : (uint16_t)0;
+  }
+}
+
+inline bool init_aligned(int vb, const tc_decode_init_args& a, int es) {
+  auto ok = [vb](uint64_t x) { return x % (uint64_t)vb == 0; };
+  if (!ok((uintptr_t)a.ring_k) || !ok((uintptr_t)a.ring_v) || !ok((uint64_t)a.Hkv * a.Dk * es) ||
+      !ok((uint64_t)a.Hkv * a.Dv * es))
+    return false;
+  for (int l = 0; l < a.num_levels; ++l) {
+    if (a.lo[l] >= a.hi[l]) continue;
+    if (!ok((uintptr_t)a.k_lv[l]) || !ok((uintptr_t)a.v_lv[l]) || !ok((uint64_t)a.k_stride_b[l] * es) ||
+        !ok((uint64_t)a.k_stride_n[l] * es) || !ok((uint64_t)a.v_stride_b[l] * es) ||
+        !ok((uint64_t)a.v_stride_n[l] * es))
+      return false;
+  }
+  return true;
+}
+
+}  // namespace
+
+extern "C" int tc_decode_init(const tc_decode_init_args* a, void* stream) {
+  if (!a || a->B <= 0 || a->B > 65535 || a->Hkv <= 0 || a->Dk <= 0 || a->Dv <= 0 || a->num_levels < 1 ||
+      a->num_levels > TC_MAX_LEVELS || !a->ring_k || !a->ring_v || !a->ring_w)
+    return TC_ERR_ARG;
+  if (a->dtype < TC_F32 || a->dtype > TC_F16 || a->w_dtype < TC_F32 || a->w_dtype > TC_F16) return TC_ERR_ARG;
+  if (a->ring_off[0] != 0) return TC_ERR_ARG;
+  for (int l = 0; l < a->num_levels; ++l) {
+    if (a->caps[l] <= 0 || a->ring_off[l + 1] != a->ring_off[l] + a->caps[l]) return TC_ERR_ARG;
+    if (a->lo[l] < 0 || a->hi[l] < a->lo[l] || a->hi[l] - a->lo[l] > a->caps[l]) return TC_ERR_ARG;
+    if (a->lo[l] < a->hi[l] && (!a->k_lv[l] || !a->v_lv[l] || !a->w_lv[l])) return TC_ERR_ARG;
+  }
+  const int total = a->ring_off[a->num_levels];
+  const int es = dtype_size(a->dtype), w_es = dtype_size(a->w_dtype);
+  const dim3 grid((total + kInitWarps - 1) / kInitWarps, a->B);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (init_aligned(16, *a, es))
+    decode_init_kernel<uint4><<<grid, 32 * kInitWarps, 0, st>>>(*a, total, es, w_es);
+  else if (init_aligned(4, *a, es))
+    decode_init_kernel<uint32_t><<<grid, 32 * kInitWarps, 0, st>>>(*a, total, es, w_es);
+  else if (init_aligned(2, *a, es))
+    decode_init_kernel<unsigned short><<<grid, 32 * kInitWarps, 0, st>>>(*a, total, es, w_es);
+  else
+    return TC_ERR_ARG;
+  return launch_status();
+}

@@ -93,8 +93,16 @@ def ring_slot(state: DecodeState, level: int, j: int) -> int:
     return state.ring_offsets[level] + j % state.caps[level]
 
 
-def _ring_slots(state: DecodeState, level: int, indices: torch.Tensor) -> torch.Tensor:
-    return state.ring_offsets[level] + torch.remainder(indices, state.caps[level])
+def _dense_rows(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """t [B, n, ...] in `dtype` with every token's trailing block dense (the
+    layout tc_decode_init copies rows from); batch and token strides stay free."""
+    t = t.to(dtype)
+    want = 1
+    for size, stride in zip(reversed(t.shape[2:]), reversed(t.stride()[2:])):
+        if size != 1 and stride != want:
+            return t.contiguous()
+        want *= size
+    return t
 
 
 def _conv_history(x_pre: torch.Tensor, kernel_size: int) -> torch.Tensor:
@@ -159,23 +167,47 @@ def init_decode_state(
         offs.append(offs[-1] + c)
     total = offs[-1]
     dev = k_levels[0].device
+    _lib.require_cuda(*k_levels[:L + 1], *v_levels[:L + 1], *w_levels[:L + 1])
+    kdt, vdt, wdt = k_levels[0].dtype, v_levels[0].dtype, w_levels[0].dtype
+    if kdt != vdt:
+        raise NotImplementedError(f"key and value levels must share a dtype ({kdt} vs {vdt})")
+    if L + 1 > _lib.MAX_LEVELS:
+        raise NotImplementedError(f"at most {_lib.MAX_LEVELS} levels are supported")
+    # every slot is written by tc_decode_init (live node or zeros)
     state = DecodeState(
-        k=torch.zeros(B, total, Hkv, Dk, device=dev, dtype=k_levels[0].dtype),
-        v=torch.zeros(B, total, Hkv, Dv, device=dev, dtype=v_levels[0].dtype),
-        w=torch.zeros(B, total, Hkv, 1, device=dev, dtype=w_levels[0].dtype),
+        k=torch.empty(B, total, Hkv, Dk, device=dev, dtype=kdt),
+        v=torch.empty(B, total, Hkv, Dv, device=dev, dtype=vdt),
+        w=torch.empty(B, total, Hkv, 1, device=dev, dtype=wdt),
         conv_k=None, conv_v=None, t=N, activation_times=a, cache_size=cache_size, caps=caps,
         ring_offsets=tuple(offs))
     spec = RangeSpec(a, cache_size, N)
+    args = _lib.DecodeInitArgs()
+    args.B, args.Hkv, args.Dk, args.Dv = B, Hkv, Dk, Dv
+    args.dtype, args.w_dtype = _lib.dtype_code(kdt), _lib.dtype_code(wdt)
+    args.num_levels = L + 1
+    args.ring_off[0] = 0
+    keep = []  # level tensors converted for the kernel stay alive until the launch
     for level in range(L + 1):
         lo, hi = range_bounds(spec, N - 1, level)
+        args.caps[level] = caps[level]
+        args.ring_off[level + 1] = offs[level + 1]
+        args.lo[level], args.hi[level] = lo, hi
         if lo == hi:
             continue
         if hi > k_levels[level].shape[1] or hi > v_levels[level].shape[1] or hi > w_levels[level].shape[1]:
             raise ValueError(f"level {level}: live range [{lo},{hi}) exceeds the given level tensors")
-        slots = _ring_slots(state, level, torch.arange(lo, hi, device=dev, dtype=torch.long))
-        state.k[:, slots] = k_levels[level][:, lo:hi]
-        state.v[:, slots] = v_levels[level][:, lo:hi]
-        state.w[:, slots] = w_levels[level][:, lo:hi]
+        if hi - lo > caps[level]:
+            raise AssertionError(f"level {level} has {hi - lo} live nodes > cap {caps[level]} at q={N - 1}")
+        kl, vl = _dense_rows(k_levels[level], kdt), _dense_rows(v_levels[level], vdt)
+        wl = _dense_rows(w_levels[level].squeeze(-1), wdt)
+        keep += [kl, vl, wl]
+        args.k_lv[level], args.v_lv[level], args.w_lv[level] = kl.data_ptr(), vl.data_ptr(), wl.data_ptr()
+        args.k_stride_b[level], args.k_stride_n[level] = kl.stride(0), kl.stride(1)
+        args.v_stride_b[level], args.v_stride_n[level] = vl.stride(0), vl.stride(1)
+        args.w_stride_b[level], args.w_stride_n[level] = wl.stride(0), wl.stride(1)
+    args.ring_k, args.ring_v, args.ring_w = state.k.data_ptr(), state.v.data_ptr(), state.w.data_ptr()
+    _lib.check(_lib.lib().tc_decode_init(ctypes.byref(args), _lib.stream_of(state.k)), "tc_decode_init")
+    del keep
     if k_pre_conv is not None:
         if conv_kernel_size <= 0:
             raise ValueError(f"conv kernel size must be positive, got {conv_kernel_size}")

@@ -31,11 +31,18 @@ def test_library_loads_and_exports_every_declared_symbol():
 def test_struct_sizes_match_header():
     # tc_schedule: 4 int32 + 2 * 16 int32 + 17 int64
     assert ctypes.sizeof(_lib.Schedule) == 4 * 4 + 2 * 16 * 4 + 17 * 8
+    # tc_decode_init_args: 7 int32, caps, ring_off, lo, hi; 3 x 16 level pointers,
+    # 6 x 16 int64 strides, 3 ring pointers
+    assert ctypes.sizeof(_lib.DecodeInitArgs) == 7 * 4 + 16 * 4 + 17 * 4 + 2 * 16 * 4 + 3 * 16 * 8 + \
+        6 * 16 * 8 + 3 * 8
+    assert _lib.DecodeInitArgs.ring_k.offset == 1440
 
 
 def test_bad_arguments_return_status_codes():
     lib = _lib.lib()
     assert lib.tc_schedule_init(None, 2, 6, 8, None) == _lib.TC_ERR_ARG
+    # no ring pointers: rejected before any launch
+    assert lib.tc_decode_init(ctypes.byref(_lib.DecodeInitArgs()), None) == _lib.TC_ERR_ARG
     vals = (ctypes.c_int32 * 1)(3)  # a[1] = 4: wrong phase
     s = _lib.Schedule()
     assert lib.tc_schedule_init(ctypes.cast(vals, ctypes.c_void_p), 1, 6, 8, ctypes.byref(s)) == \
