@@ -111,8 +111,13 @@ def _conv_history(x_pre: torch.Tensor, kernel_size: int) -> torch.Tensor:
     hist = kernel_size - 1
     if hist == 0:
         return x_pre[:, :0].clone()
-    pad = max(hist - x_pre.shape[1], 0)
-    return torch.nn.functional.pad(x_pre, (0, 0, pad, 0))[:, -hist:].contiguous()
+    # slice before padding: only the last K-1 rows are copied, not the prefill
+    tail = x_pre[:, -hist:]
+    pad = hist - tail.shape[1]
+    if pad > 0:
+        return torch.nn.functional.pad(tail, (0, 0, pad, 0)).contiguous()
+    # a copy, never a view: decode steps update the history in place
+    return tail.clone(memory_format=torch.contiguous_format)
 
 
 def short_conv_step(x: torch.Tensor, state: torch.Tensor, weight: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
