@@ -1,0 +1,55 @@
+"""Host-side index arithmetic of the prefill hand-off (tc_decode_init): for
+every schedule and a spread of prefill lengths, the live ranges the wrapper
+passes (range_bounds of query N-1) equal the oracle's, each level's live
+count fits its ring, and the kernel's slot -> node rule (the one node j in
+[lo, hi) with j mod cap = slot - ring_off[l]) reproduces the oracle's
+placement (node j at ring_off[l] + j mod cap, reference.py:1900-1930) slot for
+slot.  The kernel itself is checked on the GPU in test_gpu_decode_init.py."""
+
+import pytest
+
+import cases as C
+from oracle import schedule as S
+from telescope_cache_b200.range_spec import RangeSpec, range_bounds
+
+
+def kernel_rule(slot, offs, caps, lo, hi):
+    """decode_init_kernel's mapping, restated: (level, node) or (level, None)."""
+    l = 0
+    while l + 1 < len(caps) and slot >= offs[l + 1]:
+        l += 1
+    cap, r = caps[l], slot - offs[l]
+    if lo[l] < hi[l]:
+        j = lo[l] + ((r - lo[l] % cap) % cap + cap) % cap
+        if j < hi[l]:
+            return l, j
+    return l, None
+
+
+@pytest.mark.parametrize("sched", [s[0] for s in C.SCHEDULES])
+def test_slot_rule_matches_oracle_placement(sched):
+    _, n_max, cache, fmap = next(s for s in C.SCHEDULES if s[0] == sched)
+    a = S.activation_times(fmap)
+    caps = S.decode_caps(a, cache)
+    offs = S.ring_offsets(caps)
+    lens = sorted({1, 2, 3, 7, max(a) + 1, n_max // 3, n_max // 2 + 5, n_max - 1, n_max} - {0})
+    for n in (x for x in lens if 1 <= x <= n_max):
+        rr = S.row_ranges(n - 1, a, cache)
+        spec = RangeSpec(a, cache, n)
+        lo, hi = [], []
+        for lv in range(len(a)):
+            got = range_bounds(spec, n - 1, lv)
+            want = rr[lv] if rr[lv][0] < rr[lv][1] else (0, 0)
+            assert tuple(got) == tuple(want), (sched, n, lv)
+            assert got[1] - got[0] <= caps[lv], (sched, n, lv)
+            lo.append(got[0])
+            hi.append(got[1])
+        placed = {}
+        for lv in range(len(a)):
+            for j in range(lo[lv], hi[lv]):
+                s = S.ring_slot(offs, caps, lv, j)
+                assert s not in placed, (sched, n, lv, j)
+                placed[s] = (lv, j)
+        for s in range(offs[-1]):
+            lv, j = kernel_rule(s, offs, caps, lo, hi)
+            assert placed.get(s, (lv, None)) == (lv, j), (sched, n, s)
