@@ -53,3 +53,16 @@ def test_slot_rule_matches_oracle_placement(sched):
         for s in range(offs[-1]):
             lv, j = kernel_rule(s, offs, caps, lo, hi)
             assert placed.get(s, (lv, None)) == (lv, j), (sched, n, s)
+
+
+def test_cpu_levels_raise_no_fallback():
+    """The hand-off computes on CUDA tensors only: CPU level tensors raise
+    before any launch instead of taking a CPU path."""
+    import torch
+
+    import telescope_cache_b200 as T
+    n, fmap, cache = 40, {1: 8, 2: 16, 3: 24}, 32
+    kl = [torch.zeros(1, n >> l, 2, 8) for l in range(4)]
+    wl = [torch.zeros(1, n >> l, 2, 1) for l in range(4)]
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        T.init_decode_state(kl, kl, wl, fmap, cache)
