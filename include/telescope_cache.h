@@ -304,9 +304,10 @@ int tc_attn_bwd(const tc_attn_args* a, const tc_schedule* s, void* stream);
  * for this C ABI.  Same arguments as tc_attn_bwd except that a->delta is
  * ignored: the Delta scratch lives in a fixed 2^22-float (16 MiB) device array
  * inside the library, held by every GPU that loads it, so B * N * Hq must be
- * <= 4194304 (else TC_ERR_SCRATCH_LIMIT).  Nothing is allocated.  The first
- * call on a device looks up the array's address (call it before any stream
- * capture); calls that overlap on the GPU share the array and race. */
+ * <= 4194304 (else TC_ERR_SCRATCH_LIMIT).  Nothing is allocated.  Every call
+ * looks up the array's address on the current device; the first call on a
+ * device also loads the library there (make it before any stream capture).
+ * Calls that overlap on the GPU share the array and race. */
 int tc_attn_bwd_noalloc(const tc_attn_args* a, const tc_schedule* s, void* stream);
 
 /* Failure-detection self-test (no reference counterpart): one kernel waits on

@@ -173,6 +173,20 @@ def check(rc, what):
         raise exc(f"telescope_cache_b200: {what} failed with status {rc}")
 
 
+def launch(name, device, *args):
+    """Call the entry point `name` with `device` current, so that its kernels
+    launch on the device that owns the tensors and their stream whatever device
+    the caller has current (the caller's current device is restored).  Raises
+    on a nonzero status."""
+    fn = getattr(lib(), name)
+    if device is not None and device.type == "cuda" and device.index != torch.cuda.current_device():
+        with torch.cuda.device(device):
+            rc = fn(*args)
+    else:
+        rc = fn(*args)
+    check(rc, name)
+
+
 def dtype_code(dt):
     if dt == torch.float32:
         return TC_F32

@@ -1,8 +1,6 @@
 // C-ABI entry points of the Phase-2 attention: argument checks and the choice
 // between the tensor-core kernels (bf16/f16, Dk = Dv = 128) and the SIMT
 // kernels (every other shape and the fp32 parity mode).
-#include <mutex>
-
 #include "attn_common.cuh"
 
 namespace tc {
@@ -87,33 +85,24 @@ extern "C" int tc_attn_bwd(const tc_attn_args* a, const tc_schedule* s, void* st
 // The array holds kNoAllocMaxRows floats (16 MiB).  It is part of this
 // library's device image, so every GPU that loads the library holds it until
 // the process exits.  Host code cannot use the array's name as a device
-// address; the first call on each device looks the address up with
-// cudaGetSymbolAddress while that device is current, caches it, and passes it
-// to the kernels.  That first call therefore does one-time set-up and should
-// come before any stream capture.  Every call shares the one array: Delta is
-// fully rewritten by each call before it is read, and calls that overlap on
-// the GPU (on different streams) race on it.
+// address: every call looks the address up with cudaGetSymbolAddress while
+// the caller's device is current and passes it to the kernels.  The first
+// call on a device loads the library's module there (one-time set-up), so it
+// should come before any stream capture; later look-ups are plain queries,
+// and a device reset followed by a reload yields the new address.  Every call
+// shares the one array: Delta is fully rewritten by each call before it is
+// read, and calls that overlap on the GPU (on different streams) race on it.
 // ---------------------------------------------------------------------------
 namespace {
 
 constexpr int64_t kNoAllocMaxRows = int64_t(1) << 22;
-constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) float g_noalloc_delta[kNoAllocMaxRows];
 
-std::mutex g_noalloc_mu;
-float* g_noalloc_delta_addr[kNoAllocMaxDevices] = {};
-
 int noalloc_delta(float** out) {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return TC_ERR_CUDA;
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_delta_addr[dev]) {
-    void* addr = nullptr;
-    if (cudaGetSymbolAddress(&addr, g_noalloc_delta) != cudaSuccess || !addr) return TC_ERR_CUDA;
-    g_noalloc_delta_addr[dev] = static_cast<float*>(addr);
-  }
-  *out = g_noalloc_delta_addr[dev];
+  void* addr = nullptr;
+  if (cudaGetSymbolAddress(&addr, g_noalloc_delta) != cudaSuccess || !addr) return TC_ERR_CUDA;
+  *out = static_cast<float*>(addr);
   return TC_OK;
 }
 

@@ -23,6 +23,9 @@
 #include "tc_common.cuh"
 
 namespace tc {
+
+int attn_fwd_fa(const AttnParams& a, int dtype, cudaStream_t st);
+
 namespace {
 
 using namespace ptx;
@@ -428,6 +431,7 @@ int launch_fwd(const AttnParams& a, int dtype, cudaStream_t st) {
 template <typename T, bool CAP>
 int fwd_dispatch(const AttnParams& a, int dtype, cudaStream_t st) {
   if (a.pos_mode == TC_POS_RELATIVE) return launch_fwd<T, 64, true, CAP>(a, dtype, st);
+  if (a.tile_n == 0) return attn_fwd_fa(a, dtype, st);
   if (a.tile_n == 64) return launch_fwd<T, 64, false, CAP>(a, dtype, st);
   return launch_fwd<T, 128, false, CAP>(a, dtype, st);
 }

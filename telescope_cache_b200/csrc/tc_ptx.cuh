@@ -135,6 +135,18 @@ __device__ __forceinline__ bool named_bar_and(int id, int n, bool v) {
   return r != 0;
 }
 
+// Per-warpgroup register budgets (every warp of a warpgroup executes the same
+// one).  The block's launch total (threads x registers at launch) bounds the
+// sum of the budgets after the change.
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---------------------------------------------------------------------------
 // tcgen05
 // ---------------------------------------------------------------------------

@@ -178,8 +178,7 @@ def _forward(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope
     args.out = out.data_ptr()
     args.lse = lse.data_ptr()
     args.impl = _impl_code(impl)
-    _lib.check(_lib.lib().tc_attn_fwd(ctypes.byref(args), ctypes.byref(sched), _lib.stream_of(q)),
-               "tc_attn_fwd")
+    _lib.launch("tc_attn_fwd", q.device, ctypes.byref(args), ctypes.byref(sched), _lib.stream_of(q))
     band = getattr(args, "_band", None)
     if band is not None:
         _keep_band(lse, relative_states, relative_proj, band[0], dims[-1], band[1], band[2])
@@ -333,8 +332,7 @@ def multilevel_attention_backward(
     args.dv = dv.data_ptr()
     args.drel = None if drel is None else drel.data_ptr()
     args.impl = _impl_code(impl)
-    _lib.check(_lib.lib().tc_attn_bwd(ctypes.byref(args), ctypes.byref(sched), _lib.stream_of(q)),
-               "tc_attn_bwd")
+    _lib.launch("tc_attn_bwd", q.device, ctypes.byref(args), ctypes.byref(sched), _lib.stream_of(q))
     del keep
     stats = {"softcap_used": softcap is not None, "kernel": "cuda"}
     return (dq.to(q.dtype), dk.to(packed.k.dtype), dv.to(packed.v.dtype), drel, stats)

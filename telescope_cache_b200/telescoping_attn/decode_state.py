@@ -172,6 +172,18 @@ def init_decode_state(
         offs.append(offs[-1] + c)
     total = offs[-1]
     dev = k_levels[0].device
+    # the kernel copies (Hkv, D) rows of B batch rows from every level with live
+    # nodes: their batch and trailing sizes must match level 0's
+    spec = RangeSpec(a, cache_size, N)
+    for level in range(L + 1):
+        lo, hi = range_bounds(spec, N - 1, level)
+        if lo == hi:
+            continue
+        for name, t, tail in (("k_levels", k_levels[level], (Hkv, Dk)), ("v_levels", v_levels[level], (Hkv, Dv)),
+                              ("w_levels", w_levels[level], (Hkv, 1))):
+            if t.dim() != 4 or t.shape[0] != B or tuple(t.shape[2:]) != tail:
+                raise ValueError(
+                    f"{name}[{level}] shape {tuple(t.shape)} != [{B}, n, {tail[0]}, {tail[1]}]")
     _lib.require_cuda(*k_levels[:L + 1], *v_levels[:L + 1], *w_levels[:L + 1])
     kdt, vdt, wdt = k_levels[0].dtype, v_levels[0].dtype, w_levels[0].dtype
     if kdt != vdt:
@@ -185,7 +197,6 @@ def init_decode_state(
         w=torch.empty(B, total, Hkv, 1, device=dev, dtype=wdt),
         conv_k=None, conv_v=None, t=N, activation_times=a, cache_size=cache_size, caps=caps,
         ring_offsets=tuple(offs))
-    spec = RangeSpec(a, cache_size, N)
     args = _lib.DecodeInitArgs()
     args.B, args.Hkv, args.Dk, args.Dv = B, Hkv, Dk, Dv
     args.dtype, args.w_dtype = _lib.dtype_code(kdt), _lib.dtype_code(wdt)
@@ -211,7 +222,7 @@ def init_decode_state(
         args.v_stride_b[level], args.v_stride_n[level] = vl.stride(0), vl.stride(1)
         args.w_stride_b[level], args.w_stride_n[level] = wl.stride(0), wl.stride(1)
     args.ring_k, args.ring_v, args.ring_w = state.k.data_ptr(), state.v.data_ptr(), state.w.data_ptr()
-    _lib.check(_lib.lib().tc_decode_init(ctypes.byref(args), _lib.stream_of(state.k)), "tc_decode_init")
+    _lib.launch("tc_decode_init", state.k.device, ctypes.byref(args), _lib.stream_of(state.k))
     del keep
     if k_pre_conv is not None:
         if conv_kernel_size <= 0:
@@ -352,7 +363,7 @@ def _decode_launch(state: DecodeState, mode, q_t, k_t=None, v_t=None, w_t=None, 
         gate_dtype=_lib.dtype_code(gate_pre.dtype) if gate_pre is not None else 0,
         out=out.data_ptr(), lse=lse.data_ptr(), k_new=p(k_new), v_new=p(v_new),
         workspace=p(ws), workspace_floats=0 if ws is None else ws.numel(), ring_k_rot=p(k_rot))
-    _lib.check(_lib.lib().tc_decode_step(ctypes.byref(args), _lib.stream_of(q_t)), "tc_decode_step")
+    _lib.launch("tc_decode_step", q_t.device, ctypes.byref(args), _lib.stream_of(q_t))
     del keep
     return out, lse, k_new, v_new
 

@@ -38,10 +38,10 @@ def _rope_into(x, y, cos, sin, kind, sched=None, positions=None, inverse=False):
     B, S, H, D = x.shape
     cos = cos if cos.dtype == torch.float32 and cos.is_contiguous() else cos.float().contiguous()
     sin = sin if sin.dtype == torch.float32 and sin.is_contiguous() else sin.float().contiguous()
-    _lib.check(_lib.lib().tc_rope_apply(
+    _lib.launch("tc_rope_apply", x.device,
         B, S, H, D, _lib.dtype_code(x.dtype), _lib.ptr(x), _lib.ptr(y), _lib.ptr(cos), _lib.ptr(sin),
         cos.shape[0], kind, None if sched is None else ctypes.byref(sched),
-        _lib.ptr(positions), 1 if inverse else 0, _lib.stream_of(x)), "tc_rope_apply")
+        _lib.ptr(positions), 1 if inverse else 0, _lib.stream_of(x))
     return y
 
 

@@ -15,9 +15,9 @@ def _sink_fwd(out, lse, sinks):
     out_c, lse_c = out.contiguous(), lse.contiguous().float()
     s = sinks.contiguous()
     y = torch.empty_like(out_c)
-    _lib.check(_lib.lib().tc_sink_fwd(B * N, Hq, Dv, _lib.dtype_code(out.dtype), _lib.ptr(out_c),
+    _lib.launch("tc_sink_fwd", out.device, B * N, Hq, Dv, _lib.dtype_code(out.dtype), _lib.ptr(out_c),
                                       _lib.ptr(lse_c), _lib.dtype_code(s.dtype), _lib.ptr(s),
-                                      _lib.ptr(y), _lib.stream_of(out)), "tc_sink_fwd")
+                                      _lib.ptr(y), _lib.stream_of(out))
     return y
 
 
@@ -28,10 +28,10 @@ def _sink_bwd(out, lse, sinks, dout):
     dout_pre = torch.empty_like(g)
     dlse = torch.empty(B, N, Hq, device=out.device, dtype=torch.float32)
     dsinks = torch.empty(Hq, device=out.device, dtype=torch.float32)
-    _lib.check(_lib.lib().tc_sink_bwd(B * N, Hq, Dv, _lib.dtype_code(out.dtype), _lib.ptr(out_c),
+    _lib.launch("tc_sink_bwd", out.device, B * N, Hq, Dv, _lib.dtype_code(out.dtype), _lib.ptr(out_c),
                                       _lib.ptr(lse_c), _lib.dtype_code(s.dtype), _lib.ptr(s),
                                       _lib.ptr(g), _lib.ptr(dout_pre), _lib.ptr(dlse),
-                                      _lib.ptr(dsinks), _lib.stream_of(out)), "tc_sink_bwd")
+                                      _lib.ptr(dsinks), _lib.stream_of(out))
     return dout_pre, dlse, dsinks.to(sinks.dtype)
 
 
@@ -83,10 +83,9 @@ def attention_sink_backward(out: torch.Tensor, lse: torch.Tensor, sinks: torch.T
 def _gate_fwd(out, g):
     y = torch.empty(out.shape, device=out.device, dtype=torch.result_type(out, g))
     oc, gc = out.contiguous(), g.contiguous()
-    _lib.check(_lib.lib().tc_gate_apply(out.numel(), _lib.dtype_code(out.dtype), _lib.ptr(oc),
+    _lib.launch("tc_gate_apply", out.device, out.numel(), _lib.dtype_code(out.dtype), _lib.ptr(oc),
                                         _lib.dtype_code(g.dtype), _lib.ptr(gc),
-                                        _lib.dtype_code(y.dtype), _lib.ptr(y), _lib.stream_of(out)),
-               "tc_gate_apply")
+                                        _lib.dtype_code(y.dtype), _lib.ptr(y), _lib.stream_of(out))
     return y
 
 

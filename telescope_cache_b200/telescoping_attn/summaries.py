@@ -38,9 +38,9 @@ def compute_summary_weights(q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
     _lib.require_cuda(q, k)
     q, k = _contig(q), _contig(k.to(q.dtype))
     out = torch.empty(B, N, Hkv, 1, device=q.device, dtype=q.dtype)
-    _lib.check(_lib.lib().tc_qk_weights(B, N, Hq, Hkv, Dk, _lib.dtype_code(q.dtype), _lib.ptr(q),
+    _lib.launch("tc_qk_weights", q.device, B, N, Hq, Hkv, Dk, _lib.dtype_code(q.dtype), _lib.ptr(q),
                                         _lib.ptr(k), _lib.dtype_code(out.dtype), _lib.ptr(out),
-                                        _lib.stream_of(q)), "tc_qk_weights")
+                                        _lib.stream_of(q))
     return out
 
 
@@ -56,10 +56,9 @@ def compute_linear_weights(x: torch.Tensor, w_proj: torch.Tensor) -> torch.Tenso
         return x.matmul(w_proj.t()).unsqueeze(-1)
     x, w_proj = _contig(x), _contig(w_proj)
     out = torch.empty(B, N, Hkv, 1, device=x.device, dtype=torch.result_type(x, w_proj))
-    _lib.check(_lib.lib().tc_linear_weights(
+    _lib.launch("tc_linear_weights", x.device,
         B * N, E, Hkv, _lib.dtype_code(x.dtype), _lib.ptr(x), _lib.dtype_code(w_proj.dtype),
-        _lib.ptr(w_proj), _lib.dtype_code(out.dtype), _lib.ptr(out), _lib.stream_of(x)),
-        "tc_linear_weights")
+        _lib.ptr(w_proj), _lib.dtype_code(out.dtype), _lib.ptr(out), _lib.stream_of(x))
     return out
 
 
@@ -80,10 +79,9 @@ def short_conv(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     _lib.require_cuda(x, weight)
     x, weight = _contig(x), _contig(weight)
     y = torch.empty_like(x)
-    _lib.check(_lib.lib().tc_short_conv(B, N, C, _lib.dtype_code(x.dtype), _lib.ptr(x),
+    _lib.launch("tc_short_conv", x.device, B, N, C, _lib.dtype_code(x.dtype), _lib.ptr(x),
                                         weight.shape[1], _lib.dtype_code(weight.dtype),
-                                        _lib.ptr(weight), _lib.ptr(y), _lib.stream_of(x)),
-               "tc_short_conv")
+                                        _lib.ptr(weight), _lib.ptr(y), _lib.stream_of(x))
     return y
 
 
@@ -145,7 +143,7 @@ def _build_packed(q, k, v, num_summary_levels, x, w_proj, k_conv_weight, v_conv_
             v_conv_w=None if vcw is None else vcw.data_ptr(),
             conv_dtype=_lib.dtype_code(kcw.dtype) if conv_k else 0, conv_k=conv_k,
             k_packed=kp.data_ptr(), v_packed=vp.data_ptr(), w_packed=wp.data_ptr(), total=total)
-        _lib.check(_lib.lib().tc_build_tree(ctypes.byref(args), _lib.stream_of(k)), "tc_build_tree")
+        _lib.launch("tc_build_tree", k.device, ctypes.byref(args), _lib.stream_of(k))
     return kp, vp, wp, offs
 
 
@@ -227,7 +225,7 @@ def build_dyadic_summaries_backward(q, k, v, num_summary_levels, k_packed, v_pac
         raise ValueError("tc_tree_bwd_scratch_bytes: invalid arguments")
     scratch = torch.empty(max(int(nbytes), 1), device=dev, dtype=torch.uint8)
     args.scratch, args.scratch_bytes = scratch.data_ptr(), int(nbytes)
-    _lib.check(_lib.lib().tc_build_tree_bwd(ctypes.byref(args), _lib.stream_of(k)), "tc_build_tree_bwd")
+    _lib.launch("tc_build_tree_bwd", k.device, ctypes.byref(args), _lib.stream_of(k))
     dq_out = torch.zeros_like(q) if dq is None else dq.to(q.dtype)
     dx = dwp = None
     if dw0 is not None:
@@ -258,10 +256,9 @@ def _short_conv_vjp(x_pre, weight, dy):
     dx = torch.empty_like(xc)
     dw = torch.empty(C, K, device=x_pre.device, dtype=torch.float32)
     parts = torch.empty(max(1, B * ((N + 255) // 256) * C * K), device=x_pre.device, dtype=torch.float32)
-    _lib.check(_lib.lib().tc_short_conv_bwd(
+    _lib.launch("tc_short_conv_bwd", x_pre.device,
         B, N, C, _lib.dtype_code(xc.dtype), _lib.ptr(xc), K, _lib.dtype_code(wc.dtype), _lib.ptr(wc),
-        _lib.ptr(dy), _lib.ptr(dx), _lib.ptr(dw), _lib.ptr(parts), parts.numel(), _lib.stream_of(xc)),
-        "tc_short_conv_bwd")
+        _lib.ptr(dy), _lib.ptr(dx), _lib.ptr(dw), _lib.ptr(parts), parts.numel(), _lib.stream_of(xc))
     return dx.reshape(x_pre.shape), dw.to(weight.dtype)
 
 

@@ -66,3 +66,28 @@ def test_cpu_levels_raise_no_fallback():
     wl = [torch.zeros(1, n >> l, 2, 1) for l in range(4)]
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         T.init_decode_state(kl, kl, wl, fmap, cache)
+
+
+@pytest.mark.parametrize("bad", ["k_batch", "k_heads", "v_dim", "w_heads"])
+def test_mismatched_level_raises_before_launch(bad):
+    """A level with live nodes whose batch, head count or head dim differs
+    from level 0's raises ValueError before anything is launched (the kernel
+    would copy level 0's row size from it); the reference fails on the ring
+    write of that level instead."""
+    import torch
+
+    import telescope_cache_b200 as T
+    n, fmap, cache = 40, {1: 8, 2: 16, 3: 24}, 32
+    kl = [torch.zeros(2, n >> l, 2, 8) for l in range(4)]
+    vl = [torch.zeros(2, n >> l, 2, 8) for l in range(4)]
+    wl = [torch.zeros(2, n >> l, 2, 1) for l in range(4)]
+    if bad == "k_batch":
+        kl[1] = torch.zeros(1, n >> 1, 2, 8)
+    elif bad == "k_heads":
+        kl[2] = torch.zeros(2, n >> 2, 1, 8)
+    elif bad == "v_dim":
+        vl[1] = torch.zeros(2, n >> 1, 2, 4)
+    else:
+        wl[2] = torch.zeros(2, n >> 2, 3, 1)
+    with pytest.raises(ValueError, match="shape"):
+        T.init_decode_state(kl, vl, wl, fmap, cache)
