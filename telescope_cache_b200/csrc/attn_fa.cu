@@ -27,12 +27,16 @@
 // softmax therefore starts every tile with O_X up to date.
 // Shared memory: Q_A, Q_B (64 KB) and a two-stage K/V ring (128 KB).
 //
-// Softcap: S = c tanh(x / c).  With y = x / c, when |y| <= 0.5 over every
-// score of a row's tile (a warp-uniform test), tanh(y) comes from its odd
-// Maclaurin series through y^9 (Horner form in y^2, truncation error below
-// 1e-5 relative), evaluated on the FMA pipe; otherwise from the tanh.approx
-// instruction.  Either way the logits match the reference's c tanh(x / c)
-// well within the bf16 tolerance.
+// Softcap: S = c tanh(x / c).  With y = x / c and a the largest |y| over the
+// visible scores of a tile's rows (a warp-uniform test), tanh(y) comes from
+// its odd Maclaurin series (Horner form in y^2) on the FMA pipe: through y^5
+// when a <= 0.15, through y^9 when a <= 0.5 (truncation error below 1e-6 and
+// 1e-5 relative); otherwise from the tanh.approx instruction.  Each matches
+// the reference's c tanh(x / c) well within the bf16 tolerance.
+//
+// Masks: each row's visible nodes of a tile are one contiguous column range.
+// Every 32-column chunk is classified for the whole warp as fully visible,
+// fully masked (P = 0, no exp2) or mixed (per-column selects).
 //
 // Every mbarrier wait is bounded (tc_ptx.cuh); a timeout sets
 // TC_DEV_WAIT_TIMEOUT in the device status word and the CTA drains.
@@ -52,7 +56,8 @@ constexpr int FNS = 2;                 // K/V stages
 constexpr int kFaSmem = 2 * FT + 2 * FNS * FT + 1024 + 256;
 static_assert(kFaSmem <= 227 * 1024, "two-tile forward shared memory exceeds the per-CTA limit");
 constexpr float kFaRescale = 8.f;      // lazy rescale threshold, log2 units
-constexpr float kPolyMax = 0.5f;       // |x / c| bound of the series tanh
+constexpr float kPolyMax5 = 0.15f;     // |x / c| bound of the degree-5 series tanh
+constexpr float kPolyMax9 = 0.5f;      // |x / c| bound of the degree-9 series tanh
 
 // Maclaurin coefficients of tanh(y) = y + c3 y^3 + c5 y^5 + c7 y^7 + c9 y^9 + ...
 constexpr double kT3 = -1.0 / 3.0, kT5 = 2.0 / 15.0, kT7 = -17.0 / 315.0, kT9 = 62.0 / 2835.0;
@@ -108,48 +113,63 @@ struct FaWalk {
 
 __device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
 
-// The row's logit maximum (log2 units) from its largest visible raw score.
-template <bool CAP>
-__device__ __forceinline__ float logit_of(float u, const FaParams& p, bool fast) {
-  if constexpr (!CAP) {
+// How a tile's logits are formed: no softcap, softcap through the degree-5 or
+// degree-9 series, or softcap through tanh.approx.
+enum { kLogitPlain = 0, kLogitS5 = 1, kLogitS9 = 2, kLogitTanh = 3 };
+
+// log2-unit logit of raw score u under mode MODE.
+template <int MODE>
+__device__ __forceinline__ float logit1(float u, const FaParams& p) {
+  if constexpr (MODE == kLogitPlain) {
     return u * p.kq;
+  } else if constexpr (MODE == kLogitS5) {
+    const float w = u * u;
+    return u * fmaf(w, fmaf(w, p.e5, p.e3), p.e1);
+  } else if constexpr (MODE == kLogitS9) {
+    const float w = u * u;
+    return u * fmaf(w, fmaf(w, fmaf(w, fmaf(w, p.e9, p.e7), p.e5), p.e3), p.e1);
   } else {
-    if (fast) {
-      const float w = u * u;
-      return u * fmaf(w, fmaf(w, fmaf(w, fmaf(w, p.e9, p.e7), p.e5), p.e3), p.e1);
-    }
     return p.kc * tanh_fast(u * p.kq);
   }
 }
 
+// logit - m for a pair of raw scores.
+template <int MODE>
+__device__ __forceinline__ float2 logit2_minus(float2 u, const FaParams& p, float2 negm) {
+  if constexpr (MODE == kLogitPlain) {
+    return ffma2(u, f2(p.kq), negm);
+  } else if constexpr (MODE == kLogitS5) {
+    const float2 w = fmul2(u, u);
+    const float2 q = ffma2(w, ffma2(w, f2(p.e5), f2(p.e3)), f2(p.e1));
+    return ffma2(u, q, negm);
+  } else if constexpr (MODE == kLogitS9) {
+    const float2 w = fmul2(u, u);
+    float2 q = ffma2(w, f2(p.e9), f2(p.e7));
+    q = ffma2(w, q, f2(p.e5));
+    q = ffma2(w, q, f2(p.e3));
+    q = ffma2(w, q, f2(p.e1));
+    return ffma2(u, q, negm);
+  } else {
+    const float2 y = fmul2(u, f2(p.kq));
+    return ffma2(make_float2(tanh_fast(y.x), tanh_fast(y.y)), f2(p.kc), negm);
+  }
+}
+
 // exp2(logit - m) of 32 scores (tile columns c0 .. c0 + 31) as 16 packed
-// 16-bit pairs (column 2i in the low half of word i), masked columns 0.
-// Returns their sum.
-template <typename T, bool CAP, bool FAST, bool MASK>
+// 16-bit pairs (column 2i in the low half of word i); with MASK, columns
+// outside [jlo, jhi) are 0.  Returns their sum.
+template <typename T, int MODE, bool MASK>
 __device__ __forceinline__ float softmax_chunk(const float* sv, int c0, const FaParams& p, float m, int jlo,
                                                int jhi, uint32_t* pw) {
   const float2 negm = f2(-m);
   float2 acc0 = f2(0.f), acc1 = f2(0.f);
+  const unsigned span = (unsigned)(jhi - jlo);
 #pragma unroll
   for (int c = 0; c < 32; c += 2) {
-    const float2 u = make_float2(sv[c], sv[c + 1]);
-    float2 a;
-    if constexpr (CAP && FAST) {
-      const float2 w = fmul2(u, u);
-      float2 q = ffma2(w, f2(p.e9), f2(p.e7));
-      q = ffma2(w, q, f2(p.e5));
-      q = ffma2(w, q, f2(p.e3));
-      q = ffma2(w, q, f2(p.e1));
-      a = ffma2(u, q, negm);
-    } else if constexpr (CAP) {
-      const float2 y = fmul2(u, f2(p.kq));
-      a = ffma2(make_float2(tanh_fast(y.x), tanh_fast(y.y)), f2(p.kc), negm);
-    } else {
-      a = ffma2(u, f2(p.kq), negm);
-    }
+    float2 a = logit2_minus<MODE>(make_float2(sv[c], sv[c + 1]), p, negm);
     if constexpr (MASK) {
-      a.x = (c0 + c >= jlo && c0 + c < jhi) ? a.x : -INFINITY;
-      a.y = (c0 + c + 1 >= jlo && c0 + c + 1 < jhi) ? a.y : -INFINITY;
+      a.x = (unsigned)(c0 + c - jlo) < span ? a.x : -INFINITY;
+      a.y = (unsigned)(c0 + c + 1 - jlo) < span ? a.y : -INFINITY;
     }
     const float2 e = make_float2(exp2_fast(a.x), exp2_fast(a.y));
     if ((c >> 1) & 1) acc1 = fadd2(acc1, e);
@@ -158,6 +178,51 @@ __device__ __forceinline__ float softmax_chunk(const float* sv, int c0, const Fa
   }
   const float2 s = fadd2(acc0, acc1);
   return s.x + s.y;
+}
+
+// The 32-column chunk [c0, c0 + 32) for the warp's rows: 0 every column
+// visible, 1 none visible, 2 mixed.
+__device__ __forceinline__ int chunk_kind(int c0, int jlo, int jhi) {
+  if (__all_sync(0xffffffffu, jlo <= c0 && jhi >= c0 + 32)) return 0;
+  if (__all_sync(0xffffffffu, jhi <= c0 || jlo >= c0 + 32)) return 1;
+  return 2;
+}
+
+// Largest and smallest visible raw score of 32 columns.
+template <bool MASK>
+__device__ __forceinline__ void chunk_minmax(const float* sv, int c0, int jlo, int jhi, float& mx, float& mn) {
+  const unsigned span = (unsigned)(jhi - jlo);
+  float a0 = mx, a1 = -INFINITY, b0 = mn, b1 = INFINITY;
+#pragma unroll
+  for (int c = 0; c < 32; c += 4) {
+    float v0 = sv[c], v1 = sv[c + 1], v2 = sv[c + 2], v3 = sv[c + 3];
+    if constexpr (MASK) {
+      const bool k0 = (unsigned)(c0 + c - jlo) < span, k1 = (unsigned)(c0 + c + 1 - jlo) < span;
+      const bool k2 = (unsigned)(c0 + c + 2 - jlo) < span, k3 = (unsigned)(c0 + c + 3 - jlo) < span;
+      a0 = fmax3(a0, k0 ? v0 : -INFINITY, k1 ? v1 : -INFINITY);
+      a1 = fmax3(a1, k2 ? v2 : -INFINITY, k3 ? v3 : -INFINITY);
+      b0 = fminf(b0, fminf(k0 ? v0 : INFINITY, k1 ? v1 : INFINITY));
+      b1 = fminf(b1, fminf(k2 ? v2 : INFINITY, k3 ? v3 : INFINITY));
+    } else {
+      a0 = fmax3(a0, v0, v1);
+      a1 = fmax3(a1, v2, v3);
+      b0 = fminf(b0, fminf(v0, v1));
+      b1 = fminf(b1, fminf(v2, v3));
+    }
+  }
+  mx = fmaxf(a0, a1);
+  mn = fminf(b0, b1);
+}
+
+// P words of one 32-column chunk under the tile's logit mode.
+template <typename T, int MODE>
+__device__ __forceinline__ float chunk_p(int kind, const float* sv, int c0, const FaParams& p, float m, int jlo,
+                                         int jhi, uint32_t* pw) {
+  if (kind == 0) return softmax_chunk<T, MODE, false>(sv, c0, p, m, jlo, jhi, pw);
+  if (kind == 2) return softmax_chunk<T, MODE, true>(sv, c0, p, m, jlo, jhi, pw);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) pw[i] = 0u;
+  return 0.f;
 }
 
 template <typename T, bool CAP>
@@ -347,44 +412,34 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       tc_fence_after();
       ++n;
       const int jlo = lo - it.k0, jhi = hi - it.k0;
-      const bool interior = __all_sync(0xffffffffu, jlo <= 0 && jhi >= FBK);
-      // pass 1: largest visible raw score, and the largest |raw score| (all columns)
-      float umax = -INFINITY, amax = 0.f;
+      // pass 1: largest and smallest visible raw score
+      float umax = -INFINITY, umin = INFINITY;
 #pragma unroll 1
       for (int c0 = 0; c0 < FBK; c0 += 64) {
+        const int k0 = chunk_kind(c0, jlo, jhi), k1 = chunk_kind(c0 + 32, jlo, jhi);
+        if (k0 == 1 && k1 == 1) continue;
         float sv[64];
         tmem_ld32(s_addr + c0, sv);
         tmem_ld32(s_addr + c0 + 32, sv + 32);
         tmem_wait_ld();
-        float m0 = -INFINITY, m1 = -INFINITY;
-        if (interior) {
-#pragma unroll
-          for (int c = 0; c < 64; c += 4) {
-            m0 = fmax3(m0, sv[c], sv[c + 1]);
-            m1 = fmax3(m1, sv[c + 2], sv[c + 3]);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 64; c += 2) {
-            const float a0 = (c0 + c >= jlo && c0 + c < jhi) ? sv[c] : -INFINITY;
-            const float a1 = (c0 + c + 1 >= jlo && c0 + c + 1 < jhi) ? sv[c + 1] : -INFINITY;
-            if ((c >> 1) & 1) m1 = fmax3(m1, a0, a1);
-            else m0 = fmax3(m0, a0, a1);
-          }
-        }
-        umax = fmax3(umax, m0, m1);
-        if constexpr (CAP) {
-          float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-          for (int c = 0; c < 64; c += 4) {
-            a0 = fmax3(a0, fabsf(sv[c]), fabsf(sv[c + 1]));
-            a1 = fmax3(a1, fabsf(sv[c + 2]), fabsf(sv[c + 3]));
-          }
-          amax = fmax3(amax, a0, a1);
-        }
+        if (k0 == 0) chunk_minmax<false>(sv, c0, jlo, jhi, umax, umin);
+        else if (k0 == 2) chunk_minmax<true>(sv, c0, jlo, jhi, umax, umin);
+        if (k1 == 0) chunk_minmax<false>(sv + 32, c0 + 32, jlo, jhi, umax, umin);
+        else if (k1 == 2) chunk_minmax<true>(sv + 32, c0 + 32, jlo, jhi, umax, umin);
       }
-      const bool fast = CAP && __all_sync(0xffffffffu, amax * p.kq <= kPolyMax);
-      const float mx = umax > -INFINITY ? logit_of<CAP>(umax, p, fast) : -INFINITY;
+      int mode = kLogitPlain;
+      if constexpr (CAP) {
+        const float amax = umax > -INFINITY ? fmaxf(umax, -umin) * p.kq : 0.f;
+        mode = __all_sync(0xffffffffu, amax <= kPolyMax5)   ? kLogitS5
+               : __all_sync(0xffffffffu, amax <= kPolyMax9) ? kLogitS9
+                                                            : kLogitTanh;
+      }
+      float mx = -INFINITY;
+      if (umax > -INFINITY) {
+        if constexpr (!CAP) mx = logit1<kLogitPlain>(umax, p);
+        else mx = mode == kLogitS5 ? logit1<kLogitS5>(umax, p)
+                  : mode == kLogitS9 ? logit1<kLogitS9>(umax, p) : logit1<kLogitTanh>(umax, p);
+      }
       bool rescale = false;
       float alpha = 1.f;
       if (mx > -INFINITY) {
@@ -414,27 +469,26 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       float ts = 0.f;
 #pragma unroll 1
       for (int c0 = 0; c0 < FBK; c0 += 64) {
+        const int k0 = chunk_kind(c0, jlo, jhi), k1 = chunk_kind(c0 + 32, jlo, jhi);
         float sv[64];
         uint32_t pw[32];
-        tmem_ld32(s_addr + c0, sv);
-        tmem_ld32(s_addr + c0 + 32, sv + 32);
-        tmem_wait_ld();
-        if (interior) {
-          if (fast) {
-            ts += softmax_chunk<T, CAP, true, false>(sv, c0, p, m_eff, jlo, jhi, pw);
-            ts += softmax_chunk<T, CAP, true, false>(sv + 32, c0 + 32, p, m_eff, jlo, jhi, pw + 16);
-          } else {
-            ts += softmax_chunk<T, CAP, false, false>(sv, c0, p, m_eff, jlo, jhi, pw);
-            ts += softmax_chunk<T, CAP, false, false>(sv + 32, c0 + 32, p, m_eff, jlo, jhi, pw + 16);
-          }
+        if (k0 != 1 || k1 != 1) {
+          tmem_ld32(s_addr + c0, sv);
+          tmem_ld32(s_addr + c0 + 32, sv + 32);
+          tmem_wait_ld();
+        }
+        if constexpr (!CAP) {
+          ts += chunk_p<T, kLogitPlain>(k0, sv, c0, p, m_eff, jlo, jhi, pw);
+          ts += chunk_p<T, kLogitPlain>(k1, sv + 32, c0 + 32, p, m_eff, jlo, jhi, pw + 16);
+        } else if (mode == kLogitS5) {
+          ts += chunk_p<T, kLogitS5>(k0, sv, c0, p, m_eff, jlo, jhi, pw);
+          ts += chunk_p<T, kLogitS5>(k1, sv + 32, c0 + 32, p, m_eff, jlo, jhi, pw + 16);
+        } else if (mode == kLogitS9) {
+          ts += chunk_p<T, kLogitS9>(k0, sv, c0, p, m_eff, jlo, jhi, pw);
+          ts += chunk_p<T, kLogitS9>(k1, sv + 32, c0 + 32, p, m_eff, jlo, jhi, pw + 16);
         } else {
-          if (fast) {
-            ts += softmax_chunk<T, CAP, true, true>(sv, c0, p, m_eff, jlo, jhi, pw);
-            ts += softmax_chunk<T, CAP, true, true>(sv + 32, c0 + 32, p, m_eff, jlo, jhi, pw + 16);
-          } else {
-            ts += softmax_chunk<T, CAP, false, true>(sv, c0, p, m_eff, jlo, jhi, pw);
-            ts += softmax_chunk<T, CAP, false, true>(sv + 32, c0 + 32, p, m_eff, jlo, jhi, pw + 16);
-          }
+          ts += chunk_p<T, kLogitTanh>(k0, sv, c0, p, m_eff, jlo, jhi, pw);
+          ts += chunk_p<T, kLogitTanh>(k1, sv + 32, c0 + 32, p, m_eff, jlo, jhi, pw + 16);
         }
         tmem_st16u(s_addr + c0 / 2, pw);
         tmem_st16u(s_addr + c0 / 2 + 16, pw + 16);

@@ -104,7 +104,7 @@ def _tensor_core_shape(dtype, Dk, Dv):
 
 
 def _prepare(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope_sin,
-             relative_states, relative_proj, impl=None, band_of=None):
+             relative_states, relative_proj, impl=None, band_of=None, block_m=16, block_n=32):
     """Shared validation + operand preparation of forward and backward.
     band_of: the forward's lse in a backward, whose relative band is reused
     when it was kept for the same, unmodified states and proj."""
@@ -121,7 +121,7 @@ def _prepare(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope
                            B=B, N=N, Hq=Hq, Dk=Dk, spec=spec, rope_positions=N)
     mn, mx, _ = visible_stats(spec)
     if position_mode == "relative":
-        check_relative_bins(spec, bins, mx)
+        check_relative_bins(spec, bins, mx, block_m=block_m, block_n=block_n)
     if mn == 0:
         raise RuntimeError("Found query rows with no attended KV entries.")
     _lib.require_cuda(q, packed.k, packed.v)
@@ -168,10 +168,10 @@ def _prepare(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope
 
 
 def _forward(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope_sin,
-             relative_states, relative_proj, impl=None):
+             relative_states, relative_proj, impl=None, block_m=16, block_n=32):
     args, sched, spec, keep, dims = _prepare(q, packed, fmap, cache_size, softcap, position_mode,
                                              rope_cos, rope_sin, relative_states, relative_proj,
-                                             impl)
+                                             impl, block_m=block_m, block_n=block_n)
     B, N, Hq, Hkv, Dk, Dv, dtype = dims
     out = torch.empty(B, N, Hq, Dv, device=q.device, dtype=dtype)
     lse = torch.empty(B, N, Hq, device=q.device, dtype=torch.float32)
@@ -189,22 +189,22 @@ def _forward(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope
 class _Attention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, pk, pv, relative_states, relative_proj, offsets, fmap, cache_size, softcap,
-                position_mode, rope_cos, rope_sin, impl):
+                position_mode, rope_cos, rope_sin, impl, blocks):
         packed = PackedKV(pk, pv, offsets)
         out, lse = _forward(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope_sin,
-                            relative_states, relative_proj, impl)
+                            relative_states, relative_proj, impl, *blocks)
         ctx.save_for_backward(q, pk, pv, out, lse, relative_states, relative_proj, rope_cos, rope_sin)
-        ctx.cfg = (offsets, fmap, cache_size, softcap, position_mode, impl)
+        ctx.cfg = (offsets, fmap, cache_size, softcap, position_mode, impl, blocks)
         return out, lse
 
     @staticmethod
     def backward(ctx, dout, dlse):
         q, pk, pv, out, lse, st, pj, cos, sin = ctx.saved_tensors
-        offsets, fmap, cache_size, softcap, position_mode, impl = ctx.cfg
+        offsets, fmap, cache_size, softcap, position_mode, impl, blocks = ctx.cfg
         if dout is None:
             dout = torch.zeros_like(out)
         dq, dk, dv, dpos, _ = multilevel_attention_backward(
-            q, PackedKV(pk, pv, offsets), out, lse, dout.to(out.dtype), fmap, cache_size,
+            q, PackedKV(pk, pv, offsets), out, lse, dout.to(out.dtype), fmap, cache_size, *blocks,
             softcap=softcap, dlse=dlse, position_mode=position_mode, rope_cos=cos, rope_sin=sin,
             relative_states=st, relative_proj=pj, impl=impl)
         dst = dpj = None
@@ -214,7 +214,7 @@ class _Attention(torch.autograd.Function):
             if ctx.needs_input_grad[4]:
                 dpj = torch.einsum("bnhd,bnhr->dr", st.float(), dpos).to(pj.dtype)
         return (dq.to(q.dtype), dk.to(pk.dtype), dv.to(pv.dtype), dst, dpj,
-                None, None, None, None, None, None, None, None)
+                None, None, None, None, None, None, None, None, None)
 
 
 def multilevel_attention_forward(
@@ -236,18 +236,19 @@ def multilevel_attention_forward(
     """(out [B, N, Hq, Dv] in V's dtype, lse [B, N, Hq] fp32 natural-log,
     pre-sink) with S = c tanh(X / c) (or X when softcap is None),
     X = q.k / sqrt(Dk) [+ relative bias], softmax over exactly each query's
-    multiresolution set (reference.py:771-1071).  block_m / block_n are
-    accepted for signature compatibility; tiling is the kernel's choice.
-    ``impl`` ('simt' | 'tensor' | None) pins a kernel family for testing."""
-    del block_m, block_n
+    multiresolution set (reference.py:771-1071).  Tiling is the kernel's
+    choice; block_m / block_n only name the query blocks and node tiles at
+    which a too-small relative table is reported, as the reference's loop
+    does.  ``impl`` ('simt' | 'tensor' | None) pins a kernel family for
+    testing."""
     grad = torch.is_grad_enabled() and any(
         t is not None and t.requires_grad for t in (q, packed.k, packed.v, relative_states, relative_proj))
     if not grad:
         return _forward(q, packed, fmap, cache_size, softcap, position_mode, rope_cos, rope_sin,
-                        relative_states, relative_proj, impl)
+                        relative_states, relative_proj, impl, block_m, block_n)
     return _Attention.apply(q, packed.k, packed.v, relative_states, relative_proj,
                             tuple(packed.level_offsets), fmap, cache_size, softcap, position_mode,
-                            rope_cos, rope_sin, impl)
+                            rope_cos, rope_sin, impl, (block_m, block_n))
 
 
 @torch.no_grad()
@@ -277,8 +278,9 @@ def multilevel_attention_backward(
     dQ = scale dX K, dK = scale dX^T Q, dV = P^T dO; RoPE gradients are
     rotated back by R(-p) in fp32.  Returns the fixed 5-tuple
     (dq, dk_packed, dv_packed, dposition, stats); dposition is drel_logits
-    [B, N, Hq, max_relative_bins] fp32 in relative mode, else None."""
-    del block_m, block_n
+    [B, N, Hq, max_relative_bins] fp32 in relative mode, else None.
+    block_m / block_n only name where a too-small relative table is
+    reported (the reference's query blocks and node tiles)."""
     if position_mode not in ("none", "rope", "relative"):
         raise ValueError(
             f"position_mode must be 'none', 'rope' or 'relative', got {position_mode!r}")
@@ -305,7 +307,7 @@ def multilevel_attention_backward(
             raise ValueError("dlse must have floating dtype")
     args, sched, spec, keep, dims = _prepare(q, packed, fmap, cache_size, softcap, position_mode,
                                              rope_cos, rope_sin, relative_states, relative_proj,
-                                             impl, band_of=lse)
+                                             impl, band_of=lse, block_m=block_m, block_n=block_n)
     dtype = dims[-1]
     _lib.require_cuda(out, lse, dout, dlse)
     oc = out.to(dtype).contiguous()

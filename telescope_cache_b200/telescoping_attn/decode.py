@@ -14,7 +14,7 @@ from .position import check_relative_bins, compute_relative_states, positional_a
 
 
 def _decode_positional(state, q_t, t, position_mode, rope_cos, rope_sin, relative_states,
-                       relative_proj):
+                       relative_proj, block_n=32):
     B, _, Hq, Dk = q_t.shape
     spec = state.spec(t + 1)
     bins = positional_args(position_mode, rope_cos, rope_sin, relative_states, relative_proj,
@@ -26,7 +26,7 @@ def _decode_positional(state, q_t, t, position_mode, rope_cos, rope_sin, relativ
     elif position_mode == "relative":
         from ..range_spec import range_bounds
         visible = sum(hi - lo for lo, hi in (range_bounds(spec, t, lv) for lv in range(spec.num_levels)))
-        check_relative_bins(spec, bins, visible)
+        check_relative_bins(spec, bins, visible, block_n=block_n, query=t)
         rdt = torch.result_type(relative_states, relative_proj)
         if rdt not in (torch.float32, torch.bfloat16, torch.float16):
             rdt = torch.float32
@@ -68,7 +68,6 @@ def multilevel_attention_decode(
 ):
     """Attention of query t = state.t - 1 over its ring entries
     (reference.py:2093-2239) -> (out [B, 1, Hq, Dv], lse [B, 1, Hq] fp32, stats)."""
-    del block_n
     if q_t.dim() != 4 or q_t.shape[1] != 1:
         raise ValueError(f"q_t must be [B, 1, Hq, Dk], got {tuple(q_t.shape)}")
     if state.t < 1:
@@ -82,7 +81,7 @@ def multilevel_attention_decode(
         raise ValueError(f"Hq={Hq} must be divisible by Hkv={Hkv}.")
     t = state.t - 1
     cos, sin, st, pj = _decode_positional(state, q_t, t, position_mode, rope_cos, rope_sin,
-                                          relative_states, relative_proj)
+                                          relative_states, relative_proj, block_n)
     k_rot = _ensure_rotated_ring(state, cos, sin) if position_mode == "rope" else None
     out, lse, _, _ = _decode_launch(state, _lib.DECODE_ATTEND, q_t, softcap=softcap,
                                     position_mode=position_mode, cos=cos, sin=sin, rel_states=st,
@@ -114,7 +113,6 @@ def decode_step(
     """The telescope block for one token after the Q/K/V projections: advance
     the cache, attend, sink, gate (reference.py:2242-2317).  Returns
     (out [B, 1, Hq, Dv] post-sink/gate, lse [B, 1, Hq] pre-sink fp32)."""
-    del block_n
     if weight_mode == "qk":
         if w_proj is not None:
             raise ValueError("w_proj provided with weight_mode='qk'")
@@ -137,7 +135,7 @@ def decode_step(
         raise ValueError(f"relative_weight provided with position_mode={position_mode!r}")
     t = state.t
     cos, sin, st, pj = _decode_positional(state, q_t, t, position_mode, rope_cos, rope_sin,
-                                          relative_states, relative_proj)
+                                          relative_states, relative_proj, block_n)
     if sinks is not None and tuple(sinks.shape) != (Hq,):
         raise ValueError(f"sinks shape {tuple(sinks.shape)} != {(Hq,)} (one logit per query head)")
     gate_pre = None

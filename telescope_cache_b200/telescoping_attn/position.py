@@ -9,7 +9,7 @@ from typing import Optional, Tuple
 import torch
 
 from .. import _lib
-from ..range_spec import RangeSpec, elem_mask, range_bounds, visible_stats
+from ..range_spec import IntOps, RangeSpec, elem_mask, range_bounds, visible_stats
 
 
 def summary_token_position(level: int, local_index: int) -> int:
@@ -158,15 +158,74 @@ def positional_args(position_mode, rope_cos, rope_sin, relative_states, relative
     return bins
 
 
-def check_relative_bins(spec: RangeSpec, bins: int, max_visible: Optional[int] = None):
+def _first_bin_overflow(spec: RangeSpec, bins: int, q_blocks, block_n: int, exact: bool):
+    """(distance, q_start, q_end, level) of the first tile at which the
+    reference's loop meets a visible entry whose bin distance reaches
+    `bins`, or None.  The reference walks query blocks in order, then
+    levels, then block_n-node tiles (of the block's hull, or of the row's
+    exact range when `exact`), and raises at the first tile holding an
+    offending visible lane, reporting that tile's largest visible distance
+    (reference.py:398-452, :959-1000, :1497-1545, :2175-2206).  A visible
+    node j of level l has distance prefix(l) + hi(l) - 1 - j, prefix(l)
+    counting the finer levels' entries."""
+    import numpy as np
+
+    from ..range_spec import fwd_bounds, level_row_bounds, normalize_empty
+
+    a, cache = spec.activation_times, spec.cache_size
+    nl = spec.num_levels
+    np_ops = IntOps(minimum=np.minimum, maximum=np.maximum)
+    for q_start, q_end in q_blocks:
+        qs = np.arange(q_start, q_end, dtype=np.int64)
+        raw = level_row_bounds(qs, a, cache, np_ops)
+        lo = np.stack([np.where(l_ < h_, l_, 0) for l_, h_ in raw], 1)
+        hi = np.stack([np.where(l_ < h_, h_, 0) for l_, h_ in raw], 1)
+        cnt = hi - lo
+        if int(cnt.sum(1).max()) - 1 < bins:
+            continue
+        prefix = np.cumsum(cnt, 1) - cnt
+        for level in range(nl):
+            if exact:
+                k_lo, k_hi = int(lo[0, level]), int(hi[0, level])
+            else:
+                k_lo, k_hi = fwd_bounds(spec, q_start, q_end, level)
+            if k_lo == k_hi:
+                continue
+            for k_start in range(k_lo, k_hi, block_n):
+                k_end = min(k_start + block_n, k_hi)
+                first = np.maximum(lo[:, level], k_start)
+                vis = first < np.minimum(hi[:, level], k_end)
+                if not vis.any():
+                    continue
+                dmax = int((prefix[:, level] + hi[:, level] - 1 - first)[vis].max())
+                if dmax >= bins:
+                    return dmax, q_start, q_end, level
+    return None
+
+
+def check_relative_bins(spec: RangeSpec, bins: int, max_visible: Optional[int] = None, *,
+                        block_m: int = 16, block_n: int = 32, query: Optional[int] = None):
     """The reference raises when a visible entry's distance reaches the table
-    size (reference.py:441-452); distances run to |A(q)| - 1, so the check is
-    max_q |A(q)| > bins, decided once per schedule."""
+    size (reference.py:441-452).  Distances run to |A(q)| - 1, so whether it
+    raises is max_q |A(q)| > bins, decided once per schedule; only then is
+    the reference's tile loop replayed on the host (query blocks of block_m,
+    or the single decode query `query` over its exact ranges, and block_n
+    tiles) to raise with the same message at the same tile."""
     mx = visible_stats(spec)[1] if max_visible is None else max_visible
-    if mx - 1 >= bins:
-        raise ValueError(
-            f"relative bin distance {mx - 1} exceeds max_relative_bins={bins}; no silent "
-            f"clamping -- a table with >= cache_size={spec.cache_size} bins always suffices")
+    if mx - 1 < bins:
+        return
+    if query is None:
+        blocks = ((q, min(q + block_m, spec.seq_len)) for q in range(0, spec.seq_len, max(block_m, 1)))
+    else:
+        blocks = ((query, query + 1),)
+    hit = _first_bin_overflow(spec, bins, blocks, max(block_n, 1), query is not None)
+    if hit is None:
+        return
+    dist, q_start, q_end, level = hit
+    raise ValueError(
+        f"relative bin distance {dist} in query block [{q_start},{q_end}) at level {level} exceeds "
+        f"max_relative_bins={bins}; no silent clamping -- a table with >= cache_size={spec.cache_size} "
+        f"bins always suffices")
 
 
 __all__ = ["summary_token_position", "rope_tables", "apply_rope", "validate_summary_causality",

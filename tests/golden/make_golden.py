@@ -2,9 +2,11 @@
 implementation (Knarf04/telescope_cache ``reference.py`` and
 ``telescoping_attn/range_spec.py``) on the seeded cases of ``cases.py``.
 
-Run from the repository root, in a container where the reference is mounted:
+Run from the repository root, in a container where the reference is mounted,
+naming its checkout with --reference or the TC_REFERENCE_ROOT environment
+variable:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 The reference expects to be importable as package ``telescope_cache`` with a
 top-level ``range_spec`` module; this script builds that package as a
@@ -228,9 +230,12 @@ def gen_schedule(rs, ref, name, N, cache, fmap):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("TC_REFERENCE_ROOT"),
+                    help="reference checkout (default: $TC_REFERENCE_ROOT)")
     ap.add_argument("--only", nargs="*")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or TC_REFERENCE_ROOT")
     rs, ref = import_reference(args.reference)
     for c in C.CASES:
         if args.only and c["name"] not in args.only:
