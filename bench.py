@@ -16,9 +16,12 @@ The metric is visible-entry TFLOP/s: per visible (query, entry) pair and query
 head, 4 D FLOPs forward (QK^T and PV) + 10 D backward (five GEMMs); hull
 padding, softcap, bias and RoPE are not counted.
 
-``--impl reference`` times the CPU oracle (a numpy restatement of the
-reference's reference.py; the reference itself is Python and cannot run on
-the GPU box) on a bounded sample of the same workload, on all host threads.
+``--impl reference`` times the reference's own ``reference.py`` (pure
+Python over torch, installed under ``baseline/_ref``, which travels to the
+GPU box) on the box's host cores, on a bounded sample of the same workload:
+one (batch, head) slice of the workload's schedule and features at a shorter
+sequence.  When that install is missing it falls back to the numpy oracle
+port and says so.
 """
 
 import argparse
@@ -491,27 +494,103 @@ def cpu_reference_sample(wl, seconds_budget=20.0):
         f"numpy, {el:.1f} s; throughput scales linearly with the slice count")
 
 
+REF_SAMPLE_T = 2048  # tokens of the reference's (batch, head) sample slice
+
+
+def reference_py_sample(wl, T_s=REF_SAMPLE_T, seed=5):
+    """Time the reference's own public API (reference.py from baseline/_ref,
+    fp32 on the host cores, all threads) on one (batch, head) slice of the
+    workload's schedule and features at sequence length T_s: the tree build
+    and packing, the forward, the sink and its backward, and the backward
+    with the dlse seam -- the step this file times on the GPU.  Returns
+    (TFLOP/s on visible-entry FLOPs, seconds, description), or None when the
+    reference is not installed."""
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "telescope_cache")):
+        return None
+    if ref_root not in sys.path:
+        sys.path.insert(0, ref_root)
+    import torch
+    try:
+        import telescope_cache.reference as ref
+    except Exception:  # noqa: BLE001 - any import failure means: not installed here
+        return None
+    from telescope_cache_b200 import range_spec as R
+    torch.set_num_threads(os.cpu_count() or 1)
+    fmap, cache = schedule(wl)
+    D, levels = wl["D"], wl["levels"]
+    g = torch.Generator().manual_seed(seed)
+    q, k, v, dout = (torch.randn(1, T_s, 1, D, generator=g) for _ in range(4))
+    kw, pos = {}, {}
+    if wl["weights"] == "linear":
+        kw = dict(x=torch.randn(1, T_s, EMB, generator=g), w_proj=0.02 * torch.randn(1, EMB, generator=g))
+    if wl["conv"]:
+        kw.update(k_conv_weight=torch.randn(D, wl["conv"], generator=g) / math.sqrt(wl["conv"]),
+                  v_conv_weight=torch.randn(D, wl["conv"], generator=g) / math.sqrt(wl["conv"]))
+    if wl["position"] == "relative":
+        pos = dict(position_mode="relative", relative_states=0.02 * torch.randn(1, T_s, 1, wl["d_rel"], generator=g),
+                   relative_proj=0.02 * torch.randn(wl["d_rel"], cache, generator=g))
+    elif wl["position"] == "rope":
+        cos, sin = ref.rope_tables(T_s, D)
+        pos = dict(position_mode="rope", rope_cos=cos, rope_sin=sin)
+    sinks = torch.randn(1, generator=g)
+    t0 = time.perf_counter()
+    kl, vl, _ = ref.build_dyadic_summaries(q, k, v, levels - 1, **kw)
+    packed = ref.pack_levels(kl, vl)
+    out, lse = ref.multilevel_attention_forward(q, packed, fmap, cache, softcap=wl["softcap"], **pos)
+    dlse = None
+    if wl["sink"]:
+        ref.apply_attention_sink(out, lse, sinks)
+        dout, dlse, _ = ref.attention_sink_backward(out, lse, sinks, dout)
+    ref.multilevel_attention_backward(q, packed, out, lse, dout, fmap, cache, softcap=wl["softcap"], dlse=dlse,
+                                      **pos)
+    el = time.perf_counter() - t0
+    pairs = R.visible_stats(R.RangeSpec.from_fmap(fmap, cache, T_s))[2]
+    desc = (f"reference.py (baseline/_ref) fp32 on {os.cpu_count()} host threads: one (batch, head) slice at "
+            f"T={T_s} of the {args_workload_name(wl)} schedule and features (tree, forward, sink, sink "
+            f"backward, backward), {el:.1f} s; visible-entry FLOPs of that slice / time")
+    return (4 + 10) * D * pairs / el / 1e12, el, desc
+
+
+def args_workload_name(wl):
+    return next((n for n, w in WORKLOADS.items() if w is wl), "workload")
+
+
 def reference_arm(args, wl):
+    """--impl reference: the reference's own implementation timed on the host
+    cores (rank 0 only; other ranks exit without work).  Each step is one
+    bounded sample (reference_py_sample); the line reports the median of the
+    timed steps.  Falls back to the numpy oracle port when the reference is
+    not installed, and says so."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    times = []
-    sample = ""
+    times, secs = [], []
+    sample, kind = "", "reference"
     for i in range(args.warmup + args.steps):
-        tf, sample = cpu_reference_sample(wl, seconds_budget=max(5.0, 60.0 / (args.steps + args.warmup)))
+        got = reference_py_sample(wl)
+        if got is None:
+            tf, sample = cpu_reference_sample(wl, seconds_budget=max(5.0, 60.0 / (args.steps + args.warmup)))
+            sample = "numpy oracle port (reference.py not installed under baseline/_ref): " + sample
+            kind, el = "port", None
+        else:
+            tf, el, sample = got
         if i >= args.warmup:
             times.append(tf)
+            secs.append(el)
     val = sorted(times)[len(times) // 2]
     fmap, cache = schedule(wl)
+    sec = sorted(s_ for s_ in secs if s_ is not None)
     line = {
         "impl": "reference", "metric": "multilevel attn fwd+bwd TFLOP/s (visible-entry FLOPs)",
         "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "desc": wl["desc"], "fmap": fmap, "cache_size": cache},
-        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                         "sample": sample},
+        "warmup": args.warmup, "ms_per_step": sec[len(sec) // 2] * 1e3 if sec else None,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "desc": wl["desc"], "B_per_rank": wl["B"], "T": wl["T"],
+                   "H": wl["H"], "D": wl["D"], "fmap": fmap, "cache_size": cache,
+                   "sample": f"one (batch, head) slice at T={REF_SAMPLE_T} per step"},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -712,9 +791,14 @@ def main():
         dec = decode_bench(args, dev, world, with_e2e=not args.no_e2e)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tf, sample = cpu_reference_sample(wl, seconds_budget=15.0)
-        cpu = {"value": tf, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": sample}
+        got = reference_py_sample(wl)
+        if got is not None:
+            cpu = {"value": got[0], "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "reference",
+                   "sample": got[2]}
+        else:
+            tf, sample = cpu_reference_sample(wl, seconds_budget=15.0)
+            cpu = {"value": tf, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": "numpy oracle port (reference.py not installed under baseline/_ref): " + sample}
     launches = launches_timed
     if rank == 0:
         line = {
