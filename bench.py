@@ -450,6 +450,99 @@ def decode_bench(args, dev, world, with_e2e=True):
     return res
 
 
+def c5_sharded_bench(args, dev, world, rank):
+    """Config 5 split by heads across the ranks (strong scaling): rank r owns
+    query / KV heads [r H / N, (r + 1) H / N) (sharding.head_shard).  A step
+    builds its heads' tree (linear merge weights from x and its rows of
+    w_proj), runs the rope forward with softcap 50, the sink and its backward
+    and the Phase-2 backward, then gathers the full out and dq onto every rank
+    with one NCCL all_gather each (into one buffer, then the head-major
+    reorder) -- all inside the timed region.  value = the whole config-5
+    step's visible-entry FLOPs / the max-over-ranks step time."""
+    import torch
+    import torch.distributed as dist
+
+    import telescope_cache_b200 as T
+    from telescope_cache_b200 import range_spec as R
+    from telescope_cache_b200.sharding import head_shard
+
+    wl = WORKLOADS["c5"]
+    B, N, H, D = wl["B"], wl["T"], wl["H"], wl["D"]
+    _, _, h0, h1 = head_shard(H, H, world, rank)
+    hl = h1 - h0
+    fmap, cache = schedule(wl)
+    total_visible = R.visible_stats(R.RangeSpec.from_fmap(fmap, cache, N))[2]
+    step_flops = flops_per_step(wl, total_visible)  # all H heads
+    g = torch.Generator(device=dev)
+    g.manual_seed(2025 + 7919 * rank)
+    bf = torch.bfloat16
+    q, k, v, dout = (torch.randn(B, N, hl, D, generator=g, device=dev, dtype=bf) for _ in range(4))
+    gx = torch.Generator(device=dev)
+    gx.manual_seed(77)  # x and the full w_proj are the same on every rank
+    x = torch.randn(B, N, EMB, generator=gx, device=dev, dtype=bf)
+    w_proj = (0.02 * torch.randn(H, EMB, generator=gx, device=dev)).to(bf)[h0:h1].contiguous()
+    sinks = torch.randn(H, generator=gx, device=dev)[h0:h1].contiguous()
+    cos, sin = T.rope_tables(N, D, device=dev)
+    out_full = torch.empty(world, B, N, hl, D, device=dev, dtype=bf)
+    dq_full = torch.empty_like(out_full)
+
+    def gather(local, buf):
+        if world == 1:
+            return local
+        dist.all_gather_into_tensor(buf.view(world, -1), local.reshape(1, -1))
+        return buf.permute(1, 2, 0, 3, 4).reshape(B, N, world * hl, D)
+
+    def step(timers=None):
+        kl, vl, _ = T.build_dyadic_summaries(q, k, v, wl["levels"] - 1, x=x, w_proj=w_proj)
+        packed = T.pack_levels(kl, vl)
+        pos = dict(position_mode="rope", rope_cos=cos, rope_sin=sin)
+        out, lse = T.multilevel_attention_forward(q, packed, fmap, cache, softcap=wl["softcap"], **pos)
+        T.apply_attention_sink(out, lse, sinks)
+        d_out, dlse, _ = T.attention_sink_backward(out, lse, sinks, dout)
+        dq, _, _, _, _ = T.multilevel_attention_backward(q, packed, out, lse, d_out, fmap, cache,
+                                                         softcap=wl["softcap"], dlse=dlse, **pos)
+        if timers:
+            timers[0].record()
+        o_all = gather(out, out_full)
+        dq_all = gather(dq, dq_full)
+        if timers:
+            timers[1].record()
+        return o_all, dq_all
+
+    def sync():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    sync()
+    st = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    gev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sync()
+    for i in range(args.steps):
+        ev[i][0].record(st)
+        step(gev[i])
+        ev[i][1].record(st)
+    sync()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    gms = sum(a.elapsed_time(b) for a, b in gev) / args.steps
+    if world > 1:
+        tm = torch.tensor([ms, gms], device=dev)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms, gms = float(tm[0].item()), float(tm[1].item())
+    burst, sustained, _, src = peaks()
+    value = step_flops / (ms * 1e-3) / 1e12
+    return {"metric": "multilevel attn fwd+bwd TFLOP/s (visible-entry FLOPs), config 5 split by heads",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "scaling": "strong",
+            "ms_per_step": ms, "gather_ms": gms, "gather_share": gms / ms,
+            "config": {"workload": "c5", "desc": wl["desc"], "B": B, "T": N, "H": H, "D": D,
+                       "heads_per_rank": hl, "fmap": fmap, "cache_size": cache, "step_flops": step_flops,
+                       "gathered": "out and dq, [B, T, H, D] bf16 each, NCCL all_gather_into_tensor + head reorder"},
+            "frac_of_peak": value / world / sustained, "peak_source": f"{src} bf16_tflops_sustained (per GPU)"}
+
+
 def cpu_reference_sample(wl, seconds_budget=20.0):
     """Time the CPU oracle (fwd + bwd) on a bounded sample of the workload:
     consecutive query rows of one (batch, head) slice, in the steady state
@@ -641,6 +734,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode", action="store_true",
                     help="skip the config-4 decode measurement added to the c3 line")
+    ap.add_argument("--no-c5-sharded", action="store_true",
+                    help="skip the config-5 head-sharded (strong scaling) measurement added to the c3 line")
     ap.add_argument("--no-vjp", action="store_true",
                     help="skip the Phase-1 VJP measurement added to the line")
     args = ap.parse_args()
@@ -785,6 +880,10 @@ def main():
         _, dk_s, dv_s, _, _ = run_step(T, wl, inp, fmap, cache, tables)
         vjp = vjp_bench(T, wl, inp, (dk_s, dv_s), args, hbm, flush)
         del dk_s, dv_s
+    c5s = None
+    if args.workload == "c3" and not args.no_c5_sharded:
+        c5s = c5_sharded_bench(args, dev, world, rank)
+        torch.cuda.empty_cache()
     dec = None
     if args.workload == "c3" and not args.no_decode:
         # before the CPU baseline, whose worker threads can linger on the host
@@ -821,6 +920,8 @@ def main():
         line["phase1_vjp"] = vjp
     if dec is not None and rank == 0:
         line["decode"] = dec
+    if c5s is not None and rank == 0:
+        line["c5_sharded"] = c5s
     if rank == 0:
         print(json.dumps(line))
     if world > 1:

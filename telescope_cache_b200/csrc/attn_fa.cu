@@ -28,15 +28,11 @@
 // Shared memory: Q_A, Q_B (64 KB) and a two-stage K/V ring (128 KB).
 //
 // Softcap: S = c tanh(x / c).  With y = x / c and a the largest |y| over the
-// visible scores of a tile's rows (a warp-uniform test), tanh(y) comes from
-// its odd Maclaurin series (Horner form in y^2) on the FMA pipe: through y^5
-// when a <= 0.15, through y^9 when a <= 0.5 (truncation error below 1e-6 and
-// 1e-5 relative); otherwise from the tanh.approx instruction.  Each matches
-// the reference's c tanh(x / c) well within the bf16 tolerance.
-//
-// Masks: each row's visible nodes of a tile are one contiguous column range.
-// Every 32-column chunk is classified for the whole warp as fully visible,
-// fully masked (P = 0, no exp2) or mixed (per-column selects).
+// scores of a tile's rows (a warp-uniform test), tanh(y) comes from its odd
+// Maclaurin series (Horner form in y^2) on the FMA pipe: through y^5 when
+// a <= 0.15, through y^9 when a <= 0.5 (truncation error below 1e-6 and 1e-5
+// relative); otherwise from the tanh.approx instruction.  Each matches the
+// reference's c tanh(x / c) well within the bf16 tolerance.
 //
 // Every mbarrier wait is bounded (tc_ptx.cuh); a timeout sets
 // TC_DEV_WAIT_TIMEOUT in the device status word and the CTA drains.
@@ -133,43 +129,38 @@ __device__ __forceinline__ float logit1(float u, const FaParams& p) {
   }
 }
 
-// logit - m for a pair of raw scores.
-template <int MODE>
-__device__ __forceinline__ float2 logit2_minus(float2 u, const FaParams& p, float2 negm) {
-  if constexpr (MODE == kLogitPlain) {
-    return ffma2(u, f2(p.kq), negm);
-  } else if constexpr (MODE == kLogitS5) {
-    const float2 w = fmul2(u, u);
-    const float2 q = ffma2(w, ffma2(w, f2(p.e5), f2(p.e3)), f2(p.e1));
-    return ffma2(u, q, negm);
-  } else if constexpr (MODE == kLogitS9) {
-    const float2 w = fmul2(u, u);
-    float2 q = ffma2(w, f2(p.e9), f2(p.e7));
-    q = ffma2(w, q, f2(p.e5));
-    q = ffma2(w, q, f2(p.e3));
-    q = ffma2(w, q, f2(p.e1));
-    return ffma2(u, q, negm);
-  } else {
-    const float2 y = fmul2(u, f2(p.kq));
-    return ffma2(make_float2(tanh_fast(y.x), tanh_fast(y.y)), f2(p.kc), negm);
-  }
-}
-
 // exp2(logit - m) of 32 scores (tile columns c0 .. c0 + 31) as 16 packed
-// 16-bit pairs (column 2i in the low half of word i); with MASK, columns
-// outside [jlo, jhi) are 0.  Returns their sum.
+// 16-bit pairs (column 2i in the low half of word i), masked columns 0.
+// Returns their sum.
 template <typename T, int MODE, bool MASK>
 __device__ __forceinline__ float softmax_chunk(const float* sv, int c0, const FaParams& p, float m, int jlo,
                                                int jhi, uint32_t* pw) {
   const float2 negm = f2(-m);
   float2 acc0 = f2(0.f), acc1 = f2(0.f);
-  const unsigned span = (unsigned)(jhi - jlo);
 #pragma unroll
   for (int c = 0; c < 32; c += 2) {
-    float2 a = logit2_minus<MODE>(make_float2(sv[c], sv[c + 1]), p, negm);
+    const float2 u = make_float2(sv[c], sv[c + 1]);
+    float2 a;
+    if constexpr (MODE == kLogitS5) {
+      const float2 w = fmul2(u, u);
+      const float2 q = ffma2(w, ffma2(w, f2(p.e5), f2(p.e3)), f2(p.e1));
+      a = ffma2(u, q, negm);
+    } else if constexpr (MODE == kLogitS9) {
+      const float2 w = fmul2(u, u);
+      float2 q = ffma2(w, f2(p.e9), f2(p.e7));
+      q = ffma2(w, q, f2(p.e5));
+      q = ffma2(w, q, f2(p.e3));
+      q = ffma2(w, q, f2(p.e1));
+      a = ffma2(u, q, negm);
+    } else if constexpr (MODE == kLogitTanh) {
+      const float2 y = fmul2(u, f2(p.kq));
+      a = ffma2(make_float2(tanh_fast(y.x), tanh_fast(y.y)), f2(p.kc), negm);
+    } else {
+      a = ffma2(u, f2(p.kq), negm);
+    }
     if constexpr (MASK) {
-      a.x = (unsigned)(c0 + c - jlo) < span ? a.x : -INFINITY;
-      a.y = (unsigned)(c0 + c + 1 - jlo) < span ? a.y : -INFINITY;
+      a.x = (c0 + c >= jlo && c0 + c < jhi) ? a.x : -INFINITY;
+      a.y = (c0 + c + 1 >= jlo && c0 + c + 1 < jhi) ? a.y : -INFINITY;
     }
     const float2 e = make_float2(exp2_fast(a.x), exp2_fast(a.y));
     if ((c >> 1) & 1) acc1 = fadd2(acc1, e);
@@ -180,49 +171,15 @@ __device__ __forceinline__ float softmax_chunk(const float* sv, int c0, const Fa
   return s.x + s.y;
 }
 
-// The 32-column chunk [c0, c0 + 32) for the warp's rows: 0 every column
-// visible, 1 none visible, 2 mixed.
-__device__ __forceinline__ int chunk_kind(int c0, int jlo, int jhi) {
-  if (__all_sync(0xffffffffu, jlo <= c0 && jhi >= c0 + 32)) return 0;
-  if (__all_sync(0xffffffffu, jhi <= c0 || jlo >= c0 + 32)) return 1;
-  return 2;
-}
-
-// Largest and smallest visible raw score of 32 columns.
-template <bool MASK>
-__device__ __forceinline__ void chunk_minmax(const float* sv, int c0, int jlo, int jhi, float& mx, float& mn) {
-  const unsigned span = (unsigned)(jhi - jlo);
-  float a0 = mx, a1 = -INFINITY, b0 = mn, b1 = INFINITY;
-#pragma unroll
-  for (int c = 0; c < 32; c += 4) {
-    float v0 = sv[c], v1 = sv[c + 1], v2 = sv[c + 2], v3 = sv[c + 3];
-    if constexpr (MASK) {
-      const bool k0 = (unsigned)(c0 + c - jlo) < span, k1 = (unsigned)(c0 + c + 1 - jlo) < span;
-      const bool k2 = (unsigned)(c0 + c + 2 - jlo) < span, k3 = (unsigned)(c0 + c + 3 - jlo) < span;
-      a0 = fmax3(a0, k0 ? v0 : -INFINITY, k1 ? v1 : -INFINITY);
-      a1 = fmax3(a1, k2 ? v2 : -INFINITY, k3 ? v3 : -INFINITY);
-      b0 = fminf(b0, fminf(k0 ? v0 : INFINITY, k1 ? v1 : INFINITY));
-      b1 = fminf(b1, fminf(k2 ? v2 : INFINITY, k3 ? v3 : INFINITY));
-    } else {
-      a0 = fmax3(a0, v0, v1);
-      a1 = fmax3(a1, v2, v3);
-      b0 = fminf(b0, fminf(v0, v1));
-      b1 = fminf(b1, fminf(v2, v3));
-    }
-  }
-  mx = fmaxf(a0, a1);
-  mn = fminf(b0, b1);
-}
-
-// P words of one 32-column chunk under the tile's logit mode.
+// P words of 64 columns under the tile's logit mode.
 template <typename T, int MODE>
-__device__ __forceinline__ float chunk_p(int kind, const float* sv, int c0, const FaParams& p, float m, int jlo,
-                                         int jhi, uint32_t* pw) {
-  if (kind == 0) return softmax_chunk<T, MODE, false>(sv, c0, p, m, jlo, jhi, pw);
-  if (kind == 2) return softmax_chunk<T, MODE, true>(sv, c0, p, m, jlo, jhi, pw);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) pw[i] = 0u;
-  return 0.f;
+__device__ __forceinline__ float half_p(bool interior, const float* sv, int c0, const FaParams& p, float m,
+                                        int jlo, int jhi, uint32_t* pw) {
+  if (interior)
+    return softmax_chunk<T, MODE, false>(sv, c0, p, m, jlo, jhi, pw) +
+           softmax_chunk<T, MODE, false>(sv + 32, c0 + 32, p, m, jlo, jhi, pw + 16);
+  return softmax_chunk<T, MODE, true>(sv, c0, p, m, jlo, jhi, pw) +
+         softmax_chunk<T, MODE, true>(sv + 32, c0 + 32, p, m, jlo, jhi, pw + 16);
 }
 
 template <typename T, bool CAP>
@@ -412,27 +369,48 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       tc_fence_after();
       ++n;
       const int jlo = lo - it.k0, jhi = hi - it.k0;
-      // pass 1: largest and smallest visible raw score
-      float umax = -INFINITY, umin = INFINITY;
+      const bool interior = __all_sync(0xffffffffu, jlo <= 0 && jhi >= FBK);
+      // pass 1: largest visible raw score, and the largest |raw score| (all columns)
+      float umax = -INFINITY, amax = 0.f;
 #pragma unroll 1
       for (int c0 = 0; c0 < FBK; c0 += 64) {
-        const int k0 = chunk_kind(c0, jlo, jhi), k1 = chunk_kind(c0 + 32, jlo, jhi);
-        if (k0 == 1 && k1 == 1) continue;
         float sv[64];
         tmem_ld32(s_addr + c0, sv);
         tmem_ld32(s_addr + c0 + 32, sv + 32);
         tmem_wait_ld();
-        if (k0 == 0) chunk_minmax<false>(sv, c0, jlo, jhi, umax, umin);
-        else if (k0 == 2) chunk_minmax<true>(sv, c0, jlo, jhi, umax, umin);
-        if (k1 == 0) chunk_minmax<false>(sv + 32, c0 + 32, jlo, jhi, umax, umin);
-        else if (k1 == 2) chunk_minmax<true>(sv + 32, c0 + 32, jlo, jhi, umax, umin);
+        float m0 = -INFINITY, m1 = -INFINITY;
+        if (interior) {
+#pragma unroll
+          for (int c = 0; c < 64; c += 4) {
+            m0 = fmax3(m0, sv[c], sv[c + 1]);
+            m1 = fmax3(m1, sv[c + 2], sv[c + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; c += 2) {
+            const float a0 = (c0 + c >= jlo && c0 + c < jhi) ? sv[c] : -INFINITY;
+            const float a1 = (c0 + c + 1 >= jlo && c0 + c + 1 < jhi) ? sv[c + 1] : -INFINITY;
+            if ((c >> 1) & 1) m1 = fmax3(m1, a0, a1);
+            else m0 = fmax3(m0, a0, a1);
+          }
+        }
+        umax = fmax3(umax, m0, m1);
+        if constexpr (CAP) {
+          float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+          for (int c = 0; c < 64; c += 4) {
+            a0 = fmax3(a0, fabsf(sv[c]), fabsf(sv[c + 1]));
+            a1 = fmax3(a1, fabsf(sv[c + 2]), fabsf(sv[c + 3]));
+          }
+          amax = fmax3(amax, a0, a1);
+        }
       }
       int mode = kLogitPlain;
       if constexpr (CAP) {
-        const float amax = umax > -INFINITY ? fmaxf(umax, -umin) * p.kq : 0.f;
-        mode = __all_sync(0xffffffffu, amax <= kPolyMax5)   ? kLogitS5
-               : __all_sync(0xffffffffu, amax <= kPolyMax9) ? kLogitS9
-                                                            : kLogitTanh;
+        const float ay = amax * p.kq;
+        mode = __all_sync(0xffffffffu, ay <= kPolyMax5)   ? kLogitS5
+               : __all_sync(0xffffffffu, ay <= kPolyMax9) ? kLogitS9
+                                                          : kLogitTanh;
       }
       float mx = -INFINITY;
       if (umax > -INFINITY) {
@@ -469,26 +447,17 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       float ts = 0.f;
 #pragma unroll 1
       for (int c0 = 0; c0 < FBK; c0 += 64) {
-        const int k0 = chunk_kind(c0, jlo, jhi), k1 = chunk_kind(c0 + 32, jlo, jhi);
         float sv[64];
         uint32_t pw[32];
-        if (k0 != 1 || k1 != 1) {
-          tmem_ld32(s_addr + c0, sv);
-          tmem_ld32(s_addr + c0 + 32, sv + 32);
-          tmem_wait_ld();
-        }
+        tmem_ld32(s_addr + c0, sv);
+        tmem_ld32(s_addr + c0 + 32, sv + 32);
+        tmem_wait_ld();
         if constexpr (!CAP) {
-          ts += chunk_p<T, kLogitPlain>(k0, sv, c0, p, m_eff, jlo, jhi, pw);
-          ts += chunk_p<T, kLogitPlain>(k1, sv + 32, c0 + 32, p, m_eff, jlo, jhi, pw + 16);
-        } else if (mode == kLogitS5) {
-          ts += chunk_p<T, kLogitS5>(k0, sv, c0, p, m_eff, jlo, jhi, pw);
-          ts += chunk_p<T, kLogitS5>(k1, sv + 32, c0 + 32, p, m_eff, jlo, jhi, pw + 16);
-        } else if (mode == kLogitS9) {
-          ts += chunk_p<T, kLogitS9>(k0, sv, c0, p, m_eff, jlo, jhi, pw);
-          ts += chunk_p<T, kLogitS9>(k1, sv + 32, c0 + 32, p, m_eff, jlo, jhi, pw + 16);
+          ts += half_p<T, kLogitPlain>(interior, sv, c0, p, m_eff, jlo, jhi, pw);
         } else {
-          ts += chunk_p<T, kLogitTanh>(k0, sv, c0, p, m_eff, jlo, jhi, pw);
-          ts += chunk_p<T, kLogitTanh>(k1, sv + 32, c0 + 32, p, m_eff, jlo, jhi, pw + 16);
+          if (mode == kLogitS5) ts += half_p<T, kLogitS5>(interior, sv, c0, p, m_eff, jlo, jhi, pw);
+          else if (mode == kLogitS9) ts += half_p<T, kLogitS9>(interior, sv, c0, p, m_eff, jlo, jhi, pw);
+          else ts += half_p<T, kLogitTanh>(interior, sv, c0, p, m_eff, jlo, jhi, pw);
         }
         tmem_st16u(s_addr + c0 / 2, pw);
         tmem_st16u(s_addr + c0 / 2 + 16, pw + 16);

@@ -46,6 +46,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   return ok != 0;
 }
 
+// Non-blocking test: has the phase with parity `phase` completed?
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: gives up after about a second of polling (device global
 // timer), sets the CTA's abort flag and the device status word, and returns
 // false.  Once the abort flag is set every later wait returns false

@@ -21,6 +21,9 @@ GEOS = {
     # config-1 windows (128 per level) at head dim 64
     "d64": dict(B=1, N=1024, Hq=2, Hkv=2, Dk=64, Dv=64,
                 fmap={1: 128, 2: 256, 3: 384}, cache=512),
+    # BASELINE config 1 exactly: B=1, H=4, T=1024, Dk=Dv=64, 4 levels x 128
+    "config1": dict(B=1, N=1024, Hq=4, Hkv=4, Dk=64, Dv=64,
+                    fmap={1: 128, 2: 256, 3: 384}, cache=512),
     # head dim 128, GQA 2:1, four levels all live inside N
     "d128": dict(B=1, N=512, Hq=2, Hkv=1, Dk=128, Dv=128,
                  fmap={1: 64, 2: 128, 3: 192}, cache=256),
@@ -115,6 +118,8 @@ CASES = [
     case("bwd_rope_sink_d128_bf16", "bwd", "d128", dtype="bf16", position="rope",
          sink=True, softcap=30.0, seed=347),
     case("bwd_none_d128_bf16", "bwd", "d128", dtype="bf16", softcap=None, seed=348),
+    # BASELINE config 1 at its own shape: fp32, qk weights, no position, no softcap
+    case("bwd_config1", "bwd", "config1", softcap=None, seed=349),
     # incremental decode: prefill N - tail tokens, decode `tail`
     case("dec_plain_tiny", "decode", "tiny", tail=7, seed=500),
     case("dec_plain_evict", "decode", "evict", tail=40, seed=501),
