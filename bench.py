@@ -556,6 +556,114 @@ def c5_sharded_bench(args, dev, world, rank):
             "frac_of_peak": value / world / sustained, "peak_source": f"{src} bf16_tflops_sustained (per GPU)"}
 
 
+def config2_bench(args, dev, flush):
+    """BASELINE config 2, the full block forward: B=2, T=8192, H=16, D=128;
+    x ~ N(0, 1) of width 2048 and q / k / v = x W^T with random-init weights
+    (std 0.02; the projections are the caller's, made before the timed
+    region).  A step is the reference API's block: short causal K/V conv of
+    width 4, linear merge weights x w_proj^T, the dyadic tree, the rope forward
+    with softcap 30, the sink and the SiLU output gate.  Value: the attention's
+    visible-entry forward FLOPs (4 D per pair and head) over the block time;
+    the parts are timed with CUDA events."""
+    import torch
+
+    import telescope_cache_b200 as T
+    from telescope_cache_b200 import range_spec as R
+    B, N, H, D, L, W, K = 2, 8192, 16, 128, 6, 256, 4
+    fmap, cache = {l: l * W for l in range(1, L)}, L * W
+    g = torch.Generator(device=dev)
+    g.manual_seed(2002)
+    bf = torch.bfloat16
+    x = torch.randn(B, N, EMB, generator=g, device=dev, dtype=bf)
+    proj = [(0.02 * torch.randn(H * D, EMB, generator=g, device=dev)).to(bf) for _ in range(4)]
+    q, k, v = (x.matmul(w_.t()).reshape(B, N, H, D) for w_ in proj[:3])
+    gate_w = proj[3]
+    kcw = torch.randn(H * D, K, generator=g, device=dev) / math.sqrt(K)
+    vcw = torch.randn(H * D, K, generator=g, device=dev) / math.sqrt(K)
+    w_proj = (0.02 * torch.randn(H, EMB, generator=g, device=dev)).to(bf)
+    sinks = torch.randn(H, generator=g, device=dev)
+    cos, sin = T.rope_tables(N, D, device=dev)
+    pairs = R.visible_stats(R.RangeSpec.from_fmap(fmap, cache, N))[2]
+    fwd_flops = 4 * D * pairs * B * H
+    ev_names = ("tree", "forward", "sink_gate")
+
+    def step(evs=None):
+        if evs:
+            evs[0].record()
+        kl, vl, _ = T.build_dyadic_summaries(q, k, v, L - 1, x=x, w_proj=w_proj, k_conv_weight=kcw,
+                                             v_conv_weight=vcw)
+        packed = T.pack_levels(kl, vl)
+        if evs:
+            evs[1].record()
+        out, lse = T.multilevel_attention_forward(q, packed, fmap, cache, softcap=30.0, position_mode="rope",
+                                                  rope_cos=cos, rope_sin=sin)
+        if evs:
+            evs[2].record()
+        y = T.apply_output_gate(T.apply_attention_sink(out, lse, sinks), x, gate_w)
+        if evs:
+            evs[3].record()
+        return y
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    for e in evs:
+        flush.zero_()
+        step(e)
+    torch.cuda.synchronize()
+    parts = {n: sum(e[i].elapsed_time(e[i + 1]) for e in evs) / len(evs) for i, n in enumerate(ev_names)}
+    ms = sum(parts.values())
+    _, sustained, _, src = peaks()
+    return {"metric": "multilevel attn fwd TFLOP/s (visible-entry FLOPs) over the full block forward",
+            "value": fwd_flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "parts_ms": parts, "forward_tflops": fwd_flops / (parts["forward"] * 1e-3) / 1e12,
+            "config": {"workload": "c2", "B": B, "T": N, "H": H, "D": D, "levels": L, "window": W, "conv": K,
+                       "weights": "linear", "position": "rope", "softcap": 30.0, "sink": True,
+                       "gate": "SiLU", "fwd_flops": fwd_flops,
+                       "l2": "flushed between timed steps (256 MB write)"},
+            "peak_source": f"{src} bf16_tflops_sustained"}
+
+
+def builder_bench(args, wl, inp, flush):
+    """The dyadic builder alone at the workload's shapes (build_dyadic_summaries
+    + pack_levels: merge weights, merges, packing), W warm-up and K timed
+    calls with CUDA events, L2 flushed before each.  Algorithmic bytes: read
+    k, v (and q for qk weights, x for linear ones) once; write every packed
+    level of k and v and the packed weights once."""
+    import torch
+
+    import telescope_cache_b200 as T
+    L = wl["levels"] - 1
+    kw = {}
+    if wl["weights"] == "linear":
+        kw.update(x=inp["x"], w_proj=inp["w_proj"])
+
+    def call():
+        kl, vl, wl_ = T.build_dyadic_summaries(inp["q"], inp["k"], inp["v"], L, **kw)
+        return T.pack_levels(kl, vl)
+
+    for _ in range(max(args.warmup, 1)):
+        call()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for a, b in ev:
+        flush.zero_()
+        a.record()
+        call()
+        b.record()
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
+    B, N, H, D = wl["B"], wl["T"], wl["H"], wl["D"]
+    total = sum(N >> lv for lv in range(L + 1))
+    nbytes = 2 * B * N * H * D * 2 + 2 * B * total * H * D * 2 + B * total * H * 2
+    nbytes += B * N * H * D * 2 if wl["weights"] == "qk" else B * N * EMB * 2
+    _, _, hbm, src = peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"what": "build_dyadic_summaries + pack_levels", "ms": ms, "bytes": nbytes, "achieved_gbs": gbs,
+            "peak_gbs": hbm, "peak_source": f"{src} hbm_gbs", "frac": gbs / hbm}
+
+
 def cpu_reference_sample(wl, seconds_budget=20.0):
     """Time the CPU oracle (fwd + bwd) on a bounded sample of the workload:
     consecutive query rows of one (batch, head) slice, in the steady state
@@ -747,6 +855,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode", action="store_true",
                     help="skip the config-4 decode measurement added to the c3 line")
+    ap.add_argument("--no-c2", action="store_true",
+                    help="skip the config-2 block-forward measurement added to the c3 line")
     ap.add_argument("--no-c5-sharded", action="store_true",
                     help="skip the config-5 head-sharded (strong scaling) measurement added to the c3 line")
     ap.add_argument("--no-vjp", action="store_true",
@@ -893,6 +1003,11 @@ def main():
         _, dk_s, dv_s, _, _ = run_step(T, wl, inp, fmap, cache, tables)
         vjp = vjp_bench(T, wl, inp, (dk_s, dv_s), args, hbm, flush)
         del dk_s, dv_s
+    bld = builder_bench(args, wl, inp, flush)
+    c2 = None
+    if args.workload == "c3" and world == 1 and not args.no_c2:
+        c2 = config2_bench(args, dev, flush)
+        torch.cuda.empty_cache()
     c5s = None
     if args.workload == "c3" and not args.no_c5_sharded:
         c5s = c5_sharded_bench(args, dev, world, rank)
@@ -935,6 +1050,10 @@ def main():
         line["decode"] = dec
     if c5s is not None and rank == 0:
         line["c5_sharded"] = c5s
+    if rank == 0:
+        line["builder"] = bld
+    if c2 is not None and rank == 0:
+        line["config2"] = c2
     if rank == 0:
         print(json.dumps(line))
     if world > 1:

@@ -9,6 +9,10 @@ not grow with the problem:
   exactly the queries that see them; and the linear identity
   sum_nodes dV = sum_queries dO of every (batch, head) (each row of P sums
   to one);
+* config 2 (the full block forward: B=2, T=8192, H=16, q/k/v projected from
+  x, conv 4, linear merge weights, rope, sink, SiLU gate, softcap 30): the
+  gated output and lse of sampled rows of two (batch, head) slices against
+  the float64 oracle of the same block;
 * config 4 (batch 64, 32768-token prefill, rope, conv 4, sink, gate): the
   fused decode steps against the float64 oracle's full-sequence rows (conv,
   tree, rope forward, sink, gate) of sampled (batch, head) slices, and
@@ -133,7 +137,7 @@ def test_config3_full_size(dev):
         close(f"c3 dq {b},{h}", f64(dq[b, rows, h]), o_dq[0, rows, 0])
         close(f"c3 drel {b},{h}", f64(drel[b, rows, h]), o_drel[0, rows, 0])
         _check_nodes(f"c3 {b},{h}", dk, dv, b, h, qs, ks, vs, sl(dout), O.qk_weights(qs, ks), fmap, cache,
-                     50.0, p, L - 1, [(0, 4000), (0, 16383), (1, 6000), (3, 1500), (5, 250)])
+                     50.0, p, L - 1, [(0, 4000), (0, 16383), (1, 7935), (2, 3711), (3, 1599), (4, 543), (5, 15)])
 
 
 def test_config5_full_size(dev):
@@ -166,7 +170,42 @@ def test_config5_full_size(dev):
         close(f"c5 lse {h}", f64(lse[0, rows, h]), o_lse[0, rows, 0])
         close(f"c5 dq {h}", f64(dq[0, rows, h]), o_dq[0, rows, 0])
         _check_nodes(f"c5 {h}", dk, dv, 0, h, sl(q), sl(k), sl(v), sl(dout), w, fmap, cache, 50.0, p, L - 1,
-                     [(0, 70000), (0, 131071), (2, 20000), (5, 3000), (7, 400)])
+                     [(0, 131071), (1, 65023), (2, 31999), (3, 15487), (5, 3103), (7, 7)])
+
+
+def test_config2_block_forward_full_size(dev):
+    B, N, H, D, L, W, K, E = 2, 8192, 16, 128, 6, 256, 4, 2048
+    fmap, cache = {l: l * W for l in range(1, L)}, L * W
+    g = torch.Generator(device=dev)
+    g.manual_seed(202)
+    bf = torch.bfloat16
+    x = torch.randn(B, N, E, generator=g, device=dev, dtype=bf)
+    wq, wk, wv, wg = ((0.02 * torch.randn(H * D, E, generator=g, device=dev)).to(bf) for _ in range(4))
+    q, k, v = (x.matmul(w_.t()).reshape(B, N, H, D) for w_ in (wq, wk, wv))
+    kcw = torch.randn(H * D, K, generator=g, device=dev) / math.sqrt(K)
+    vcw = torch.randn(H * D, K, generator=g, device=dev) / math.sqrt(K)
+    w_proj = (0.02 * torch.randn(H, E, generator=g, device=dev)).to(bf)
+    sinks = torch.randn(H, generator=g, device=dev)
+    cos, sin = T.rope_tables(N, D, device=dev)
+    kl, vl, _ = T.build_dyadic_summaries(q, k, v, L - 1, x=x, w_proj=w_proj, k_conv_weight=kcw,
+                                         v_conv_weight=vcw)
+    out, lse = T.multilevel_attention_forward(q, T.pack_levels(kl, vl), fmap, cache, softcap=30.0,
+                                              position_mode="rope", rope_cos=cos, rope_sin=sin)
+    y = T.apply_output_gate(T.apply_attention_sink(out, lse, sinks), x, wg)
+    ocos, osin = O.rope_tables(N, D)
+    opos = O.Positional("rope", cos=ocos, sin=osin)
+    rows = [0, 255, 1000, 4097, 8191]
+    for b, h in ((0, 3), (1, 14)):
+        sl = lambda t: f64(t[b:b + 1, :, h:h + 1])  # noqa: E731
+        kc = O.short_conv(sl(k).reshape(1, N, D), f64(kcw[h * D:(h + 1) * D])).reshape(1, N, 1, D)
+        vc = O.short_conv(sl(v).reshape(1, N, D), f64(vcw[h * D:(h + 1) * D])).reshape(1, N, 1, D)
+        w = O.linear_weights(f64(x[b:b + 1]), f64(w_proj[h:h + 1]))
+        kl_o, vl_o, _ = O.build_tree(kc, vc, w, L - 1)
+        o_out, o_lse = O.forward(sl(q), kl_o, vl_o, fmap, cache, 30.0, opos, rows=rows)
+        sunk = O.sink_forward(o_out[:, rows], o_lse[:, rows], f64(sinks[h:h + 1]))
+        gated = O.output_gate(sunk, f64(x[b:b + 1, rows]), f64(wg[h * D:(h + 1) * D]))
+        close(f"c2 gated out {b},{h}", f64(y[b, rows, h]), gated[0, :, 0])
+        close(f"c2 lse {b},{h}", f64(lse[b, rows, h]), o_lse[0, rows, 0])
 
 
 def test_config4_decode_equals_forward(dev):
