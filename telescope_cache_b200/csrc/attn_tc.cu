@@ -190,14 +190,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- MMA issuer ----------------
       constexpr uint32_t kIdQK = idesc_f16(128, BK, Pack2<T>::kFmt, 0, 0);
       constexpr uint32_t kIdPV = idesc_f16(128, 128, Pack2<T>::kFmt, 0, 1);
-      const uint32_t qa = smem_addr(q_s), pa = smem_addr(p_s);
+      const uint32_t pa = smem_addr(p_s);
+      const uint64_t qd = sdesc_sw128(smem_addr(q_s), 16, 1024);
       auto issue_pv = [&](int t) {
-        const uint32_t va = smem_addr(v_s + (t % NS) * Sh::KVTILE);
-        const uint32_t pb = pa + (t % NP) * Sh::PTILE;
+        const uint64_t vd = sdesc_sw128(smem_addr(v_s + (t % NS) * Sh::KVTILE), Sh::KVBLK, 1024);
+        const uint64_t pd = sdesc_sw128(pa + (t % NP) * Sh::PTILE, 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128(pb + (kk >> 2) * QBLK + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(va + kk * 2048, Sh::KVBLK, 1024);
+          const uint64_t ad = sdesc_add(pd, (kk >> 2) * QBLK + (kk & 3) * 32);
+          const uint64_t bd = sdesc_add(vd, kk * 2048);
           mma_f16(tmem + Sh::O_COL, ad, bd, kIdPV, (t > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(&p_empty[t % NP]);
@@ -213,11 +214,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&kv_full[st], (j / NS) & 1, abort_flag, status)) { alive = false; break; }
         if (j >= 2 && !mbar_wait(&s_free[bb], ((j >> 1) - 1) & 1, abort_flag, status)) { alive = false; break; }
         tc_fence_after();
-        const uint32_t ka = smem_addr(k_s + st * Sh::KVTILE);
+        const uint64_t kd = sdesc_sw128(smem_addr(k_s + st * Sh::KVTILE), 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = sdesc_sw128(qa + (kk >> 2) * QBLK + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(ka + (kk >> 2) * Sh::KVBLK + (kk & 3) * 32, 16, 1024);
+          const uint64_t ad = sdesc_add(qd, (kk >> 2) * QBLK + (kk & 3) * 32);
+          const uint64_t bd = sdesc_add(kd, (kk >> 2) * Sh::KVBLK + (kk & 3) * 32);
           mma_f16(tmem + bb * BK, ad, bd, kIdQK, kk > 0 ? 1u : 0u);
         }
         mma_commit(&s_full[bb]);

@@ -212,10 +212,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t xa = smem_addr(x_s);
       auto issue_dq = [&](int t) {
         const uint32_t ka = smem_addr(k_s + (t % NKV) * T64), xb = xa + (t % NX) * 128 * 128;
+        const uint64_t xd = sdesc_sw128(xb, 16, 1024), kd = sdesc_sw128(ka, B64, 1024);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_f16(tmem + 256, sdesc_sw128(xb + kk * 32, 16, 1024), sdesc_sw128(ka + kk * 2048, B64, 1024), kIdQ,
-                  (t > 0 || kk > 0) ? 1u : 0u);
+          mma_f16(tmem + 256, sdesc_add(xd, kk * 32), sdesc_add(kd, kk * 2048), kIdQ, (t > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&x_free[t % NX]);
         mma_commit(&kv_empty[t % NKV]);
       };
@@ -229,18 +229,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&kv_full[st], (j / NKV) & 1, abort_flag, status)) { alive = false; break; }
         if (j >= 2 && !mbar_wait(&s_free[bb], ((j >> 1) - 1) & 1, abort_flag, status)) { alive = false; break; }
         tc_fence_after();
-        const uint32_t ka = smem_addr(k_s + st * T64), va = smem_addr(v_s + st * T64);
+        const uint64_t kd = sdesc_sw128(smem_addr(k_s + st * T64), 16, 1024);
+        const uint64_t vd = sdesc_sw128(smem_addr(v_s + st * T64), 16, 1024);
         // A = Q / dO from TMEM (8 columns = 16 head dims per K step)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t bo = (kk >> 2) * B64 + (kk & 3) * 32;
-          mma_f16_ta(tmem + bb * 64, tmem + kColQ + 8 * kk, sdesc_sw128(ka + bo, 16, 1024), kIdS, kk > 0 ? 1u : 0u);
+          mma_f16_ta(tmem + bb * 64, tmem + kColQ + 8 * kk, sdesc_add(kd, bo), kIdS, kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t bo = (kk >> 2) * B64 + (kk & 3) * 32;
-          mma_f16_ta(tmem + 128 + bb * 64, tmem + kColG + 8 * kk, sdesc_sw128(va + bo, 16, 1024), kIdS,
-                     kk > 0 ? 1u : 0u);
+          mma_f16_ta(tmem + 128 + bb * 64, tmem + kColG + 8 * kk, sdesc_add(vd, bo), kIdS, kk > 0 ? 1u : 0u);
         }
         mma_commit(&s_full[bb]);
         if (j >= 1) {
@@ -555,15 +555,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t kIdS = idesc_f16(128, 64, Pack2<T>::kFmt, 0, 0);
       constexpr uint32_t kIdA = idesc_f16(128, 128, Pack2<T>::kFmt, 0, 1);
-      const uint32_t ka = smem_addr(k_s), va = smem_addr(v_s), pa = smem_addr(pt_s), xa = smem_addr(xt_s);
+      const uint32_t pa = smem_addr(pt_s), xa = smem_addr(xt_s);
+      const uint64_t kd0 = sdesc_sw128(smem_addr(k_s), 16, 1024), vd0 = sdesc_sw128(smem_addr(v_s), 16, 1024);
       auto issue_acc = [&](int t) {
-        const uint32_t qa = smem_addr(q_s + (t % NQ) * T64), ga = smem_addr(g_s + (t % NQ) * T64);
-        const uint32_t pb = pa + (t % NX) * 128 * 128, xb = xa + (t % NX) * 128 * 128;
+        const uint64_t qd = sdesc_sw128(smem_addr(q_s + (t % NQ) * T64), B64, 1024);
+        const uint64_t gd = sdesc_sw128(smem_addr(g_s + (t % NQ) * T64), B64, 1024);
+        const uint64_t pd = sdesc_sw128(pa + (t % NX) * 128 * 128, 16, 1024);
+        const uint64_t xd = sdesc_sw128(xa + (t % NX) * 128 * 128, 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-          mma_f16(tmem + 256, sdesc_sw128(pb + kk * 32, 16, 1024), sdesc_sw128(ga + kk * 2048, B64, 1024), kIdA, acc);
-          mma_f16(tmem + 384, sdesc_sw128(xb + kk * 32, 16, 1024), sdesc_sw128(qa + kk * 2048, B64, 1024), kIdA, acc);
+          mma_f16(tmem + 256, sdesc_add(pd, kk * 32), sdesc_add(gd, kk * 2048), kIdA, acc);
+          mma_f16(tmem + 384, sdesc_add(xd, kk * 32), sdesc_add(qd, kk * 2048), kIdA, acc);
         }
         mma_commit(&x_free[t % NX]);
         mma_commit(&q_empty[t % NQ]);
@@ -581,18 +584,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&q_full[st], (i / NQ) & 1, abort_flag, status)) { alive = false; break; }
         if (i >= 2 && !mbar_wait(&s_free[bb], ((i >> 1) - 1) & 1, abort_flag, status)) { alive = false; break; }
         tc_fence_after();
-        const uint32_t qa = smem_addr(q_s + st * T64), ga = smem_addr(g_s + st * T64);
+        const uint64_t qd = sdesc_sw128(smem_addr(q_s + st * T64), 16, 1024);
+        const uint64_t gd = sdesc_sw128(smem_addr(g_s + st * T64), 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t ao = (kk >> 2) * B128 + (kk & 3) * 32, bo = (kk >> 2) * B64 + (kk & 3) * 32;
-          mma_f16(tmem + bb * 64, sdesc_sw128(ka + ao, 16, 1024), sdesc_sw128(qa + bo, 16, 1024), kIdS,
-                  kk > 0 ? 1u : 0u);
+          mma_f16(tmem + bb * 64, sdesc_add(kd0, ao), sdesc_add(qd, bo), kIdS, kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t ao = (kk >> 2) * B128 + (kk & 3) * 32, bo = (kk >> 2) * B64 + (kk & 3) * 32;
-          mma_f16(tmem + 128 + bb * 64, sdesc_sw128(va + ao, 16, 1024), sdesc_sw128(ga + bo, 16, 1024), kIdS,
-                  kk > 0 ? 1u : 0u);
+          mma_f16(tmem + 128 + bb * 64, sdesc_add(vd0, ao), sdesc_add(gd, bo), kIdS, kk > 0 ? 1u : 0u);
         }
         mma_commit(&s_full[bb]);
         if (i >= 1) {

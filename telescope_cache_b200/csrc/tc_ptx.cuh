@@ -286,6 +286,11 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
   return d;
 }
 
+// The descriptor of the same operand `byte_off` bytes further on (the start
+// address field holds address / 16 in its low 14 bits; shared-memory offsets
+// stay below 2^18 bytes, so the add never carries out of the field).
+__device__ __forceinline__ uint64_t sdesc_add(uint64_t d, uint32_t byte_off) { return d + (byte_off >> 4); }
+
 // kind::f16 instruction descriptor: f32 accumulator, A/B format (0 f16,
 // 1 bf16), K-major (0) or MN-major (1) operands, M x N tile.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_fmt, int a_mn, int b_mn) {
