@@ -344,7 +344,7 @@ def decode_bench(args, dev, world, with_e2e=True):
     kcw = torch.randn(H * D, c["conv"], generator=g, device=dev) / math.sqrt(c["conv"])
     vcw = torch.randn(H * D, c["conv"], generator=g, device=dev) / math.sqrt(c["conv"])
     steps = args.warmup + args.steps
-    cos, sin = T.rope_tables(N + steps + args.steps + 1, D, device=dev)
+    cos, sin = T.rope_tables(N + 2 * steps + 1, D, device=dev)
     sinks = torch.randn(H, generator=g, device=dev)
     gate_w = (0.02 * torch.randn(H * D, EMB, generator=g, device=dev)).to(bf)
     q = torch.randn(B, N, H, D, generator=g, device=dev, dtype=bf)
@@ -422,25 +422,33 @@ def decode_bench(args, dev, world, with_e2e=True):
                     bufs[slot][k_].copy_(t_[i], non_blocking=True)
                 evs[slot].record(s_in)
 
-        sync()
-        a.record(st)  # continues at t_first + K with the same token values
-        upload(args.warmup, 0)
-        for n, i in enumerate(range(args.warmup, steps)):
-            slot = n & 1
-            if i + 1 < steps:
-                upload(i + 1, slot ^ 1)
-            st.wait_event(evs[slot])
-            d_ = bufs[slot]
-            out, _ = T.decode_step(d_["x"], d_["q"], d_["k"], d_["v"], state, **kw)
-            used[slot].record(st)
-            s_out.wait_stream(st)
-            with torch.cuda.stream(s_out):
-                out.record_stream(s_out)
-                out_host.copy_(out, non_blocking=True)
-        st.wait_stream(s_out)  # the last read-back inside the timed region
-        b.record(st)
-        sync()
-        ems = a.elapsed_time(b) / args.steps
+        def pipelined(idx):
+            """decode_step over the tokens idx, inputs uploaded and outputs read
+            back per step; returns ms per step (events on the compute stream)."""
+            sync()
+            a.record(st)
+            upload(idx[0], 0)
+            for n in range(len(idx)):
+                slot = n & 1
+                if n + 1 < len(idx):
+                    upload(idx[n + 1], slot ^ 1)
+                st.wait_event(evs[slot])
+                d_ = bufs[slot]
+                out, _ = T.decode_step(d_["x"], d_["q"], d_["k"], d_["v"], state, **kw)
+                used[slot].record(st)
+                s_out.wait_stream(st)
+                with torch.cuda.stream(s_out):
+                    out.record_stream(s_out)
+                    out_host.copy_(out, non_blocking=True)
+            st.wait_stream(s_out)  # the last read-back inside the timed region
+            b.record(st)
+            sync()
+            return a.elapsed_time(b) / len(idx)
+
+        # the state continues at t_first + K with the same token values
+        if args.warmup:
+            pipelined(list(range(args.warmup)))
+        ems = pipelined(list(range(args.warmup, steps)))
         if world > 1:
             tm = torch.tensor([ems], device=dev)
             dist.all_reduce(tm, op=dist.ReduceOp.MAX)

@@ -16,7 +16,7 @@ from typing import Dict, List, Optional, Tuple
 import torch
 
 from .. import _lib
-from ..range_spec import (RangeSpec, activation_times_from_fmap, level_row_bounds, normalize_empty,
+from ..range_spec import (RangeSpec, activation_times_from_fmap, level_row_bounds,
                           range_bounds)
 from .position import compute_relative_states, positional_args, check_relative_bins
 from .summaries import _check_conv_weight, compute_linear_weights, short_conv
@@ -240,8 +240,8 @@ def _check_tick(state: DecodeState, t: int):
     """The schedule invariants the reference asserts at every step
     (reference.py:2036-2082): at most one level fires, its children are live
     at t-1, and no level exceeds its ring capacity at t.  Every level's range
-    of a row comes from one pass of the closed forms (level_row_bounds), so a
-    step costs two such passes, not one per level."""
+    of a row comes from one pass of the closed forms; the ranges of query t
+    are memoised for the next step's check of t - 1."""
     a = state.activation_times
     fired = None
     for level in range(1, len(a)):
@@ -264,18 +264,31 @@ def _check_tick(state: DecodeState, t: int):
                 f"level {level} needs {hi - lo} live slots > cap {state.caps[level]} at t={t}")
 
 
+_BOUNDS_MEMO: Dict[Tuple, list] = {}
+
+
 def _checked_bounds(state: DecodeState, q: int, seq_len: int):
     """range_bounds(spec(seq_len), q, level) for every level at once: the
-    normalised ranges of query q with the reference's level-length check."""
+    normalised ranges of query q with the reference's level-length check.
+    The last two results per schedule are memoised (a step checks t - 1 and
+    t; the next step checks t and t + 1)."""
     if not 0 <= q < seq_len:
         raise ValueError(f"q={q} out of range [0, {seq_len})")
+    key = (state.activation_times, state.cache_size, q, seq_len)
+    hit = _BOUNDS_MEMO.get(key)
+    if hit is not None:
+        return hit
     out = []
     for level, (lo, hi) in enumerate(level_row_bounds(q, state.activation_times, state.cache_size)):
-        lo, hi = normalize_empty((lo, hi))
+        if lo >= hi:
+            lo = hi = 0
         if hi > seq_len >> level:
             raise AssertionError(
                 f"range [{lo},{hi}) exceeds level_len={seq_len >> level} at q={q}, level={level}")
         out.append((lo, hi))
+    if len(_BOUNDS_MEMO) >= 64:
+        _BOUNDS_MEMO.clear()
+    _BOUNDS_MEMO[key] = out
     return out
 
 
@@ -303,6 +316,44 @@ def _ensure_rotated_ring(state: DecodeState, cos, sin):
     return state.k_rot
 
 
+_WORKSPACE: Dict[Tuple, torch.Tensor] = {}
+
+
+def _workspace(device, stream, numel):
+    """The split-attention scratch (partial softmax states): one buffer per
+    device, stream and size, reused by the steps issued on that stream (which
+    run in issue order, so they never overlap)."""
+    key = (device, stream.value, numel)
+    ws = _WORKSPACE.get(key)
+    if ws is None:
+        if len(_WORKSPACE) >= 32:
+            _WORKSPACE.clear()
+        ws = torch.empty(numel, device=device, dtype=torch.float32)
+        _WORKSPACE[key] = ws
+    return ws
+
+
+def _static_args(state: DecodeState, Hq: int):
+    """The fields of tc_decode_args that depend only on the state (dims,
+    dtypes, schedule, ring pointers), built once per state and copied into
+    each call's struct."""
+    key = (Hq, state.k.data_ptr(), state.v.data_ptr(), state.w.data_ptr(), state.k.dtype, state.w.dtype,
+           tuple(state.k.shape), tuple(state.v.shape))
+    cached = getattr(state, "_args_proto", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    B, _, Hkv, Dk = state.k.shape
+    proto = _lib.DecodeArgs(
+        B=B, Hq=Hq, Hkv=Hkv, Dk=Dk, Dv=state.v.shape[-1], dtype=_lib.dtype_code(state.k.dtype),
+        w_dtype=_lib.dtype_code(state.w.dtype), num_levels=state.num_levels, cache_size=state.cache_size,
+        act=(ctypes.c_int32 * _lib.MAX_LEVELS)(*state.activation_times),
+        caps=(ctypes.c_int32 * _lib.MAX_LEVELS)(*state.caps),
+        ring_off=(ctypes.c_int32 * (_lib.MAX_LEVELS + 1))(*state.ring_offsets),
+        ring_k=state.k.data_ptr(), ring_v=state.v.data_ptr(), ring_w=state.w.data_ptr())
+    object.__setattr__(state, "_args_proto", (key, proto))
+    return proto
+
+
 def _decode_launch(state: DecodeState, mode, q_t, k_t=None, v_t=None, w_t=None, kcw=None, vcw=None,
                    softcap=None, position_mode="none", cos=None, sin=None, rel_states=None,
                    rel_proj=None, sinks=None, gate_pre=None, t=None, want_kv=False, k_rot=None):
@@ -321,12 +372,11 @@ def _decode_launch(state: DecodeState, mode, q_t, k_t=None, v_t=None, w_t=None, 
     lse = torch.empty(B, 1, Hq, device=q_t.device, dtype=torch.float32)
     k_new = torch.empty(B, 1, Hkv, Dk, device=q_t.device, dtype=dtype) if want_kv else None
     v_new = torch.empty(B, 1, Hkv, Dv, device=q_t.device, dtype=dtype) if want_kv else None
-    L1 = state.num_levels
+    stream = _lib.stream_of(q_t)
     ws = None
     if Dk == 128 and Dv == 128 and dtype in (torch.bfloat16, torch.float16):
         # scratch for splitting each (batch, KV head)'s entries over CTAs
-        ws = torch.empty(B * Hkv * DECODE_MAX_SPLITS * (Hq // Hkv) * 130, device=q_t.device,
-                         dtype=torch.float32)
+        ws = _workspace(q_t.device, stream, B * Hkv * DECODE_MAX_SPLITS * (Hq // Hkv) * 130)
     conv_w = 0 if kcw is None else kcw.shape[1]
     if kcw is not None:
         kcw = kcw.contiguous()
@@ -342,28 +392,35 @@ def _decode_launch(state: DecodeState, mode, q_t, k_t=None, v_t=None, w_t=None, 
         keep.append(t_)
         return t_.data_ptr()
 
-    args = _lib.DecodeArgs(
-        mode=mode, B=B, Hq=Hq, Hkv=Hkv, Dk=Dk, Dv=Dv, dtype=_lib.dtype_code(dtype),
-        w_dtype=_lib.dtype_code(state.w.dtype), t=state.t if t is None else t, num_levels=L1,
-        cache_size=state.cache_size,
-        act=(ctypes.c_int32 * _lib.MAX_LEVELS)(*state.activation_times),
-        caps=(ctypes.c_int32 * _lib.MAX_LEVELS)(*state.caps),
-        ring_off=(ctypes.c_int32 * (_lib.MAX_LEVELS + 1))(*state.ring_offsets),
-        ring_k=state.k.data_ptr(), ring_v=state.v.data_ptr(), ring_w=state.w.data_ptr(),
-        conv_k=p(state.conv_k) if conv_w else None, conv_v=p(state.conv_v) if conv_w else None,
-        k_conv_w=p(kcw), v_conv_w=p(vcw), conv_dtype=_lib.dtype_code(kcw.dtype) if conv_w else 0,
-        conv_k_width=conv_w, q_t=p(qc), k_t=p(kc), v_t=p(vc), w_t=p(w_t),
-        has_softcap=0 if softcap is None else 1, softcap=0.0 if softcap is None else float(softcap),
-        position_mode=_lib.POS[position_mode], rope_cos=p(cos), rope_sin=p(sin),
-        rel_states=p(rel_states), rel_proj=p(rel_proj),
-        rel_dtype=_lib.dtype_code(rel_states.dtype) if rel_states is not None else 0,
-        d_rel=0 if rel_states is None else rel_states.shape[-1],
-        rel_bins=0 if rel_proj is None else rel_proj.shape[1], sinks=p(sinks),
-        sink_dtype=_lib.dtype_code(sinks.dtype) if sinks is not None else 0, gate_pre=p(gate_pre),
-        gate_dtype=_lib.dtype_code(gate_pre.dtype) if gate_pre is not None else 0,
-        out=out.data_ptr(), lse=lse.data_ptr(), k_new=p(k_new), v_new=p(v_new),
-        workspace=p(ws), workspace_floats=0 if ws is None else ws.numel(), ring_k_rot=p(k_rot))
-    _lib.launch("tc_decode_step", q_t.device, ctypes.byref(args), _lib.stream_of(q_t))
+    args = _lib.DecodeArgs()
+    ctypes.pointer(args)[0] = _static_args(state, Hq)
+    args.mode = mode
+    args.t = state.t if t is None else t
+    if conv_w:
+        args.conv_k, args.conv_v = p(state.conv_k), p(state.conv_v)
+        args.k_conv_w, args.v_conv_w = p(kcw), p(vcw)
+        args.conv_dtype = _lib.dtype_code(kcw.dtype)
+        args.conv_k_width = conv_w
+    args.q_t, args.k_t, args.v_t, args.w_t = p(qc), p(kc), p(vc), p(w_t)
+    args.has_softcap = 0 if softcap is None else 1
+    args.softcap = 0.0 if softcap is None else float(softcap)
+    args.position_mode = _lib.POS[position_mode]
+    args.rope_cos, args.rope_sin = p(cos), p(sin)
+    if rel_states is not None:
+        args.rel_states, args.rel_proj = p(rel_states), p(rel_proj)
+        args.rel_dtype = _lib.dtype_code(rel_states.dtype)
+        args.d_rel = rel_states.shape[-1]
+        args.rel_bins = rel_proj.shape[1]
+    if sinks is not None:
+        args.sinks, args.sink_dtype = p(sinks), _lib.dtype_code(sinks.dtype)
+    if gate_pre is not None:
+        args.gate_pre, args.gate_dtype = p(gate_pre), _lib.dtype_code(gate_pre.dtype)
+    args.out, args.lse = out.data_ptr(), lse.data_ptr()
+    args.k_new, args.v_new = p(k_new), p(v_new)
+    if ws is not None:
+        args.workspace, args.workspace_floats = ws.data_ptr(), ws.numel()
+    args.ring_k_rot = p(k_rot)
+    _lib.launch("tc_decode_step", q_t.device, ctypes.byref(args), stream)
     del keep
     return out, lse, k_new, v_new
 
