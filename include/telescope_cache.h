@@ -200,6 +200,37 @@ int tc_short_conv_bwd(int32_t B, int32_t N, int32_t C, int32_t dtype, const void
                       int32_t w_dtype, const void* w, const float* dy, void* dx, float* dw, float* partials,
                       int64_t partial_floats, void* stream);
 
+/* Projection epilogues of tc_linear */
+#define TC_LIN_STORE 0  /* out = A B^T                                  */
+#define TC_LIN_GATE 1   /* out = SiLU(A B^T) * aux (aux: out's type)    */
+
+/* out[m, n] = sum_k A[m, k] B[n, k] (x @ W^T) for row-major A [M, K] (row
+ * stride lda), B [N, K] (ldb) and out [M, N] (ldo), fp32 accumulation; with
+ * TC_LIN_GATE, out = SiLU(A B^T) * aux for aux [M, N] (ld_aux, out's type).
+ * Replaces the x.matmul(W.t()) of compute_linear_weights (reference.py:148-164),
+ * compute_relative_states (reference.py:374-395), apply_output_gate
+ * (reference.py:1187-1219, gate and product fused) and the relative-bias
+ * logits states @ proj (reference.py:764-767).  bf16/f16 operands of one type
+ * (lda, ldb multiples of 8, 16-byte aligned) run on the tensor cores with an
+ * output of that type or f32; other types run a SIMT kernel.  dev_status
+ * (optional) receives TC_DEV_WAIT_TIMEOUT if a bounded wait gave up. */
+int tc_linear(int64_t M, int32_t N, int32_t K, int32_t a_dtype, const void* a, int64_t lda,
+              int32_t b_dtype, const void* b, int64_t ldb, int32_t out_dtype, void* out, int64_t ldo,
+              int32_t epilogue, const void* aux, int64_t ld_aux, int32_t* dev_status, void* stream);
+
+/* out[n1, n2] = sum_m A[m, n1] B[m, n2] for row-major A [M, N1] and B [M, N2]
+ * (the weight gradient dW = dy^T x of a projection, autograd of
+ * x @ W^T in reference.py:148-164 and :1187-1219), fp32 accumulation,
+ * deterministic (row chunks reduced in order).  bf16/f16 operands of one
+ * type run on the tensor cores (B read in place, A transposed into the
+ * scratch), others on a SIMT kernel.  scratch: caller-owned, 16-byte
+ * aligned, tc_linear_wgrad_scratch_floats(M, N1, N2) floats (0: none).
+ * dev_status (optional) as for tc_linear. */
+int64_t tc_linear_wgrad_scratch_floats(int64_t M, int32_t N1, int32_t N2);
+int tc_linear_wgrad(int64_t M, int32_t N1, int32_t N2, int32_t a_dtype, const void* a, int64_t lda,
+                    int32_t b_dtype, const void* b, int64_t ldb, int32_t out_dtype, void* out, int64_t ldo,
+                    float* scratch, int64_t scratch_floats, int32_t* dev_status, void* stream);
+
 /* w[b, t, h] = x[b, t, :] . w_proj[h, :] (compute_linear_weights,
  * reference.py:148-164).  x [rows, E], w_proj [H, E], out [rows, H]. */
 int tc_linear_weights(int64_t rows, int32_t E, int32_t H, int32_t x_dtype, const void* x,

@@ -17,6 +17,7 @@ MAX_LEVELS = 16
 
 TC_OK, TC_ERR_ARG, TC_ERR_UNSUPPORTED, TC_ERR_CUDA, TC_ERR_SCHEDULE = 0, 1, 2, 3, 4
 TC_F32, TC_BF16, TC_F16 = 0, 1, 2
+TC_LIN_STORE, TC_LIN_GATE = 0, 1
 POS = {"none": 0, "rope": 1, "relative": 2}
 DECODE_FULL, DECODE_ADVANCE, DECODE_ATTEND, DECODE_ROTATE = 0, 1, 2, 3
 
@@ -114,6 +115,11 @@ SIGNATURES = {
     "tc_short_conv_bwd": [_c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_i32, _c_i32, _c_vp, _c_vp, _c_vp, _c_vp,
                           _c_vp, _c_i64, _c_vp],
     "tc_linear_weights": [_c_i64, _c_i32, _c_i32, _c_i32, _c_vp, _c_i32, _c_vp, _c_i32, _c_vp, _c_vp],
+    "tc_linear": [_c_i64, _c_i32, _c_i32, _c_i32, _c_vp, _c_i64, _c_i32, _c_vp, _c_i64, _c_i32, _c_vp, _c_i64,
+                  _c_i32, _c_vp, _c_i64, _c_vp, _c_vp],
+    "tc_linear_wgrad": [_c_i64, _c_i32, _c_i32, _c_i32, _c_vp, _c_i64, _c_i32, _c_vp, _c_i64, _c_i32, _c_vp,
+                        _c_i64, _c_vp, _c_i64, _c_vp, _c_vp],
+    "tc_linear_wgrad_scratch_floats": [_c_i64, _c_i32, _c_i32],
     "tc_qk_weights": [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_vp, _c_i32, _c_vp,
                       _c_vp],
     "tc_short_conv": [_c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_i32, _c_i32, _c_vp, _c_vp, _c_vp],
@@ -150,6 +156,7 @@ def lib():
         handle.tc_launch_count.argtypes = []
         handle.tc_launch_count.restype = ctypes.c_int64
         handle.tc_tree_bwd_scratch_bytes.restype = ctypes.c_int64
+        handle.tc_linear_wgrad_scratch_floats.restype = ctypes.c_int64
         _LIB = handle
     return _LIB
 

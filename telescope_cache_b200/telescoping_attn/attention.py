@@ -20,6 +20,7 @@ from typing import Dict, Optional
 import torch
 
 from .. import _lib
+from .linear import linear
 from ..range_spec import RangeSpec, native_schedule, visible_stats
 from .packing import PackedKV
 from .position import _rope_into, check_relative_bins, positional_args
@@ -57,18 +58,17 @@ def _relative_band(st, pj, max_visible, dtype):
     """Bias logits rel[row, REL_PAD + d] = states[row] . proj[:, d] for every
     distance d a query can reach (< max_visible), in the kernels' element
     type, with REL_PAD zero columns on both sides -- the operand of the
-    tensor-core relative path.  One plain GEMM (cuBLAS through torch)."""
+    tensor-core relative path.  One tc_linear launch: states [rows, d_rel]
+    times the padded table (as [width, d_rel] rows), fp32 accumulation,
+    rounded once to the kernels' type."""
     d_rel, bins = pj.shape
     reach = min(bins, max_visible)
     width = (reach + 2 * REL_PAD + 7) // 8 * 8
     proj_pad = torch.zeros(d_rel, width, device=pj.device, dtype=pj.dtype)
     proj_pad[:, REL_PAD:REL_PAD + reach] = pj[:, :reach]
     rows = st.reshape(-1, d_rel)
-    if st.dtype == dtype and pj.dtype == dtype:
-        band = rows.matmul(proj_pad)  # exact products, fp32 accumulation
-    else:
-        band = rows.float().matmul(proj_pad.float()).to(dtype)
-    return band.contiguous(), width
+    band = linear(rows, proj_pad.t().contiguous(), out_dtype=dtype)
+    return band, width
 
 
 # The relative band of a forward, kept for the backward of the same call:

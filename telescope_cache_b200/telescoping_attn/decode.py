@@ -8,6 +8,7 @@ from typing import Optional, Tuple
 import torch
 
 from .. import _lib
+from .linear import linear
 from .decode_state import (DecodeState, _check_tick, _decode_launch, _ensure_rotated_ring, _rot_key,
                            _validate_advance)
 from .position import check_relative_bins, compute_relative_states, positional_args
@@ -145,7 +146,7 @@ def decode_step(
         if tuple(gate_weight.shape) != (Hq * Dv, x_t.shape[-1]):
             raise ValueError(
                 f"gate_weight shape {tuple(gate_weight.shape)} != {(Hq * Dv, x_t.shape[-1])}")
-        gate_pre = x_t.matmul(gate_weight.t()).reshape(B, Hq * Dv).contiguous()
+        gate_pre = linear(x_t, gate_weight).reshape(B, Hq * Dv)
     _check_tick(state, t)
     k_rot = _ensure_rotated_ring(state, cos, sin) if position_mode == "rope" else None
     out, lse, _, _ = _decode_launch(

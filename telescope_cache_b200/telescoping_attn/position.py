@@ -9,6 +9,7 @@ from typing import Optional, Tuple
 import torch
 
 from .. import _lib
+from .linear import project
 from ..range_spec import IntOps, RangeSpec, elem_mask, range_bounds, visible_stats
 
 
@@ -98,14 +99,14 @@ def relative_bin_distance(spec: RangeSpec, q: int, level: int, k_local: int) -> 
 
 def compute_relative_states(x: torch.Tensor, relative_weight: torch.Tensor, Hq: int) -> torch.Tensor:
     """relative_states [B, N, Hq, d_rel] = x @ relative_weight^T, reshaped
-    (reference.py:374-395).  A plain GEMM (cuBLAS through torch.matmul)."""
+    (reference.py:374-395), on tc_linear (gradients included)."""
     B, N, E = x.shape
     rows, Ew = relative_weight.shape
     if Ew != E or rows % Hq != 0:
         raise ValueError(
             f"relative_weight shape {tuple(relative_weight.shape)} incompatible with "
             f"emb_dim={E}, Hq={Hq}")
-    return x.matmul(relative_weight.t()).reshape(B, N, Hq, rows // Hq)
+    return project(x, relative_weight).reshape(B, N, Hq, rows // Hq)
 
 
 def positional_args(position_mode, rope_cos, rope_sin, relative_states, relative_proj, *,

@@ -8,6 +8,7 @@ from typing import Tuple
 import torch
 
 from .. import _lib
+from .linear import linear, project
 
 
 def _sink_fwd(out, lse, sinks):
@@ -108,8 +109,10 @@ class _Gate(torch.autograd.Function):
 
 def apply_output_gate(out: torch.Tensor, x: torch.Tensor, gate_weight: torch.Tensor) -> torch.Tensor:
     """SiLU(x @ gate_weight^T).reshape(B, N, Hq, Dv) * out
-    (reference.py:1187-1219).  The projection is a plain GEMM (cuBLAS via
-    torch.matmul); SiLU and the product run in one CUDA kernel."""
+    (reference.py:1187-1219).  Without gradients: one tc_linear launch with
+    SiLU and the product in its epilogue.  With gradients: the projection on
+    tc_linear (Projection, whose backward is also this library's), then the
+    SiLU-product kernel, which keeps the pre-activation for its backward."""
     B, N, Hq, Dv = out.shape
     if x.dim() != 3 or x.shape[0] != B or x.shape[1] != N:
         raise ValueError(
@@ -118,7 +121,10 @@ def apply_output_gate(out: torch.Tensor, x: torch.Tensor, gate_weight: torch.Ten
     if tuple(gate_weight.shape) != (Hq * Dv, x.shape[-1]):
         raise ValueError(f"gate_weight shape {tuple(gate_weight.shape)} != {(Hq * Dv, x.shape[-1])}")
     _lib.require_cuda(out, x, gate_weight)
-    g = x.matmul(gate_weight.t()).reshape(B, N, Hq, Dv)
+    grad = torch.is_grad_enabled() and (out.requires_grad or x.requires_grad or gate_weight.requires_grad)
+    if not grad and out.dtype == torch.result_type(x, gate_weight):
+        return linear(x, gate_weight, gate_out=out).reshape(B, N, Hq, Dv)
+    g = project(x, gate_weight).reshape(B, N, Hq, Dv)
     return _Gate.apply(out, g)
 
 

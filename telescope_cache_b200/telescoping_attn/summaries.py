@@ -20,6 +20,7 @@ from typing import Optional
 import torch
 
 from .. import _lib
+from . import linear as _proj
 
 
 def _contig(t):
@@ -52,8 +53,8 @@ def compute_linear_weights(x: torch.Tensor, w_proj: torch.Tensor) -> torch.Tenso
     assert E == Ew
     _lib.require_cuda(x, w_proj)
     if x.dtype == w_proj.dtype:
-        # the reference's own op: one plain GEMM (cuBLAS through torch)
-        return x.matmul(w_proj.t()).unsqueeze(-1)
+        # the reference's x @ w_proj^T (with its gradients) on tc_linear
+        return _proj.project(x, w_proj).unsqueeze(-1)
     x, w_proj = _contig(x), _contig(w_proj)
     out = torch.empty(B, N, Hkv, 1, device=x.device, dtype=torch.result_type(x, w_proj))
     _lib.launch("tc_linear_weights", x.device,
@@ -229,13 +230,14 @@ def build_dyadic_summaries_backward(q, k, v, num_summary_levels, k_packed, v_pac
     dq_out = torch.zeros_like(q) if dq is None else dq.to(q.dtype)
     dx = dwp = None
     if dw0 is not None:
-        # w0 = x @ w_proj^T: two plain GEMMs (cuBLAS through torch, fp32
-        # accumulation) in the inputs' precision, as autograd runs them on
-        # the reference's x @ w_proj^T; dw0 is rounded to that precision first
+        # w0 = x @ w_proj^T: dx = g w_proj (tc_linear) and dw_proj = g^T x
+        # (tc_linear_wgrad), fp32 accumulation, results rounded to the
+        # inputs' precision as autograd's products on the reference's
+        # x @ w_proj^T are; dw0 is rounded to that precision first
         ct = torch.promote_types(x.dtype, w_proj.dtype)
-        g = dw0.to(ct)
-        dx = g.matmul(w_proj.to(ct)).to(x.dtype)
-        dwp = g.reshape(-1, Hkv).t().matmul(x.reshape(-1, x.shape[-1]).to(ct)).to(w_proj.dtype)
+        g = dw0.to(ct).reshape(-1, Hkv)
+        dx = _proj.linear(g, w_proj.to(ct).t().contiguous()).to(x.dtype).reshape(x.shape)
+        dwp = _proj.linear_wgrad(g, x.reshape(-1, x.shape[-1]).to(ct), ct).to(w_proj.dtype)
     dkcw = dvcw = None
     if conv:
         dk, dkcw = _short_conv_vjp(k, kcw, dk0)
