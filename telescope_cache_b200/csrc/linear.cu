@@ -10,18 +10,20 @@
 // Tensor-core path (A and B both bf16 or both f16, row strides multiples of
 // 8 elements, 16-byte aligned bases): a persistent kernel; CTA b takes the
 // 128-row x BN-column tiles b, b + G, ... of C.
-//   warp 0      TMA producer: K-blocks A [128 x 64] and B [BN x 64]
-//               (128-byte swizzle, no multicast) into an NS-stage ring that
-//               runs on across tiles
+//   warps 0, 2  TMA producers of A and B: K-blocks [128 x 64] and [BN x 64]
+//               (128-byte swizzle, no multicast), up to four per instruction
+//               (3-D boxes), into an NS-stage ring that runs on across tiles
 //   warp 1      MMA issuer: tcgen05.mma kind::f16 (both operands K-major),
 //               fp32 accumulators [128 x BN] double buffered in TMEM, so a
 //               tile's epilogue overlaps the next tile's main loop
-//   warps 2-5   epilogue: warp w owns TMEM lanes 32 (w % 4) .. + 31, one C
-//   (2-9)       row per thread (with 8 warps, two per lane quadrant, each
+//   warps 4-7   epilogue: warp w owns TMEM lanes 32 (w % 4) .. + 31, one C
+//   (4-11)      row per thread (with 8 warps, two per lane quadrant, each
 //               half of the columns); the epilogue is applied and the rows go
 //               out through shared memory and TMA stores (rows of 128 bytes
 //               and wider) or with 16-byte stores.
-// Rows and columns past M / N read as zeros (TMA bounds) and are not stored.
+// Rows and columns past M / N read as zeros (TMA bounds; when M < 128 the A
+// box stops at M rounded up to 8, and the MMA rows beyond it read stale
+// shared memory) and are never stored.
 // Other element types (fp32, mixed) run a tiled SIMT kernel with fp32
 // accumulation in ascending K order.
 //
@@ -46,29 +48,35 @@ constexpr int kLinThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue 
 
 template <int BN, int OSZ>
 struct LinCfg {
-  static constexpr int TA = LM * LK * 2, TB = BN * LK * 2;
+  static constexpr int TA = LM * LK * 2, TB = BN * LK * 2;  // one K-block of A, of B
+  // K-blocks per stage: a TMA instruction costs its issuing thread several
+  // hundred cycles whatever its size, so narrow tiles (little MMA work per
+  // K-block) load four K-blocks per instruction (3-D boxes); A and B have a
+  // producer each
+  static constexpr int KBM = BN <= 32 ? 4 : 1;
+  static constexpr int SA = KBM * TA, SB = KBM * TB;
   // rows of 128 bytes or more go out through shared memory and TMA stores
   static constexpr bool kTmaStore = BN * OSZ >= 128;
   // epilogue warps: two per TMEM lane quadrant (each half the columns) when a
   // row of the tile holds 256 bytes or more, else one
   static constexpr int kEpi = BN * OSZ >= 256 ? 8 : 4;
-  static constexpr int kThr = 64 + 32 * kEpi;
+  // warp 0 A loads, 1 MMA, 2 B loads, 3 idle, 4 .. 4 + kEpi - 1 epilogue
+  static constexpr int kThr = 128 + 32 * kEpi;
   static constexpr int BW = BN / (kEpi / 4);  // columns per epilogue warp
   // per epilogue warp kSlabs slabs of 32 rows in 128-byte column blocks (4 KB
-  // each), two for 16-bit outputs so a slab is rewritten only after the
-  // stores of the tile before last have read it
-  static constexpr int kSlabs = kTmaStore ? (OSZ == 2 ? 2 : 1) : 0;
+  // each), two for 16-bit outputs of tiles up to 128 wide so a slab is
+  // rewritten only after the stores of the tile before last have read it
+  static constexpr int kSlabs = kTmaStore ? (OSZ == 2 && BN <= 128 ? 2 : 1) : 0;
   static constexpr int kSlab = kTmaStore ? 32 * BW * OSZ : 0;
-  // as many K-block stages as fit in 200 KB (up to 12): narrow tiles keep
-  // more loads in flight
-  static constexpr int NS0 = (200 * 1024 - kEpi * kSlabs * kSlab) / (TA + TB);
+  // as many stages as fit in 220 KB (up to 12)
+  static constexpr int NS0 = (220 * 1024 - kEpi * kSlabs * kSlab) / (SA + SB);
   static constexpr int NS = NS0 > 12 ? 12 : (NS0 < 2 ? 2 : NS0);
-  static constexpr int kSmem = NS * (TA + TB) + kEpi * kSlabs * kSlab + 1024 + 256;
+  static constexpr int kSmem = NS * (SA + SB) + kEpi * kSlabs * kSlab + 1024 + 256;
   static constexpr int kCols = 2 * BN < 32 ? 32 : 2 * BN;  // two accumulators (power of two >= 32)
   static constexpr int CW = BN < 32 ? BN : 32;             // epilogue columns per TMEM load
 };
-static_assert(LinCfg<128, 4>::kSmem <= 227 * 1024 && LinCfg<128, 2>::kSmem <= 227 * 1024 &&
-                  LinCfg<16, 4>::kSmem <= 227 * 1024,
+static_assert(LinCfg<256, 2>::kSmem <= 227 * 1024 && LinCfg<128, 4>::kSmem <= 227 * 1024 &&
+                  LinCfg<128, 2>::kSmem <= 227 * 1024 && LinCfg<16, 4>::kSmem <= 227 * 1024,
               "projection shared memory exceeds the per-CTA limit");
 
 struct LinParams {
@@ -80,6 +88,11 @@ struct LinParams {
   const void* aux;  // TC_LIN_GATE: the tensor multiplied by SiLU(C), output type, row stride ld_aux
   int64_t ld_aux;
   int tma_store;    // out is TMA-addressable (16-byte aligned base and row stride)
+  int rot;          // tile t walks its K-blocks from block t mod nk on (few row blocks: the CTAs,
+                    // which all read the same A rows, then do not read the same block at once)
+  int a_rows;       // rows of A's TMA box: 128, or M rounded up to 8 when M < 128 (the MMA's
+                    // rows past the box read stale shared memory; their results are not stored)
+  int kb;           // K-blocks per stage load: KBM with 3-D maps (K a multiple of 64), else 1
   int32_t* status;
 };
 
@@ -158,26 +171,27 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
   using C = LinCfg<BN, OSZ>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* a_s = sm;                   // [NS] A K-blocks
-  uint8_t* b_s = a_s + C::NS * C::TA;  // [NS] B K-blocks
-  uint8_t* o_s = b_s + C::NS * C::TB;  // [kEpi][kSlabs] epilogue slabs (TMA stores)
+  uint8_t* a_s = sm;                   // [NS] A stages (KBM K-blocks of a_rows x 128 B)
+  uint8_t* b_s = a_s + C::NS * C::SA;  // [NS] B stages (KBM K-blocks of BN x 128 B)
+  uint8_t* o_s = b_s + C::NS * C::SB;  // [kEpi][kSlabs] epilogue slabs (TMA stores)
   uint64_t* bars = reinterpret_cast<uint64_t*>(o_s + C::kEpi * C::kSlabs * C::kSlab);
-  uint64_t* full = bars;               // [NS]
+  uint64_t* full = bars;               // [NS] (both producers arrive)
   uint64_t* empty = full + C::NS;      // [NS]
   uint64_t* acc_full = empty + C::NS;  // [2] accumulator complete
   uint64_t* acc_empty = acc_full + 2;  // [2] accumulator drained by the epilogue
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   static_assert((2 * C::NS + 4) * 8 + 8 <= 256, "barrier area");
-  static_assert(C::kSlab % 1024 == 0 && (C::NS * (C::TA + C::TB)) % 1024 == 0, "slab alignment (128-byte swizzle)");
+  static_assert(C::kSlab % 1024 == 0 && (C::NS * (C::SA + C::SB)) % 1024 == 0, "slab alignment (128-byte swizzle)");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = (p.K + LK - 1) / LK;
+  const int nst = (nk + p.kb - 1) / p.kb;  // stage loads per tile
   const int64_t G = gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::NS; ++i) {
-      mbar_init(&full[i], 1);
+      mbar_init(&full[i], 2);
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -201,29 +215,35 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == 0) {
+  if (warp == 0 || warp == 2) {
+    // producers: warp 0 loads A, warp 2 loads B, into the same stages
     if (lane == 0) {
-      int64_t kc = 0;  // K-blocks issued, across tiles
+      const bool is_a = warp == 0;
+      const CUtensorMap* map = is_a ? &ta : &tb;
+      uint8_t* base = is_a ? a_s : b_s;
+      const int sbytes = is_a ? C::SA : C::SB;
+      const uint32_t bytes = (uint32_t)((is_a ? p.a_rows : BN) * LK * 2 * p.kb);
+      int64_t sc = 0;  // stage loads issued, across tiles
       bool alive = true;
       for (int64_t t = blockIdx.x; t < ntiles && alive; t += G) {
-        const int n0 = (int)(t % ntn) * BN;
-        const int m0 = (int)(t / ntn) * LM;
-        for (int kb = 0; kb < nk; ++kb, ++kc) {
-          const int s = (int)(kc % C::NS);
-          if (kc >= C::NS && !mbar_wait(&empty[s], (uint32_t)((kc / C::NS) - 1) & 1, abort_flag, p.status)) {
+        const int row0 = is_a ? (int)(t / ntn) * LM : (int)(t % ntn) * BN;
+        for (int st = 0; st < nst; ++st, ++sc) {
+          const int s = (int)(sc % C::NS);
+          if (sc >= C::NS && !mbar_wait(&empty[s], (uint32_t)((sc / C::NS) - 1) & 1, abort_flag, p.status)) {
             alive = false;
             break;
           }
-          mbar_expect_tx(&full[s], C::TA + C::TB);
-          tma_load_2d(a_s + s * C::TA, &ta, kb * LK, m0, &full[s]);
-          tma_load_2d(b_s + s * C::TB, &tb, kb * LK, n0, &full[s]);
+          const int sq = p.rot ? (int)((st + t) % nst) : st;
+          mbar_expect_tx(&full[s], bytes);
+          if (p.kb > 1) tma_load_3d(base + s * sbytes, map, 0, row0, sq * p.kb, &full[s]);
+          else tma_load_2d(base + s * sbytes, map, sq * LK, row0, &full[s]);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t kId = idesc_f16(128, BN, Pack2<T>::kFmt, 0, 0);
-      int64_t kc = 0;
+      int64_t sc = 0;
       bool alive = true;
       int i = 0;
       for (int64_t t = blockIdx.x; t < ntiles && alive; t += G, ++i) {
@@ -231,26 +251,33 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
         if (i >= 2 && !mbar_wait(&acc_empty[ab], ((i >> 1) - 1) & 1, abort_flag, p.status)) break;
         tc_fence_after();
         const uint32_t acc = tmem + ab * BN;
-        for (int kb = 0; kb < nk; ++kb, ++kc) {
-          const int s = (int)(kc % C::NS);
-          if (!mbar_wait(&full[s], (uint32_t)(kc / C::NS) & 1, abort_flag, p.status)) {
+        for (int st = 0; st < nst; ++st, ++sc) {
+          const int s = (int)(sc % C::NS);
+          if (!mbar_wait(&full[s], (uint32_t)(sc / C::NS) & 1, abort_flag, p.status)) {
             alive = false;
             break;
           }
           tc_fence_after();
-          const uint64_t ad = sdesc_sw128(smem_addr(a_s + s * C::TA), 16, 1024);
-          const uint64_t bd = sdesc_sw128(smem_addr(b_s + s * C::TB), 16, 1024);
-          const int ks = min(LK / 16, (p.K - kb * LK + 15) / 16);  // K steps of 16 holding data
-          for (int kk = 0; kk < ks; ++kk)
-            mma_f16(acc, sdesc_add(ad, kk * 32), sdesc_add(bd, kk * 32), kId, (kb > 0 || kk > 0) ? 1u : 0u);
+          const int sq = p.rot ? (int)((st + t) % nst) : st;
+          const int kb0 = sq * p.kb, kbs = min(p.kb, nk - kb0);
+          const uint64_t ad0 = sdesc_sw128(smem_addr(a_s + s * C::SA), 16, 1024);
+          const uint64_t bd0 = sdesc_sw128(smem_addr(b_s + s * C::SB), 16, 1024);
+          for (int j = 0; j < kbs; ++j) {
+            const uint64_t ad = sdesc_add(ad0, (uint32_t)(j * p.a_rows * LK * 2));
+            const uint64_t bd = sdesc_add(bd0, (uint32_t)(j * C::TB));
+            const int ks = min(LK / 16, (p.K - (kb0 + j) * LK + 15) / 16);  // K steps of 16 holding data
+            for (int kk = 0; kk < ks; ++kk)
+              mma_f16(acc, sdesc_add(ad, kk * 32), sdesc_add(bd, kk * 32), kId,
+                      (st > 0 || j > 0 || kk > 0) ? 1u : 0u);
+          }
           mma_commit(&empty[s]);
         }
         if (alive) mma_commit(&acc_full[ab]);
       }
     }
-  } else {
+  } else if (warp >= 4) {
     const int quad = warp & 3;  // TMEM lanes of this warp: 32 quad .. 32 quad + 31
-    const int ew = warp - 2;    // epilogue warp: columns [cb, cb + BW) of each tile
+    const int ew = warp - 4;    // epilogue warp: columns [cb, cb + BW) of each tile
     const int cb = (ew >> 2) * C::BW;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const bool via_tma = C::kTmaStore && p.tma_store;
@@ -344,6 +371,23 @@ int make_map_2d(CUtensorMap* m, const void* base, int dt, int64_t rows, int64_t 
   return r == CUDA_SUCCESS ? TC_OK : TC_ERR_CUDA;
 }
 
+// [rows, K] 16-bit row-major matrix (K a multiple of 64) as a 3-D map
+// (k in block, row, K-block) with 64 x box_rows x kb boxes: one box is kb
+// consecutive K-blocks, each a [box_rows x 128 B] swizzled tile.
+int make_map_kblocks(CUtensorMap* m, const void* base, int dt, int64_t rows, int64_t K, int64_t ld, int box_rows,
+                     int kb) {
+  auto fn = encode_fn();
+  if (!fn) return TC_ERR_CUDA;
+  const CUtensorMapDataType t = dt == TC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[3] = {(cuuint64_t)LK, (cuuint64_t)rows, (cuuint64_t)(K / LK)};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(LK * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)LK, (cuuint32_t)box_rows, (cuuint32_t)kb};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, t, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TC_OK : TC_ERR_CUDA;
+}
+
 constexpr int kMaxDev = 64;
 
 int current_device() {
@@ -366,9 +410,17 @@ int launch_lin_tc(const void* a, int64_t lda, const void* b, int64_t ldb, int dt
                   cudaStream_t st) {
   using C = LinCfg<BN, (int)sizeof(OT)>;
   CUtensorMap ta, tb, to;
-  if (int rc = make_map_2d(&ta, a, dt, p.M, p.K, lda, LK, LM)) return rc;
-  if (int rc = make_map_2d(&tb, b, dt, p.N, p.K, ldb, LK, BN)) return rc;
+  p.a_rows = p.M < LM ? (int)((p.M + 7) / 8 * 8) : LM;
+  p.kb = (C::KBM > 1 && p.K % LK == 0) ? C::KBM : 1;
+  if (p.kb > 1) {
+    if (int rc = make_map_kblocks(&ta, a, dt, p.M, p.K, lda, p.a_rows, p.kb)) return rc;
+    if (int rc = make_map_kblocks(&tb, b, dt, p.N, p.K, ldb, BN, p.kb)) return rc;
+  } else {
+    if (int rc = make_map_2d(&ta, a, dt, p.M, p.K, lda, LK, p.a_rows)) return rc;
+    if (int rc = make_map_2d(&tb, b, dt, p.N, p.K, ldb, LK, BN)) return rc;
+  }
   p.tma_store = 0;
+  p.rot = (p.M + LM - 1) / LM < 8 ? 1 : 0;
   memset(&to, 0, sizeof(to));
   if (C::kTmaStore && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && (p.ldo * (int64_t)sizeof(OT)) % 16 == 0) {
     if (int rc = make_map_2d(&to, p.out, odt, p.M, p.N, p.ldo, 128 / (int)sizeof(OT), 32)) return rc;
@@ -394,14 +446,19 @@ int launch_lin_tc(const void* a, int64_t lda, const void* b, int64_t ldb, int dt
   return launch_status();
 }
 
-// Widest tile that still gives every SM a tile.
+// Widest tile that still gives every SM a tile.  256 columns only for
+// 16-bit outputs (whose epilogue slabs leave room for three stages) and
+// K > 64: with one K-block per tile the kernel is bound by its stores, which
+// the double-buffered slabs of the 128-column tile drain faster.
 template <typename T, typename OT>
 int launch_lin_tc_bn(const void* a, int64_t lda, const void* b, int64_t ldb, int dt, int odt, const LinParams& p,
                      cudaStream_t st) {
   const int64_t mt = (p.M + LM - 1) / LM;
   const int64_t sms = sm_count(current_device());
-  int bn = p.N > 64 ? 128 : p.N > 32 ? 64 : p.N > 16 ? 32 : 16;
+  int bn = p.N > 128 && sizeof(OT) == 2 && p.K > LK ? 256 : p.N > 64 ? 128 : p.N > 32 ? 64 : p.N > 16 ? 32 : 16;
   while (bn > 16 && mt * ((p.N + bn - 1) / bn) < sms) bn >>= 1;
+  if constexpr (sizeof(OT) == 2)
+    if (bn == 256) return launch_lin_tc<T, OT, 256>(a, lda, b, ldb, dt, odt, p, st);
   if (bn == 128) return launch_lin_tc<T, OT, 128>(a, lda, b, ldb, dt, odt, p, st);
   if (bn == 64) return launch_lin_tc<T, OT, 64>(a, lda, b, ldb, dt, odt, p, st);
   if (bn == 32) return launch_lin_tc<T, OT, 32>(a, lda, b, ldb, dt, odt, p, st);
@@ -708,6 +765,9 @@ extern "C" int tc_linear(int64_t M, int32_t N, int32_t K, int32_t a_dtype, const
   p.aux = aux;
   p.ld_aux = ld_aux;
   p.tma_store = 0;
+  p.rot = 0;
+  p.a_rows = LM;
+  p.kb = 1;
   p.status = dev_status;
   const bool tc_ok = a_dtype == b_dtype && a_dtype != TC_F32 && (out_dtype == a_dtype || out_dtype == TC_F32) &&
                      lda % 8 == 0 && ldb % 8 == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
