@@ -212,11 +212,17 @@ int tc_short_conv_bwd(int32_t B, int32_t N, int32_t C, int32_t dtype, const void
  * (reference.py:1187-1219, gate and product fused) and the relative-bias
  * logits states @ proj (reference.py:764-767).  bf16/f16 operands of one type
  * (lda, ldb multiples of 8, 16-byte aligned) run on the tensor cores with an
- * output of that type or f32; other types run a SIMT kernel.  dev_status
- * (optional) receives TC_DEV_WAIT_TIMEOUT if a bounded wait gave up. */
+ * output of that type or f32; other types run a SIMT kernel.  With few
+ * row blocks and a long K (a decode-time projection) the tensor-core path
+ * splits K and needs caller-owned, 16-byte aligned fp32 scratch of
+ * tc_linear_scratch_floats(M, N, K, out_dtype) floats (0: none); with less
+ * it runs unsplit.  dev_status (optional) receives TC_DEV_WAIT_TIMEOUT if a
+ * bounded wait gave up. */
+int64_t tc_linear_scratch_floats(int64_t M, int32_t N, int32_t K, int32_t out_dtype);
 int tc_linear(int64_t M, int32_t N, int32_t K, int32_t a_dtype, const void* a, int64_t lda,
               int32_t b_dtype, const void* b, int64_t ldb, int32_t out_dtype, void* out, int64_t ldo,
-              int32_t epilogue, const void* aux, int64_t ld_aux, int32_t* dev_status, void* stream);
+              int32_t epilogue, const void* aux, int64_t ld_aux, float* scratch, int64_t scratch_floats,
+              int32_t* dev_status, void* stream);
 
 /* out[n1, n2] = sum_m A[m, n1] B[m, n2] for row-major A [M, N1] and B [M, N2]
  * (the weight gradient dW = dy^T x of a projection, autograd of

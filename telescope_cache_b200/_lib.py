@@ -116,7 +116,8 @@ SIGNATURES = {
                           _c_vp, _c_i64, _c_vp],
     "tc_linear_weights": [_c_i64, _c_i32, _c_i32, _c_i32, _c_vp, _c_i32, _c_vp, _c_i32, _c_vp, _c_vp],
     "tc_linear": [_c_i64, _c_i32, _c_i32, _c_i32, _c_vp, _c_i64, _c_i32, _c_vp, _c_i64, _c_i32, _c_vp, _c_i64,
-                  _c_i32, _c_vp, _c_i64, _c_vp, _c_vp],
+                  _c_i32, _c_vp, _c_i64, _c_vp, _c_i64, _c_vp, _c_vp],
+    "tc_linear_scratch_floats": [_c_i64, _c_i32, _c_i32, _c_i32],
     "tc_linear_wgrad": [_c_i64, _c_i32, _c_i32, _c_i32, _c_vp, _c_i64, _c_i32, _c_vp, _c_i64, _c_i32, _c_vp,
                         _c_i64, _c_vp, _c_i64, _c_vp, _c_vp],
     "tc_linear_wgrad_scratch_floats": [_c_i64, _c_i32, _c_i32],
@@ -157,6 +158,7 @@ def lib():
         handle.tc_launch_count.restype = ctypes.c_int64
         handle.tc_tree_bwd_scratch_bytes.restype = ctypes.c_int64
         handle.tc_linear_wgrad_scratch_floats.restype = ctypes.c_int64
+        handle.tc_linear_scratch_floats.restype = ctypes.c_int64
         _LIB = handle
     return _LIB
 

@@ -93,7 +93,22 @@ struct LinParams {
   int a_rows;       // rows of A's TMA box: 128, or M rounded up to 8 when M < 128 (the MMA's
                     // rows past the box read stale shared memory; their results are not stored)
   int kb;           // K-blocks per stage load: KBM with 3-D maps (K a multiple of 64), else 1
+  int ksplit;       // K split over ksplit tile sets (few tiles, long K); each writes fp32
+  int nkp;          // partial sums of nkp K-blocks to part [ksplit][M][N], reduced afterwards
+  float* part;
   int32_t* status;
+};
+
+// Tile t of the split grid: K part, row block, column block (columns fastest).
+struct LinTile {
+  int n0, m0, kpart;
+  __device__ LinTile(int64_t t, int ntn, int64_t mt, int BN) {
+    const int64_t per = (int64_t)ntn * mt;
+    kpart = (int)(t / per);
+    const int64_t r = t - (int64_t)kpart * per;
+    n0 = (int)(r % ntn) * BN;
+    m0 = (int)(r / ntn) * LM;
+  }
 };
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
@@ -186,7 +201,12 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = (p.K + LK - 1) / LK;
-  const int nst = (nk + p.kb - 1) / p.kb;  // stage loads per tile
+  const int64_t mt = (p.M + LM - 1) / LM;
+  // K-blocks [kstart, kend) of split part kp, in stage loads of kb
+  const auto krange = [&](int kp, int* kstart, int* kend) {
+    *kstart = kp * p.nkp;
+    *kend = min(nk, *kstart + p.nkp);
+  };
   const int64_t G = gridDim.x;
 
   if (threadIdx.x == 0) {
@@ -226,7 +246,11 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
       int64_t sc = 0;  // stage loads issued, across tiles
       bool alive = true;
       for (int64_t t = blockIdx.x; t < ntiles && alive; t += G) {
-        const int row0 = is_a ? (int)(t / ntn) * LM : (int)(t % ntn) * BN;
+        const LinTile tl(t, ntn, mt, BN);
+        const int row0 = is_a ? tl.m0 : tl.n0;
+        int ks0, ke0;
+        krange(tl.kpart, &ks0, &ke0);
+        const int nst = (ke0 - ks0 + p.kb - 1) / p.kb;
         for (int st = 0; st < nst; ++st, ++sc) {
           const int s = (int)(sc % C::NS);
           if (sc >= C::NS && !mbar_wait(&empty[s], (uint32_t)((sc / C::NS) - 1) & 1, abort_flag, p.status)) {
@@ -234,9 +258,10 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
             break;
           }
           const int sq = p.rot ? (int)((st + t) % nst) : st;
+          const int kq = ks0 + sq * p.kb;
           mbar_expect_tx(&full[s], bytes);
-          if (p.kb > 1) tma_load_3d(base + s * sbytes, map, 0, row0, sq * p.kb, &full[s]);
-          else tma_load_2d(base + s * sbytes, map, sq * LK, row0, &full[s]);
+          if (p.kb > 1) tma_load_3d(base + s * sbytes, map, 0, row0, kq, &full[s]);
+          else tma_load_2d(base + s * sbytes, map, kq * LK, row0, &full[s]);
         }
       }
     }
@@ -247,6 +272,10 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
       bool alive = true;
       int i = 0;
       for (int64_t t = blockIdx.x; t < ntiles && alive; t += G, ++i) {
+        const LinTile tl(t, ntn, mt, BN);
+        int ks0, ke0;
+        krange(tl.kpart, &ks0, &ke0);
+        const int nst = (ke0 - ks0 + p.kb - 1) / p.kb;
         const int ab = i & 1;
         if (i >= 2 && !mbar_wait(&acc_empty[ab], ((i >> 1) - 1) & 1, abort_flag, p.status)) break;
         tc_fence_after();
@@ -259,7 +288,7 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
           }
           tc_fence_after();
           const int sq = p.rot ? (int)((st + t) % nst) : st;
-          const int kb0 = sq * p.kb, kbs = min(p.kb, nk - kb0);
+          const int kb0 = ks0 + sq * p.kb, kbs = min(p.kb, ke0 - kb0);
           const uint64_t ad0 = sdesc_sw128(smem_addr(a_s + s * C::SA), 16, 1024);
           const uint64_t bd0 = sdesc_sw128(smem_addr(b_s + s * C::SB), 16, 1024);
           for (int j = 0; j < kbs; ++j) {
@@ -283,8 +312,8 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
     const bool via_tma = C::kTmaStore && p.tma_store;
     int i = 0;
     for (int64_t t = blockIdx.x; t < ntiles; t += G, ++i) {
-      const int n0 = (int)(t % ntn) * BN;
-      const int m0 = (int)(t / ntn) * LM;
+      const LinTile tl(t, ntn, mt, BN);
+      const int n0 = tl.n0, m0 = tl.m0;
       const int64_t row = (int64_t)m0 + quad * 32 + lane;
       const int ab = i & 1;
       uint8_t* slab = o_s + (ew * C::kSlabs + (C::kSlabs > 1 ? (i & 1) : 0)) * C::kSlab;
@@ -304,6 +333,22 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
         if constexpr (C::CW == 32) tmem_ld32(tmem + lane_base + ab * BN + c0, v);
         else tmem_ld16(tmem + lane_base + ab * BN + c0, v);
         tmem_wait_ld();
+        if (p.part) {
+          // split K: this part's fp32 partial sums, the epilogue comes with their reduction
+          if (row < p.M) {
+            float* o = p.part + ((int64_t)tl.kpart * p.M + row) * p.N + n0 + c0;
+            const int cnt = min(C::CW, p.N - n0 - c0);
+            if (cnt == C::CW && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+              for (int e = 0; e < C::CW; e += 4) *reinterpret_cast<float4*>(o + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < C::CW; ++e)
+                if (e < cnt) o[e] = v[e];
+            }
+          }
+          continue;
+        }
         if (p.epi == TC_LIN_GATE && row < p.M) gate_chunk<OT, C::CW>(p, row, n0 + c0, v);
         if (via_tma) {
           if constexpr (C::kTmaStore) {
@@ -405,6 +450,69 @@ int sm_count(int dev) {
   return n;
 }
 
+// out[m, n] = epilogue(sum over the K parts of part[., m, n]), parts in order;
+// four columns per thread, the parts' loads issued together.
+__global__ void lin_reduce_kernel(int64_t M, int N, int parts, const float* part, int epi, const void* aux,
+                                  int64_t ld_aux, int odt, void* out, int64_t ldo) {
+  const int64_t total = M * N;
+  const int64_t i0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i0 >= total) return;
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  if (i0 + 4 <= total && (total & 3) == 0) {
+    int c = 0;
+    for (; c + 4 <= parts; c += 4) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float4*>(part + (int64_t)(c + u) * total + i0);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) s[0] += v[u].x, s[1] += v[u].y, s[2] += v[u].z, s[3] += v[u].w;
+    }
+    for (; c < parts; ++c) {
+      const float4 v = *reinterpret_cast<const float4*>(part + (int64_t)c * total + i0);
+      s[0] += v.x, s[1] += v.y, s[2] += v.z, s[3] += v.w;
+    }
+  } else {
+    for (int c = 0; c < parts; ++c)
+      for (int e = 0; e < 4 && i0 + e < total; ++e) s[e] += part[(int64_t)c * total + i0 + e];
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int64_t i = i0 + e;
+    if (i >= total) break;
+    const int64_t m = i / N;
+    const int n = (int)(i - m * N);
+    float x = s[e];
+    if (epi == TC_LIN_GATE) x = silu(x) * load_any(aux, m * ld_aux + n, odt);
+    store_any(out, m * ldo + n, odt, x);
+  }
+}
+
+// Tile width before the fill-the-SMs narrowing (see launch_lin_tc_bn).
+int lin_bn0(int N, int K, int osz) {
+  return N > 128 && osz == 2 && K > LK ? 256 : N > 64 ? 128 : N > 32 ? 64 : N > 16 ? 32 : 16;
+}
+
+// Split K when the tile grid is small and K long (a decode-time projection:
+// few rows): about 148 tiles with at least two K-blocks (a multiple of the
+// stage's K-blocks) per part.  One MMA per 16 K of a narrow tile costs about
+// as much to issue as one of a wide tile, so wide tiles with split K beat
+// narrow tiles with long K loops.
+void lin_split(int64_t M, int N, int K, int bn, int* parts, int* nkp) {
+  const int64_t tiles = ((M + LM - 1) / LM) * ((N + bn - 1) / bn);
+  const int nk = (K + LK - 1) / LK;
+  const int kb = (bn <= 32 && K % LK == 0) ? 4 : 1;
+  *parts = 1;
+  *nkp = nk;
+  if (tiles >= 74 || nk < 8) return;
+  const int64_t want = (148 + tiles - 1) / tiles;
+  const int s = (int)(nk / 2 < want ? nk / 2 : want);
+  if (s < 2) return;
+  int per = (nk + s - 1) / s;
+  per = (per + kb - 1) / kb * kb;
+  *nkp = per;
+  *parts = (nk + per - 1) / per;
+}
+
 template <typename T, typename OT, int BN>
 int launch_lin_tc(const void* a, int64_t lda, const void* b, int64_t ldb, int dt, int odt, LinParams p,
                   cudaStream_t st) {
@@ -420,9 +528,10 @@ int launch_lin_tc(const void* a, int64_t lda, const void* b, int64_t ldb, int dt
     if (int rc = make_map_2d(&tb, b, dt, p.N, p.K, ldb, LK, BN)) return rc;
   }
   p.tma_store = 0;
-  p.rot = (p.M + LM - 1) / LM < 8 ? 1 : 0;
+  p.rot = (p.M + LM - 1) / LM < 8 && p.ksplit == 1 ? 1 : 0;
   memset(&to, 0, sizeof(to));
-  if (C::kTmaStore && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && (p.ldo * (int64_t)sizeof(OT)) % 16 == 0) {
+  if (p.ksplit == 1 && C::kTmaStore && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
+      (p.ldo * (int64_t)sizeof(OT)) % 16 == 0) {
     if (int rc = make_map_2d(&to, p.out, odt, p.M, p.N, p.ldo, 128 / (int)sizeof(OT), 32)) return rc;
     p.tma_store = 1;
   }
@@ -440,9 +549,14 @@ int launch_lin_tc(const void* a, int64_t lda, const void* b, int64_t ldb, int dt
     if (dev >= 0) resident[dev].store(per_sm, std::memory_order_relaxed);
   }
   const int ntn = (p.N + BN - 1) / BN;
-  const int64_t ntiles = (int64_t)ntn * ((p.M + LM - 1) / LM);
+  const int64_t ntiles = (int64_t)ntn * ((p.M + LM - 1) / LM) * p.ksplit;
   const int64_t grid = min(ntiles, (int64_t)sm_count(dev) * per_sm);
   k<<<(unsigned)grid, C::kThr, C::kSmem, st>>>(ta, tb, to, p, ntn, ntiles);
+  if (int rc = launch_status()) return rc;
+  if (p.ksplit == 1) return TC_OK;
+  const int64_t total = p.M * p.N;
+  lin_reduce_kernel<<<(unsigned)((total / 4 + 256) / 256), 256, 0, st>>>(p.M, p.N, p.ksplit, p.part, p.epi,
+                                                                        p.aux, p.ld_aux, odt, p.out, p.ldo);
   return launch_status();
 }
 
@@ -451,12 +565,19 @@ int launch_lin_tc(const void* a, int64_t lda, const void* b, int64_t ldb, int dt
 // K > 64: with one K-block per tile the kernel is bound by its stores, which
 // the double-buffered slabs of the 128-column tile drain faster.
 template <typename T, typename OT>
-int launch_lin_tc_bn(const void* a, int64_t lda, const void* b, int64_t ldb, int dt, int odt, const LinParams& p,
+int launch_lin_tc_bn(const void* a, int64_t lda, const void* b, int64_t ldb, int dt, int odt, LinParams p,
                      cudaStream_t st) {
   const int64_t mt = (p.M + LM - 1) / LM;
   const int64_t sms = sm_count(current_device());
-  int bn = p.N > 128 && sizeof(OT) == 2 && p.K > LK ? 256 : p.N > 64 ? 128 : p.N > 32 ? 64 : p.N > 16 ? 32 : 16;
-  while (bn > 16 && mt * ((p.N + bn - 1) / bn) < sms) bn >>= 1;
+  int bn = lin_bn0(p.N, p.K, (int)sizeof(OT));
+  int parts = 1, nkp = (p.K + LK - 1) / LK;
+  if (p.part) lin_split(p.M, p.N, p.K, bn, &parts, &nkp);
+  p.ksplit = parts;
+  p.nkp = nkp;
+  if (parts == 1) {
+    p.part = nullptr;
+    while (bn > 16 && mt * ((p.N + bn - 1) / bn) < sms) bn >>= 1;
+  }
   if constexpr (sizeof(OT) == 2)
     if (bn == 256) return launch_lin_tc<T, OT, 256>(a, lda, b, ldb, dt, odt, p, st);
   if (bn == 128) return launch_lin_tc<T, OT, 128>(a, lda, b, ldb, dt, odt, p, st);
@@ -744,9 +865,17 @@ int64_t wgrad_mpad(int64_t M) { return (M + 7) / 8 * 8; }
 
 using namespace tc;
 
+extern "C" int64_t tc_linear_scratch_floats(int64_t M, int32_t N, int32_t K, int32_t out_dtype) {
+  if (M < 0 || N <= 0 || K <= 0 || out_dtype < TC_F32 || out_dtype > TC_F16) return -1;
+  int parts = 1, nkp = 0;
+  lin_split(M, N, K, lin_bn0(N, K, dtype_size(out_dtype)), &parts, &nkp);
+  return parts > 1 ? (int64_t)parts * M * N : 0;
+}
+
 extern "C" int tc_linear(int64_t M, int32_t N, int32_t K, int32_t a_dtype, const void* a, int64_t lda,
                          int32_t b_dtype, const void* b, int64_t ldb, int32_t out_dtype, void* out, int64_t ldo,
-                         int32_t epilogue, const void* aux, int64_t ld_aux, int32_t* dev_status, void* stream) {
+                         int32_t epilogue, const void* aux, int64_t ld_aux, float* scratch, int64_t scratch_floats,
+                         int32_t* dev_status, void* stream) {
   if (M < 0 || N <= 0 || K <= 0 || !a || !b || !out || lda < K || ldb < K || ldo < N) return TC_ERR_ARG;
   if (epilogue != TC_LIN_STORE && epilogue != TC_LIN_GATE) return TC_ERR_ARG;
   if (epilogue == TC_LIN_GATE && (!aux || ld_aux < N)) return TC_ERR_ARG;
@@ -768,6 +897,13 @@ extern "C" int tc_linear(int64_t M, int32_t N, int32_t K, int32_t a_dtype, const
   p.rot = 0;
   p.a_rows = LM;
   p.kb = 1;
+  p.ksplit = 1;
+  p.nkp = (K + LK - 1) / LK;
+  const int64_t need = tc_linear_scratch_floats(M, N, K, out_dtype);
+  // split K only with the scratch it needs (16-byte aligned); without it the
+  // call runs unsplit
+  p.part = (need > 0 && scratch && scratch_floats >= need && (reinterpret_cast<uintptr_t>(scratch) & 15) == 0)
+               ? scratch : nullptr;
   p.status = dev_status;
   const bool tc_ok = a_dtype == b_dtype && a_dtype != TC_F32 && (out_dtype == a_dtype || out_dtype == TC_F32) &&
                      lda % 8 == 0 && ldb % 8 == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&

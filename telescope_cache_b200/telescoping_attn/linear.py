@@ -52,9 +52,13 @@ def linear(x: torch.Tensor, w: torch.Tensor, *, out_dtype: Optional[torch.dtype]
         aux = _rows(gate_out.reshape(M, N))
         ld_aux, epi = aux.stride(0), _lib.TC_LIN_GATE
     if M and N:
+        # split-K scratch (few rows, long K); torch's allocator, stream ordered
+        nscratch = int(_lib.lib().tc_linear_scratch_floats(M, N, K, _lib.dtype_code(out_dtype)))
+        scratch = torch.empty(nscratch, device=x.device, dtype=torch.float32) if nscratch > 0 else None
         _lib.launch("tc_linear", x.device, M, N, K, _lib.dtype_code(a.dtype), _lib.ptr(a), a.stride(0),
                     _lib.dtype_code(b.dtype), _lib.ptr(b), b.stride(0), _lib.dtype_code(out_dtype),
-                    _lib.ptr(out), N, epi, _lib.ptr(aux), ld_aux, _status(x.device), _lib.stream_of(x))
+                    _lib.ptr(out), N, epi, _lib.ptr(aux), ld_aux, _lib.ptr(scratch), max(nscratch, 0),
+                    _status(x.device), _lib.stream_of(x))
     return out.reshape(*x.shape[:-1], N)
 
 

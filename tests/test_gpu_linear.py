@@ -47,7 +47,9 @@ def test_linear_matches_fp32_product(M, N, K, dtype, out_dtype):
     before = _lib.launch_count()
     y = linear(x, w, out_dtype=out_dtype)
     torch.cuda.synchronize()
-    assert _lib.launch_count() == before + 1
+    # one launch, or two when few row blocks and a long K split K (partial sums, then their reduction)
+    split = _lib.lib().tc_linear_scratch_floats(M, N, K, _lib.dtype_code(out_dtype)) > 0 and dtype != torch.float32
+    assert _lib.launch_count() == before + (2 if split else 1)
     assert y.dtype == out_dtype and y.shape == (M, N)
     _close(y, x.float() @ w.float().t(), out_dtype)
 
