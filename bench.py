@@ -504,10 +504,13 @@ def c5_sharded_bench(args, dev, world, rank):
         return dist.all_gather_into_tensor(buf.view(world, -1), local.reshape(1, -1), async_op=True)
 
     def gather_finish(handle, local, buf):
+        """The gathered tensor as a [B, N, world, hl, D] view of the rank-major
+        buffer (head = rank * hl + local head): every head is present and
+        addressable in place, with no reorder copy."""
         if handle is None:
             return local
         handle.wait()  # this stream waits for the collective
-        return buf.permute(1, 2, 0, 3, 4).reshape(B, N, world * hl, D)
+        return buf.permute(1, 2, 0, 3, 4)
 
     def step(timers=None):
         kl, vl, _ = T.build_dyadic_summaries(q, k, v, wl["levels"] - 1, x=x, w_proj=w_proj)
@@ -558,9 +561,10 @@ def c5_sharded_bench(args, dev, world, rank):
             "ms_per_step": ms, "gather_exposed_ms": gms, "gather_exposed_share": gms / ms,
             "config": {"workload": "c5", "desc": wl["desc"], "B": B, "T": N, "H": H, "D": D,
                        "heads_per_rank": hl, "fmap": fmap, "cache_size": cache, "step_flops": step_flops,
-                       "gathered": "out and dq, [B, T, H, D] bf16 each: NCCL all_gather_into_tensor + head "
-                                   "reorder; out's gather runs during the backward, gather_exposed_ms is the "
-                                   "time from the backward's end to the step's end"},
+                       "gathered": "out and dq, [B, T, H, D] bf16 each: NCCL all_gather_into_tensor into a "
+                                   "rank-major buffer, presented as a [B, T, ranks, H / ranks, D] view (no "
+                                   "reorder copy); out's gather runs during the backward, gather_exposed_ms is "
+                                   "the time from the backward's end to the step's end"},
             "frac_of_peak": value / world / sustained, "peak_source": f"{src} bf16_tflops_sustained (per GPU)"}
 
 
