@@ -40,7 +40,9 @@ constexpr int kSmemA = 2 * kNkvA * T64 + kNxA * 128 * 128 + 1024 + 256;
 // relative Pass A: + an fp32 dX staging tile [128 x 66], per-row run info,
 // row totals and the double-buffered bias runs [2][128][kRunStride]
 constexpr int kDxfStride = 66;  // even: 8-byte column pairs; 16 rows per phase hit distinct banks
-constexpr int kSmemArel = 2 * kNkvA * T64 + kNxA * 128 * 128 + 1024 + 256 + 128 * kDxfStride * 4 + 128 * 4 * 4 + 128 * 4 + 2 * 128 * kRunStride * 2 + 256;
+constexpr int kZeroBytes = 16384;  // relative Pass A: zeros the bulk stores of drel's unattended tail read
+constexpr int kSmemArel = 2 * kNkvA * T64 + kNxA * 128 * 128 + 1024 + 256 + 128 * kDxfStride * 4 + 128 * 4 * 4 +
+                          128 * 4 + 2 * 128 * kRunStride * 2 + 256 + kZeroBytes;
 // Pass B: tiles (NQ Q/dO stages: three, so a step's TMA load starts two
 // steps before its MMAs, unless the relative variant's staging leaves no
 // room) + per-step query info [2][64] x {-lse2, -Delta} (fp32) and {lo, hi}
@@ -154,6 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* mtot = reinterpret_cast<int*>(rinfo + 128);
   uint16_t* run_s = reinterpret_cast<uint16_t*>(mtot + 128);
   uint8_t* sh_s = reinterpret_cast<uint8_t*>(run_s + 2 * 128 * kRunStride);  // [2][128] run offsets
+  uint4* zero_s = reinterpret_cast<uint4*>(sh_s + 2 * 128);                   // [kZeroBytes] zeros
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * 128, hq = blockIdx.y, b = blockIdx.z;
@@ -184,6 +187,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tmem_alloc(tmem_holder, 512);
     tmem_relinquish();
+  }
+  if (REL && p.drel != nullptr) {
+    for (int i = threadIdx.x; i < kZeroBytes / 16; i += kThreads) zero_s[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_async_smem();  // the zeros are read by bulk copies
   }
   tc_fence_before();
   __syncthreads();
@@ -291,13 +298,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(qg_full);
     }
     const bool want_drel = REL && p.drel != nullptr;
-    if (want_drel && ch == 0) mtot[r] = row_ok ? visible_count(q, p.s) : 0;
     // drel write-out rows of this warp: kRowsPerWarp rows of its lane quadrant;
     // the quadrant's four warps synchronise on barrier 2 + quadrant
     const int quad = warp & 3, wrow0 = quad * 32 + ch * kRowsPerWarp;
     const int qbar = 2 + quad;
     const int64_t drel_stride = (int64_t)p.Hq * p.bins;
     float* drel_rows = want_drel ? p.drel + (((int64_t)b * p.N + q0 + wrow0) * p.Hq + hq) * p.bins : nullptr;
+    // distances at or beyond a row's visible count are never attended: lane k
+    // of the warp zeroes row wrow0 + k's tail [count, bins) now, with bulk
+    // copies from the zero block (16-byte aligned middle) and plain stores
+    // for the ends, so that the write overlaps the whole walk
+    if (want_drel && lane < kRowsPerWarp && q0 + wrow0 + lane < p.N) {
+      float* dst = drel_rows + lane * drel_stride;
+      const int m = visible_count(q0 + wrow0 + lane, p.s);
+      const uintptr_t a0 = reinterpret_cast<uintptr_t>(dst + m), a1 = reinterpret_cast<uintptr_t>(dst + p.bins);
+      uintptr_t ab = (a0 + 15) & ~uintptr_t(15), ae = a1 & ~uintptr_t(15);
+      if (ab > a1) ab = a1;
+      if (ae < ab) ae = ab;
+      for (float* z = dst + m; reinterpret_cast<uintptr_t>(z) < ab; ++z) *z = 0.f;
+      for (float* z = reinterpret_cast<float*>(ae); reinterpret_cast<uintptr_t>(z) < a1; ++z) *z = 0.f;
+      for (uintptr_t c = ab; c < ae; c += kZeroBytes) {
+        const uint32_t nb = (uint32_t)min((uintptr_t)kZeroBytes, ae - c);
+        bulk_store(reinterpret_cast<void*>(c), zero_s, nb);
+      }
+      bulk_commit();
+    }
     int lo = 0, hi = 0, base = 0, cur = -1;
     TileWalk it{-1, 0, 0, q0, q1, 64};
     bool ok = it.start(p.s);
@@ -401,15 +426,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (want_drel) {  // the quadrant's four warps all reach this barrier, also after an abort
-      // distances at or beyond a row's visible count are never attended: zero them
-      named_bar(qbar, kQuadThreads);
-      for (int k = 0; k < kRowsPerWarp; ++k) {
-        if (q0 + wrow0 + k >= p.N) break;
-        float* dst = drel_rows + k * drel_stride;
-        for (int d = mtot[wrow0 + k] + lane; d < p.bins; d += 32) dst[d] = 0.f;
-      }
-    }
+    // the tail zeroes are written, and the zero block has been read, before the CTA ends
+    if (want_drel && lane < kRowsPerWarp) bulk_wait_all();
     if (alive && j >= 1) alive = __all_sync(0xffffffffu, mbar_wait(dq_done, 0, abort_flag, status));
     if (alive) {
       tc_fence_after();

@@ -125,12 +125,21 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int c0, int
                "r"(c0), "r"(c1), "r"(smem_addr(src))
                : "memory");
 }
+// Untiled bulk copy shared -> global (no multicast): dst and src 16-byte
+// aligned, bytes a multiple of 16; joins this thread's current bulk group.
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+               "r"(smem_addr(src)), "r"(bytes)
+               : "memory");
+}
 // Close this thread's current bulk group.
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until every bulk group this thread committed has read its shared-memory
 // source (which may then be rewritten).
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-// The same, leaving this thread's most recent bulk group possibly unread.
+// Wait until every bulk group this thread committed has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// The same as bulk_wait_read_all, leaving this thread's most recent bulk group possibly unread.
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // Untiled bulk copy global -> shared (no multicast): dst and src 16-byte
 // aligned, bytes a multiple of 16; completes `bytes` of tx on `bar`.
