@@ -255,7 +255,7 @@ __device__ __forceinline__ void pair_weights(float w0, float w1, float* a0, floa
 }
 
 template <typename T, typename TW>
-__global__ void __launch_bounds__(kThreads) tree_chunk128_kernel(TreeParams p) {
+__global__ void __launch_bounds__(kThreads, 3) tree_chunk128_kernel(TreeParams p) {
   constexpr int D = 128;
   // shared: raw rows with the conv halo (16-bit), then levels 2.. as fp32
   extern __shared__ uint4 smem4[];
