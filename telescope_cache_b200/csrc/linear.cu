@@ -100,14 +100,21 @@ struct LinParams {
 };
 
 // Tile t of the split grid: K part, row block, column block (columns fastest).
+// Tile counts stay below 2^31 (checked by the launcher): 32-bit unsigned
+// division, and none for the K part when K is not split.
 struct LinTile {
   int n0, m0, kpart;
-  __device__ LinTile(int64_t t, int ntn, int64_t mt, int BN) {
-    const int64_t per = (int64_t)ntn * mt;
-    kpart = (int)(t / per);
-    const int64_t r = t - (int64_t)kpart * per;
-    n0 = (int)(r % ntn) * BN;
-    m0 = (int)(r / ntn) * LM;
+  __device__ LinTile(int64_t t, int ntn, int64_t mt, int ksplit, int BN) {
+    uint32_t r = (uint32_t)t;
+    kpart = 0;
+    if (ksplit > 1) {
+      const uint32_t per = (uint32_t)ntn * (uint32_t)mt;
+      kpart = (int)(r / per);
+      r -= (uint32_t)kpart * per;
+    }
+    const uint32_t mq = r / (uint32_t)ntn;
+    n0 = (int)(r - mq * (uint32_t)ntn) * BN;
+    m0 = (int)mq * LM;
   }
 };
 
@@ -178,7 +185,9 @@ __device__ __forceinline__ void store_chunk(const LinParams& p, int64_t row, int
 // Persistent: CTA b takes tiles b, b + G, ... (G = grid size) of the
 // [ceil(M / 128) x ceil(N / BN)] tile grid, N fastest (neighbouring CTAs
 // share A rows in L2).
-template <typename T, typename OT, int BN>
+// SPLIT: K split over tile sets (partial sums to p.part); the unsplit kernel
+// carries none of that bookkeeping.
+template <typename T, typename OT, int BN, bool SPLIT>
 __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                      const __grid_constant__ CUtensorMap to, LinParams p, int ntn, int64_t ntiles) {
@@ -203,9 +212,15 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
   const int nk = (p.K + LK - 1) / LK;
   const int64_t mt = (p.M + LM - 1) / LM;
   // K-blocks [kstart, kend) of split part kp, in stage loads of kb
+  const int nst_all = (nk + p.kb - 1) / p.kb;  // stage loads of an unsplit tile
   const auto krange = [&](int kp, int* kstart, int* kend) {
-    *kstart = kp * p.nkp;
-    *kend = min(nk, *kstart + p.nkp);
+    if constexpr (SPLIT) {
+      *kstart = kp * p.nkp;
+      *kend = min(nk, *kstart + p.nkp);
+    } else {
+      *kstart = 0;
+      *kend = nk;
+    }
   };
   const int64_t G = gridDim.x;
 
@@ -246,11 +261,11 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
       int64_t sc = 0;  // stage loads issued, across tiles
       bool alive = true;
       for (int64_t t = blockIdx.x; t < ntiles && alive; t += G) {
-        const LinTile tl(t, ntn, mt, BN);
+        const LinTile tl(t, ntn, mt, SPLIT ? p.ksplit : 1, BN);
         const int row0 = is_a ? tl.m0 : tl.n0;
         int ks0, ke0;
         krange(tl.kpart, &ks0, &ke0);
-        const int nst = (ke0 - ks0 + p.kb - 1) / p.kb;
+        const int nst = SPLIT ? (ke0 - ks0 + p.kb - 1) / p.kb : nst_all;
         for (int st = 0; st < nst; ++st, ++sc) {
           const int s = (int)(sc % C::NS);
           if (sc >= C::NS && !mbar_wait(&empty[s], (uint32_t)((sc / C::NS) - 1) & 1, abort_flag, p.status)) {
@@ -272,10 +287,10 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
       bool alive = true;
       int i = 0;
       for (int64_t t = blockIdx.x; t < ntiles && alive; t += G, ++i) {
-        const LinTile tl(t, ntn, mt, BN);
+        const LinTile tl(t, ntn, mt, SPLIT ? p.ksplit : 1, BN);
         int ks0, ke0;
         krange(tl.kpart, &ks0, &ke0);
-        const int nst = (ke0 - ks0 + p.kb - 1) / p.kb;
+        const int nst = SPLIT ? (ke0 - ks0 + p.kb - 1) / p.kb : nst_all;
         const int ab = i & 1;
         if (i >= 2 && !mbar_wait(&acc_empty[ab], ((i >> 1) - 1) & 1, abort_flag, p.status)) break;
         tc_fence_after();
@@ -312,7 +327,7 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
     const bool via_tma = C::kTmaStore && p.tma_store;
     int i = 0;
     for (int64_t t = blockIdx.x; t < ntiles; t += G, ++i) {
-      const LinTile tl(t, ntn, mt, BN);
+      const LinTile tl(t, ntn, mt, SPLIT ? p.ksplit : 1, BN);
       const int n0 = tl.n0, m0 = tl.m0;
       const int64_t row = (int64_t)m0 + quad * 32 + lane;
       const int ab = i & 1;
@@ -333,7 +348,7 @@ __global__ void __launch_bounds__(LinCfg<BN, (int)sizeof(OT)>::kThr, 1)
         if constexpr (C::CW == 32) tmem_ld32(tmem + lane_base + ab * BN + c0, v);
         else tmem_ld16(tmem + lane_base + ab * BN + c0, v);
         tmem_wait_ld();
-        if (p.part) {
+        if constexpr (SPLIT) {
           // split K: this part's fp32 partial sums, the epilogue comes with their reduction
           if (row < p.M) {
             float* o = p.part + ((int64_t)tl.kpart * p.M + row) * p.N + n0 + c0;
@@ -535,21 +550,23 @@ int launch_lin_tc(const void* a, int64_t lda, const void* b, int64_t ldb, int dt
     if (int rc = make_map_2d(&to, p.out, odt, p.M, p.N, p.ldo, 128 / (int)sizeof(OT), 32)) return rc;
     p.tma_store = 1;
   }
-  auto k = linear_tc_kernel<T, OT, BN>;
-  // per device, once: the shared-memory opt-in and the resident CTAs per SM
-  static std::atomic<int> resident[kMaxDev];
+  const bool split = p.ksplit > 1;
+  auto k = split ? linear_tc_kernel<T, OT, BN, true> : linear_tc_kernel<T, OT, BN, false>;
+  // per device and variant, once: the shared-memory opt-in and the resident CTAs per SM
+  static std::atomic<int> resident[2][kMaxDev];
   const int dev = current_device();
-  int per_sm = dev >= 0 ? resident[dev].load(std::memory_order_relaxed) : 0;
+  int per_sm = dev >= 0 ? resident[split][dev].load(std::memory_order_relaxed) : 0;
   if (per_sm <= 0) {
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
       return TC_ERR_CUDA;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, C::kThr, C::kSmem) != cudaSuccess || per_sm < 1)
       per_sm = 1;
     per_sm = min(per_sm, 512 / C::kCols);  // TMEM columns per SM
-    if (dev >= 0) resident[dev].store(per_sm, std::memory_order_relaxed);
+    if (dev >= 0) resident[split][dev].store(per_sm, std::memory_order_relaxed);
   }
   const int ntn = (p.N + BN - 1) / BN;
   const int64_t ntiles = (int64_t)ntn * ((p.M + LM - 1) / LM) * p.ksplit;
+  if (ntiles > 0x7fffffffLL) return TC_ERR_UNSUPPORTED;
   const int64_t grid = min(ntiles, (int64_t)sm_count(dev) * per_sm);
   k<<<(unsigned)grid, C::kThr, C::kSmem, st>>>(ta, tb, to, p, ntn, ntiles);
   if (int rc = launch_status()) return rc;
