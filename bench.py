@@ -464,9 +464,9 @@ def c5_sharded_bench(args, dev, world, rank):
     builds its heads' tree (linear merge weights from x and its rows of
     w_proj), runs the rope forward with softcap 50, the sink and its backward
     and the Phase-2 backward, and gathers the full out and dq onto every rank
-    with one NCCL all_gather each (into one buffer, then the head-major
-    reorder) -- all inside the timed region; out's gather is started before
-    the backward and overlaps it.  value = the whole config-5
+    with one NCCL all_gather each (into one rank-major buffer, returned as a
+    [B, T, ranks, H / ranks, D] view) -- all inside the timed region; out's
+    gather is started before the backward and overlaps it.  value = the whole config-5
     step's visible-entry FLOPs / the max-over-ranks step time."""
     import torch
     import torch.distributed as dist
