@@ -200,6 +200,15 @@ int tc_short_conv_bwd(int32_t B, int32_t N, int32_t C, int32_t dtype, const void
                       int32_t w_dtype, const void* w, const float* dy, void* dx, float* dw, float* partials,
                       int64_t partial_floats, void* stream);
 
+/* tc_short_conv_bwd with segment resets: seq_idx [B, N] int32 (NULL = one
+ * sequence per batch row) pairs a tap between rows s and t only when
+ * seq_idx[b, s] == seq_idx[b, t].  The VJP of tc_short_conv_seg.  No
+ * reference counterpart: the reference's short_conv leaves resets across
+ * packed examples as a TODO (reference.py:186-189). */
+int tc_short_conv_seg_bwd(int32_t B, int32_t N, int32_t C, int32_t dtype, const void* x, int32_t K,
+                          int32_t w_dtype, const void* w, const int32_t* seq_idx, const float* dy, void* dx,
+                          float* dw, float* partials, int64_t partial_floats, void* stream);
+
 /* Projection epilogues of tc_linear */
 #define TC_LIN_STORE 0  /* out = A B^T                                  */
 #define TC_LIN_GATE 1   /* out = SiLU(A B^T) * aux (aux: out's type)    */
@@ -249,11 +258,27 @@ int tc_linear_weights(int64_t rows, int32_t E, int32_t H, int32_t x_dtype, const
 int tc_qk_weights(int32_t B, int32_t N, int32_t Hq, int32_t Hkv, int32_t Dk, int32_t dtype,
                   const void* q, const void* k, int32_t out_dtype, void* out, void* stream);
 
+/* VJP of tc_qk_weights (the autograd of compute_summary_weights,
+ * reference.py:117-145) for an upstream gradient dw [B, N, Hkv] of type
+ * g_dtype: with p_e = softmax over the group of q_e . k / sqrt(Dk),
+ * dq_e = dw p_e k / sqrt(Dk), dk = sum_e dw p_e q_e / sqrt(Dk); fp32 math,
+ * dq / dk written in dtype.  Dk <= 256. */
+int tc_qk_weights_bwd(int32_t B, int32_t N, int32_t Hq, int32_t Hkv, int32_t Dk, int32_t dtype,
+                      const void* q, const void* k, int32_t g_dtype, const void* dw, void* dq, void* dk,
+                      void* stream);
+
 /* Causal depthwise short conv with fp32 taps and fp32 residual, one cast:
  * y[b, t, c] = x[b, t, c] + sum_j w[c, j] x[b, t - K + 1 + j, c]
  * (short_conv, reference.py:167-211).  x, y [B, N, C]; w [C, K]. */
 int tc_short_conv(int32_t B, int32_t N, int32_t C, int32_t dtype, const void* x, int32_t K,
                   int32_t w_dtype, const void* w, void* y, void* stream);
+
+/* tc_short_conv with segment resets for packed examples: seq_idx [B, N]
+ * int32 (NULL = one sequence per batch row); the tap at row s reaches row t
+ * only when seq_idx[b, s] == seq_idx[b, t].  No reference counterpart: the
+ * reference's short_conv leaves these resets as a TODO (reference.py:186-189). */
+int tc_short_conv_seg(int32_t B, int32_t N, int32_t C, int32_t dtype, const void* x, int32_t K,
+                      int32_t w_dtype, const void* w, const int32_t* seq_idx, void* y, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* positional helpers                                                        */

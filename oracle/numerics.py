@@ -46,9 +46,21 @@ STORE = {"fp64": identity, "fp32": to_fp32, "bf16": to_bf16}
 # Phase 1: short conv, merge weights, dyadic tree
 # ----------------------------------------------------------------------------
 
-def short_conv(x, weight):
+def _same_segment(seq_idx, n, back):
+    """[B, n - back, 1] mask: rows t and t - back belong to one segment
+    (all ones without segment ids)."""
+    if seq_idx is None:
+        return 1.0
+    s = np.asarray(seq_idx)
+    return (s[:, back:] == s[:, : n - back])[..., None].astype(np.float64)
+
+
+def short_conv(x, weight, seq_idx=None):
     """y[b,t,c] = x[b,t,c] + sum_j weight[c,j] x[b,t-K+1+j,c], causal, zero
-    left padding (reference.py:167-211).  Returns float64 (caller rounds)."""
+    left padding (reference.py:167-211).  Returns float64 (caller rounds).
+    seq_idx [B, N] (the reset the reference leaves as a TODO at
+    reference.py:186-189): a tap at row s reaches row t only when
+    seq_idx[b, s] == seq_idx[b, t]."""
     x = np.asarray(x, dtype=np.float64)
     w = np.asarray(weight, dtype=np.float64)
     n = x.shape[1]
@@ -57,7 +69,7 @@ def short_conv(x, weight):
     for j in range(kk):
         back = kk - 1 - j
         if back < n:
-            y[:, back:, :] += w[:, j] * x[:, : n - back, :]
+            y[:, back:, :] += w[:, j] * x[:, : n - back, :] * _same_segment(seq_idx, n, back)
     return x + y
 
 
@@ -104,9 +116,10 @@ def build_tree(k, v, w, num_summary_levels, store=identity):
     return kl, vl, wl
 
 
-def short_conv_vjp(x, weight, dy):
+def short_conv_vjp(x, weight, dy, seq_idx=None):
     """VJP of short_conv: dx[s] = dy[s] + sum_j weight[c,j] dy[s+K-1-j] and
-    dweight[c,j] = sum_{b,t} dy[t,c] x[t-K+1+j,c] (zero padding)."""
+    dweight[c,j] = sum_{b,t} dy[t,c] x[t-K+1+j,c] (zero padding; with
+    seq_idx only taps within one segment)."""
     x = np.asarray(x, np.float64)
     w = np.asarray(weight, np.float64)
     dy = np.asarray(dy, np.float64)
@@ -116,8 +129,9 @@ def short_conv_vjp(x, weight, dy):
     for j in range(kk):
         back = kk - 1 - j
         if back < n:
-            dx[:, : n - back, :] += w[:, j] * dy[:, back:, :]
-            dw[:, j] = np.einsum("btc,btc->c", dy[:, back:, :], x[:, : n - back, :])
+            g = dy[:, back:, :] * _same_segment(seq_idx, n, back)
+            dx[:, : n - back, :] += w[:, j] * g
+            dw[:, j] = np.einsum("btc,btc->c", g, x[:, : n - back, :])
     return dx, dw
 
 

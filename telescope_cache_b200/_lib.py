@@ -124,6 +124,11 @@ SIGNATURES = {
     "tc_qk_weights": [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_vp, _c_i32, _c_vp,
                       _c_vp],
     "tc_short_conv": [_c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_i32, _c_i32, _c_vp, _c_vp, _c_vp],
+    "tc_short_conv_seg": [_c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_i32, _c_i32, _c_vp, _c_vp, _c_vp, _c_vp],
+    "tc_short_conv_seg_bwd": [_c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_i32, _c_i32, _c_vp, _c_vp, _c_vp, _c_vp,
+                              _c_vp, _c_vp, _c_i64, _c_vp],
+    "tc_qk_weights_bwd": [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_vp, _c_i32, _c_vp, _c_vp,
+                          _c_vp, _c_vp],
     "tc_rope_apply": [_c_i32, _c_i64, _c_i32, _c_i32, _c_i32, _c_vp, _c_vp, _c_vp, _c_vp, _c_i32,
                       _c_i32, ctypes.POINTER(Schedule), _c_vp, _c_i32, _c_vp],
     "tc_attn_fwd": [ctypes.POINTER(AttnArgs), ctypes.POINTER(Schedule), _c_vp],

@@ -248,19 +248,87 @@ __global__ void qk_weights_kernel(int64_t rows, int Hq, int Hkv, int Dk, const T
   if (lane == 0) store_any(out, w, odt, m + logf(s));
 }
 
+// seq (optional, [B, N]): a tap at tt reaches t only when seq[tt] == seq[t],
+// so packed examples do not see each other's rows
 template <typename T>
-__global__ void short_conv_kernel(int B, int N, int C, const T* x, int K, int wdt, const void* w, T* y) {
+__global__ void short_conv_kernel(int B, int N, int C, const T* x, int K, int wdt, const void* w,
+                                  const int32_t* seq, T* y) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)B * N * C) return;
   const int c = (int)(i % C);
   const int64_t bt = i / C;
   const int t = (int)(bt % N);
+  const int sid = seq ? seq[bt] : 0;
   float acc = 0.f;
   for (int j = 0; j < K; ++j) {
     const int tt = t - K + 1 + j;
-    if (tt >= 0) acc += load_any(w, (int64_t)c * K + j, wdt) * to_f(x[i + (int64_t)(tt - t) * C]);
+    if (tt >= 0 && (!seq || seq[bt + tt - t] == sid))
+      acc += load_any(w, (int64_t)c * K + j, wdt) * to_f(x[i + (int64_t)(tt - t) * C]);
   }
   y[i] = from_f<T>(to_f(x[i]) + acc);
+}
+
+// one warp per (b, t, hkv): with p_e = exp(s_e - w), s_e = q_e . k / sqrt(Dk)
+// and g = dw, dq_e = g p_e k / sqrt(Dk) and dk = sum_e g p_e q_e / sqrt(Dk)
+template <typename T>
+__global__ void qk_weights_bwd_kernel(int64_t rows, int Hq, int Hkv, int Dk, const T* q, const T* k, int gdt,
+                                     const void* gw, T* dq, T* dk) {
+  constexpr int kMaxPer = 8;  // Dk <= 256
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= rows * Hkv) return;
+  const int64_t bt = w / Hkv;
+  const int h = (int)(w % Hkv);
+  const int E = Hq / Hkv;
+  const float scale = 1.f / sqrtf((float)Dk);
+  const T* kr = k + (bt * Hkv + h) * Dk;
+  float kv[kMaxPer], dkv[kMaxPer];
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int d = lane + 32 * i;
+    kv[i] = d < Dk ? to_f(kr[d]) : 0.f;
+    dkv[i] = 0.f;
+  }
+  auto score = [&](int e) {
+    const T* qr = q + (bt * Hq + h * E + e) * Dk;
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int d = lane + 32 * i;
+      if (d < Dk) dot += to_f(qr[d]) * kv[i];
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    return dot * scale;
+  };
+  float m = -INFINITY, s = 0.f;
+  for (int e = 0; e < E; ++e) {
+    const float dot = score(e);
+    const float mn = fmaxf(m, dot);
+    s = s * expf(m - mn) + expf(dot - mn);
+    m = mn;
+  }
+  const float lse = m + logf(s);
+  const float g = load_any(gw, w, gdt);
+  for (int e = 0; e < E; ++e) {
+    const float coef = g * expf(score(e) - lse) * scale;
+    const T* qr = q + (bt * Hq + h * E + e) * Dk;
+    T* dqr = dq + (bt * Hq + h * E + e) * Dk;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int d = lane + 32 * i;
+      if (d < Dk) {
+        dqr[d] = from_f<T>(coef * kv[i]);
+        dkv[i] += coef * to_f(qr[d]);
+      }
+    }
+  }
+  T* dkr = dk + (bt * Hkv + h) * Dk;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int d = lane + 32 * i;
+    if (d < Dk) dkr[d] = from_f<T>(dkv[i]);
+  }
 }
 
 }  // namespace
@@ -277,16 +345,38 @@ extern "C" int tc_qk_weights(int32_t B, int32_t N, int32_t Hq, int32_t Hkv, int3
   return launch_status();
 }
 
-extern "C" int tc_short_conv(int32_t B, int32_t N, int32_t C, int32_t dtype, const void* x, int32_t K,
-                             int32_t w_dtype, const void* w, void* y, void* stream) {
+extern "C" int tc_qk_weights_bwd(int32_t B, int32_t N, int32_t Hq, int32_t Hkv, int32_t Dk, int32_t dtype,
+                                 const void* q, const void* k, int32_t g_dtype, const void* dw, void* dq,
+                                 void* dk, void* stream) {
+  if (B <= 0 || N < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Dk <= 0 || Dk > 256 || !q || !k || !dw || !dq ||
+      !dk)
+    return TC_ERR_ARG;
+  const int64_t rows = (int64_t)B * N;
+  if (rows == 0) return TC_OK;
+  TC_DISPATCH(dtype, T, {
+    qk_weights_bwd_kernel<T><<<blocks_for(rows * Hkv * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+        rows, Hq, Hkv, Dk, static_cast<const T*>(q), static_cast<const T*>(k), g_dtype, dw,
+        static_cast<T*>(dq), static_cast<T*>(dk));
+  });
+  return launch_status();
+}
+
+extern "C" int tc_short_conv_seg(int32_t B, int32_t N, int32_t C, int32_t dtype, const void* x, int32_t K,
+                                 int32_t w_dtype, const void* w, const int32_t* seq_idx, void* y,
+                                 void* stream) {
   if (B <= 0 || N < 0 || C <= 0 || K <= 0 || !x || !w || !y) return TC_ERR_ARG;
   const int64_t n = (int64_t)B * N * C;
   if (n == 0) return TC_OK;
   TC_DISPATCH(dtype, T, {
     short_conv_kernel<T><<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
-        B, N, C, static_cast<const T*>(x), K, w_dtype, w, static_cast<T*>(y));
+        B, N, C, static_cast<const T*>(x), K, w_dtype, w, seq_idx, static_cast<T*>(y));
   });
   return launch_status();
+}
+
+extern "C" int tc_short_conv(int32_t B, int32_t N, int32_t C, int32_t dtype, const void* x, int32_t K,
+                             int32_t w_dtype, const void* w, void* y, void* stream) {
+  return tc_short_conv_seg(B, N, C, dtype, x, K, w_dtype, w, nullptr, y, stream);
 }
 
 extern "C" int tc_rope_apply(int32_t B, int64_t S, int32_t H, int32_t D, int32_t dtype, const void* x,

@@ -651,9 +651,11 @@ __global__ void tree_vjp_up_init_kernel(int64_t rows, int Hkv, int Dk, int Dv, i
 
 // dx and the dw partials of one (batch, chunk, channel); the K - 1 rows of dy
 // ahead and of x behind each token are re-read (L1 hits) rather than kept.
+// seq (optional, [B, N]): a tap pairs rows s and t only when seq[s] == seq[t].
 template <typename T>
 __global__ void __launch_bounds__(256) conv_bwd_kernel(int B, int N, int C, int K, const T* x, const void* w,
-                                                        int w_dtype, const float* dy, T* dx, float* partials) {
+                                                        int w_dtype, const int32_t* seq, const float* dy, T* dx,
+                                                        float* partials) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int chunk = blockIdx.y, b = blockIdx.z;
   if (c >= C) return;
@@ -666,21 +668,23 @@ __global__ void __launch_bounds__(256) conv_bwd_kernel(int B, int N, int C, int 
   for (int j = 0; j < kMaxK; ++j) acc[j] = 0.f;
   const int t0 = chunk * kChunk, t1 = min(t0 + kChunk, N);
   const int64_t base = (int64_t)b * N * C + c;
+  const int32_t* sq = seq ? seq + (int64_t)b * N : nullptr;
   for (int t = t0; t < t1; ++t) {
     const float g = dy[base + (int64_t)t * C];
+    const int sid = sq ? sq[t] : 0;
     // dx[t] = dy[t] + sum_j w[j] dy[t + K - 1 - j]
     float v = g;
 #pragma unroll
     for (int j = 0; j < kMaxK; ++j) {
       const int s = t + K - 1 - j;
-      if (j < K && s < N) v += wc[j] * dy[base + (int64_t)s * C];
+      if (j < K && s < N && (!sq || sq[s] == sid)) v += wc[j] * dy[base + (int64_t)s * C];
     }
     dx[base + (int64_t)t * C] = from_f<T>(v);
     // dw[j] += dy[t] x[t - K + 1 + j]
 #pragma unroll
     for (int j = 0; j < kMaxK; ++j) {
       const int s = t - K + 1 + j;
-      if (j < K && s >= 0) acc[j] += g * to_f(x[base + (int64_t)s * C]);
+      if (j < K && s >= 0 && (!sq || sq[s] == sid)) acc[j] += g * to_f(x[base + (int64_t)s * C]);
     }
   }
   float* pp = partials + (((int64_t)b * nchunk + chunk) * C + c) * K;
@@ -882,9 +886,10 @@ extern "C" int tc_build_tree_bwd(const tc_tree_bwd_args* a, void* stream) {
   return TC_ERR_ARG;
 }
 
-extern "C" int tc_short_conv_bwd(int32_t B, int32_t N, int32_t C, int32_t dtype, const void* x, int32_t K,
-                                 int32_t w_dtype, const void* w, const float* dy, void* dx, float* dw,
-                                 float* partials, int64_t partial_floats, void* stream) {
+extern "C" int tc_short_conv_seg_bwd(int32_t B, int32_t N, int32_t C, int32_t dtype, const void* x,
+                                     int32_t K, int32_t w_dtype, const void* w, const int32_t* seq_idx,
+                                     const float* dy, void* dx, float* dw, float* partials,
+                                     int64_t partial_floats, void* stream) {
   if (B < 0 || N < 0 || C <= 0 || K <= 0 || K > kMaxK || !x || !w || !dy || !dx || !dw || !partials)
     return TC_ERR_ARG;
   const int nchunk = (N + kChunk - 1) / kChunk;
@@ -896,10 +901,17 @@ extern "C" int tc_short_conv_bwd(int32_t B, int32_t N, int32_t C, int32_t dtype,
   }
   TC_DISPATCH(dtype, T, {
     conv_bwd_kernel<T><<<dim3((C + 255) / 256, nchunk, B), 256, 0, st>>>(
-        B, N, C, K, static_cast<const T*>(x), w, w_dtype, dy, static_cast<T*>(dx), partials);
+        B, N, C, K, static_cast<const T*>(x), w, w_dtype, seq_idx, dy, static_cast<T*>(dx), partials);
     if (int rc = launch_status()) return rc;
     conv_dw_sum_kernel<<<(C * K + 255) / 256, 256, 0, st>>>(B * nchunk, C, K, partials, dw);
     return launch_status();
   });
   return TC_ERR_ARG;
+}
+
+extern "C" int tc_short_conv_bwd(int32_t B, int32_t N, int32_t C, int32_t dtype, const void* x, int32_t K,
+                                 int32_t w_dtype, const void* w, const float* dy, void* dx, float* dw,
+                                 float* partials, int64_t partial_floats, void* stream) {
+  return tc_short_conv_seg_bwd(B, N, C, dtype, x, K, w_dtype, w, nullptr, dy, dx, dw, partials,
+                               partial_floats, stream);
 }

@@ -105,14 +105,19 @@ def _dense_rows(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return t
 
 
-def _conv_history(x_pre: torch.Tensor, kernel_size: int) -> torch.Tensor:
+def _conv_history(x_pre: torch.Tensor, kernel_size: int, seq_idx: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Last K-1 rows of x_pre [B, N, C], zero-padded on the left when N < K-1
-    (reference.py:1796-1807)."""
+    (reference.py:1796-1807).  With segment ids seq_idx [B, N], rows of an
+    earlier example than the last row's are zeroed: decoding continues the
+    last packed example only."""
     hist = kernel_size - 1
     if hist == 0:
         return x_pre[:, :0].clone()
     # slice before padding: only the last K-1 rows are copied, not the prefill
     tail = x_pre[:, -hist:]
+    if seq_idx is not None:
+        same = seq_idx[:, -tail.shape[1]:] == seq_idx[:, -1:]
+        tail = torch.where(same.unsqueeze(-1), tail, torch.zeros((), dtype=tail.dtype, device=tail.device))
     pad = hist - tail.shape[1]
     if pad > 0:
         return torch.nn.functional.pad(tail, (0, 0, pad, 0)).contiguous()
@@ -147,10 +152,13 @@ def init_decode_state(
     k_pre_conv: Optional[torch.Tensor] = None,
     v_pre_conv: Optional[torch.Tensor] = None,
     conv_kernel_size: Optional[int] = None,
+    seq_idx: Optional[torch.Tensor] = None,
 ) -> DecodeState:
     """Prefill hand-off: the nodes live at query N-1 go to their ring slots and
     t = N; the last K-1 pre-conv rows seed the conv history
-    (reference.py:1848-1945)."""
+    (reference.py:1848-1945).  seq_idx (an extension, as for short_conv):
+    segment ids [B, N] of a packed prefill; history rows of earlier examples
+    than the last row's are zeroed."""
     if (k_pre_conv is None) != (v_pre_conv is None):
         raise ValueError("k_pre_conv and v_pre_conv must both be provided or both be None")
     if (k_pre_conv is None) != (conv_kernel_size is None):
@@ -231,8 +239,13 @@ def init_decode_state(
             raise ValueError(
                 f"pre-conv rows must be [B={B}, N={N}, ...], got {tuple(k_pre_conv.shape)} / "
                 f"{tuple(v_pre_conv.shape)}")
-        state.conv_k = _conv_history(k_pre_conv.reshape(B, N, -1), conv_kernel_size)
-        state.conv_v = _conv_history(v_pre_conv.reshape(B, N, -1), conv_kernel_size)
+        seq = None
+        if seq_idx is not None:
+            if tuple(seq_idx.shape) != (B, N) or seq_idx.dtype.is_floating_point:
+                raise ValueError(f"seq_idx must be an integer tensor [{B}, {N}], got {tuple(seq_idx.shape)}")
+            seq = seq_idx.to(k_pre_conv.device)
+        state.conv_k = _conv_history(k_pre_conv.reshape(B, N, -1), conv_kernel_size, seq)
+        state.conv_v = _conv_history(v_pre_conv.reshape(B, N, -1), conv_kernel_size, seq)
     return state
 
 

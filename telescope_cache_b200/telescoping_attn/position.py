@@ -46,11 +46,43 @@ def _rope_into(x, y, cos, sin, kind, sched=None, positions=None, inverse=False):
     return y
 
 
+def _rope_rows(x, pos, cos, sin, inverse):
+    """tc_rope_apply at per-row positions pos (int32, x.shape[:-1])."""
+    D = x.shape[-1]
+    xc = x.contiguous()
+    y = torch.empty_like(xc)
+    if xc.numel():
+        _rope_into(xc.reshape(1, 1, -1, D), y.reshape(1, 1, -1, D), cos, sin, 2,
+                   positions=pos.reshape(-1), inverse=inverse)
+    return y
+
+
+class _Rope(torch.autograd.Function):
+    """apply_rope with its VJP as backward: R(p) is orthogonal, so the
+    gradient of y = R(p) x is R(p)^T dy = R(-p) dy, rotated in fp32 and cast
+    to x's dtype as autograd does through the reference's x.float()."""
+
+    @staticmethod
+    def forward(ctx, x, pos, cos, sin, inverse):
+        ctx.save_for_backward(pos, cos, sin)
+        ctx.inverse = inverse
+        ctx.x_dtype = x.dtype
+        return _rope_rows(x, pos, cos, sin, inverse)
+
+    @staticmethod
+    def backward(ctx, gy):
+        pos, cos, sin = ctx.saved_tensors
+        g = gy if gy.dtype == ctx.x_dtype else gy.float()
+        dx = _rope_rows(g, pos, cos, sin, not ctx.inverse).to(ctx.x_dtype)
+        return dx, None, None, None, None
+
+
 def apply_rope(x: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                inverse: bool = False) -> torch.Tensor:
     """Rotate-half RoPE of x [..., D] at integer `positions` (broadcastable to
     x.shape[:-1]) in fp32, cast back; inverse=True applies R(-p)
-    (reference.py:267-302)."""
+    (reference.py:267-302).  Differentiable in x; the tables are constants
+    (a cos / sin that requires gradients raises)."""
     if cos.shape != sin.shape:
         raise ValueError(f"cos shape {tuple(cos.shape)} != sin shape {tuple(sin.shape)}")
     D = x.shape[-1]
@@ -62,12 +94,11 @@ def apply_rope(x: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, sin:
     pos = positions.to(device=x.device).expand(x.shape[:-1]).to(torch.int32).contiguous()
     if pos.numel() and (int(pos.min()) < 0 or int(pos.max()) >= cos.shape[0]):
         raise IndexError("rope position outside the tables")
-    xc = x.contiguous()
-    y = torch.empty_like(xc)
-    if xc.numel():
-        _rope_into(xc.reshape(1, 1, -1, D), y.reshape(1, 1, -1, D), cos, sin, 2,
-                   positions=pos.reshape(-1), inverse=inverse)
-    return y
+    if torch.is_grad_enabled() and (x.requires_grad or cos.requires_grad or sin.requires_grad):
+        if cos.requires_grad or sin.requires_grad:
+            raise NotImplementedError("gradients with respect to the rope tables are not supported")
+        return _Rope.apply(x, pos, cos, sin, bool(inverse))
+    return _rope_rows(x, pos, cos, sin, inverse)
 
 
 def validate_summary_causality(spec: RangeSpec) -> None:

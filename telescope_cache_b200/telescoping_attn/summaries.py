@@ -27,22 +27,54 @@ def _contig(t):
     return t if t.is_contiguous() else t.contiguous()
 
 
+def _qk_weights(q, k):
+    B, N, Hq, Dk = q.shape
+    Hkv = k.shape[2]
+    out = torch.empty(B, N, Hkv, 1, device=q.device, dtype=q.dtype)
+    _lib.launch("tc_qk_weights", q.device, B, N, Hq, Hkv, Dk, _lib.dtype_code(q.dtype), _lib.ptr(q),
+                                        _lib.ptr(k), _lib.dtype_code(out.dtype), _lib.ptr(out),
+                                        _lib.stream_of(q))
+    return out
+
+
+class _QKWeights(torch.autograd.Function):
+    """compute_summary_weights with its VJP (tc_qk_weights_bwd) as backward:
+    the gradients torch autograd gives the reference's logsumexp."""
+
+    @staticmethod
+    def forward(ctx, q, k, k_dtype):
+        ctx.save_for_backward(q, k)
+        ctx.k_dtype = k_dtype
+        return _qk_weights(q, k)
+
+    @staticmethod
+    def backward(ctx, gw):
+        q, k = ctx.saved_tensors
+        B, N, Hq, Dk = q.shape
+        Hkv = k.shape[2]
+        g = _contig(gw)
+        dq, dk = torch.empty_like(q), torch.empty_like(k)
+        _lib.launch("tc_qk_weights_bwd", q.device, B, N, Hq, Hkv, Dk, _lib.dtype_code(q.dtype),
+                    _lib.ptr(q), _lib.ptr(k), _lib.dtype_code(g.dtype), _lib.ptr(g), _lib.ptr(dq),
+                    _lib.ptr(dk), _lib.stream_of(q))
+        return dq, dk.to(ctx.k_dtype), None
+
+
 def compute_summary_weights(q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
     """w[b, t, hkv] = logsumexp over the KV head's query group of
     q_h . k / sqrt(Dk).  q [B, N, Hq, Dk], k [B, N, Hkv, Dk] -> [B, N, Hkv, 1]
-    in q's dtype (reference.py:117-145)."""
+    in q's dtype (reference.py:117-145); differentiable in q and k."""
     B, N, Hq, Dk = q.shape
     _, Nk, Hkv, Dkk = k.shape
     assert N == Nk
     assert Dk == Dkk
     assert Hq % Hkv == 0
     _lib.require_cuda(q, k)
+    k_dtype = k.dtype
     q, k = _contig(q), _contig(k.to(q.dtype))
-    out = torch.empty(B, N, Hkv, 1, device=q.device, dtype=q.dtype)
-    _lib.launch("tc_qk_weights", q.device, B, N, Hq, Hkv, Dk, _lib.dtype_code(q.dtype), _lib.ptr(q),
-                                        _lib.ptr(k), _lib.dtype_code(out.dtype), _lib.ptr(out),
-                                        _lib.stream_of(q))
-    return out
+    if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad):
+        return _QKWeights.apply(q, k, k_dtype)
+    return _qk_weights(q, k)
 
 
 def compute_linear_weights(x: torch.Tensor, w_proj: torch.Tensor) -> torch.Tensor:
@@ -71,19 +103,62 @@ def _check_conv_weight(weight, C):
         raise ValueError(f"conv kernel size must be positive, got {weight.shape[1]}")
 
 
-def short_conv(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+def _check_seq_idx(seq_idx, B, N, device):
+    """seq_idx [B, N] integer segment ids -> contiguous int32 on device."""
+    if seq_idx is None:
+        return None
+    if not torch.is_tensor(seq_idx) or seq_idx.dtype.is_floating_point or seq_idx.dtype == torch.bool:
+        raise ValueError("seq_idx must be an integer tensor [B, N]")
+    if tuple(seq_idx.shape) != (B, N):
+        raise ValueError(f"seq_idx shape {tuple(seq_idx.shape)} != {(B, N)}")
+    _lib.require_cuda(seq_idx)
+    if seq_idx.device != device:
+        raise ValueError("seq_idx must be on the same device as x")
+    return seq_idx.to(torch.int32).contiguous()
+
+
+def _conv_forward(x, weight, seq):
+    B, N, C = x.shape
+    y = torch.empty_like(x)
+    _lib.launch("tc_short_conv_seg", x.device, B, N, C, _lib.dtype_code(x.dtype), _lib.ptr(x),
+                weight.shape[1], _lib.dtype_code(weight.dtype), _lib.ptr(weight), _lib.ptr(seq),
+                _lib.ptr(y), _lib.stream_of(x))
+    return y
+
+
+class _ShortConv(torch.autograd.Function):
+    """short_conv with its VJP (tc_short_conv_seg_bwd) as backward."""
+
+    @staticmethod
+    def forward(ctx, x, weight, seq):
+        ctx.save_for_backward(x, weight, seq)
+        return _conv_forward(x, weight, seq)
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, weight, seq = ctx.saved_tensors
+        dx, dw = _short_conv_vjp(x, weight, _contig(gy.float()), seq)
+        return dx, dw, None
+
+
+def short_conv(x: torch.Tensor, weight: torch.Tensor, seq_idx: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Causal depthwise conv with an fp32 residual, cast once:
     y[b,t,c] = x[b,t,c] + sum_j weight[c,j] x[b,t-K+1+j,c]
-    (reference.py:167-211).  x [B, N, C], weight [C, K]."""
+    (reference.py:167-211).  x [B, N, C], weight [C, K]; differentiable in x
+    and weight.
+
+    seq_idx (an extension; the reference leaves it as a TODO at
+    reference.py:186-189): optional integer segment ids [B, N] of packed
+    examples; the tap at row s reaches row t only when seq_idx[b, s] ==
+    seq_idx[b, t], so each example's conv starts from zero history."""
     B, N, C = x.shape
     _check_conv_weight(weight, C)
     _lib.require_cuda(x, weight)
     x, weight = _contig(x), _contig(weight)
-    y = torch.empty_like(x)
-    _lib.launch("tc_short_conv", x.device, B, N, C, _lib.dtype_code(x.dtype), _lib.ptr(x),
-                                        weight.shape[1], _lib.dtype_code(weight.dtype),
-                                        _lib.ptr(weight), _lib.ptr(y), _lib.stream_of(x))
-    return y
+    seq = _check_seq_idx(seq_idx, B, N, x.device)
+    if torch.is_grad_enabled() and (x.requires_grad or weight.requires_grad):
+        return _ShortConv.apply(x, weight, seq)
+    return _conv_forward(x, weight, seq)
 
 
 def _build_packed(q, k, v, num_summary_levels, x, w_proj, k_conv_weight, v_conv_weight):
@@ -247,9 +322,10 @@ def build_dyadic_summaries_backward(q, k, v, num_summary_levels, k_packed, v_pac
     return dq_out, dk, dv, dx, dwp, dkcw, dvcw
 
 
-def _short_conv_vjp(x_pre, weight, dy):
+def _short_conv_vjp(x_pre, weight, dy, seq=None):
     """dx (x_pre's dtype) and dweight (weight's dtype) of short_conv for fp32
-    dy [B, N, H, D] (tc_short_conv_bwd)."""
+    dy [B, N, H, D] or [B, N, C] (tc_short_conv_seg_bwd; seq: int32 segment
+    ids [B, N] or None)."""
     B, N = x_pre.shape[:2]
     C = x_pre[0, 0].numel()
     K = weight.shape[1]
@@ -258,9 +334,10 @@ def _short_conv_vjp(x_pre, weight, dy):
     dx = torch.empty_like(xc)
     dw = torch.empty(C, K, device=x_pre.device, dtype=torch.float32)
     parts = torch.empty(max(1, B * ((N + 255) // 256) * C * K), device=x_pre.device, dtype=torch.float32)
-    _lib.launch("tc_short_conv_bwd", x_pre.device,
+    _lib.launch("tc_short_conv_seg_bwd", x_pre.device,
         B, N, C, _lib.dtype_code(xc.dtype), _lib.ptr(xc), K, _lib.dtype_code(wc.dtype), _lib.ptr(wc),
-        _lib.ptr(dy), _lib.ptr(dx), _lib.ptr(dw), _lib.ptr(parts), parts.numel(), _lib.stream_of(xc))
+        _lib.ptr(seq), _lib.ptr(dy), _lib.ptr(dx), _lib.ptr(dw), _lib.ptr(parts), parts.numel(),
+        _lib.stream_of(xc))
     return dx.reshape(x_pre.shape), dw.to(weight.dtype)
 
 
@@ -274,6 +351,7 @@ def build_dyadic_summaries(
     w_proj: Optional[torch.Tensor] = None,
     k_conv_weight: Optional[torch.Tensor] = None,
     v_conv_weight: Optional[torch.Tensor] = None,
+    seq_idx: Optional[torch.Tensor] = None,
 ):
     """The canonical dyadic K/V tree, levels 0..L (reference.py:465-584).
 
@@ -288,7 +366,18 @@ def build_dyadic_summaries(
     the buffers carry the Phase-1 VJP; ``detach_weights`` then cuts the
     gradient through the merge weights (q / k in qk mode, x / w_proj in
     linear mode), as in the reference.
+
+    seq_idx (an extension, see short_conv): segment ids [B, N] of packed
+    examples; the short conv then restarts at each example (it has no
+    effect without conv weights).  The conv runs as its own launch
+    (short_conv) ahead of the builder, with its own VJP under autograd.
     """
+    if seq_idx is not None and k_conv_weight is not None and v_conv_weight is not None:
+        B, N, Hkv, Dk = k.shape
+        Dv = v.shape[-1]
+        k = short_conv(k.reshape(B, N, Hkv * Dk), k_conv_weight, seq_idx).reshape(B, N, Hkv, Dk)
+        v = short_conv(v.reshape(B, N, Hkv * Dv), v_conv_weight, seq_idx).reshape(B, N, Hkv, Dv)
+        k_conv_weight = v_conv_weight = None
     inputs = (q, k, v, x, w_proj, k_conv_weight, v_conv_weight)
     if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in inputs):
         kp, vp, wp = _DyadicTree.apply(q, k, v, x, w_proj, k_conv_weight, v_conv_weight,
