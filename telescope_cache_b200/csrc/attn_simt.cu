@@ -388,6 +388,9 @@ __global__ void __launch_bounds__(NT) bwd_dkv_simt(AttnParams p, TileMap tm) {
   int qlo, qhi;
   bwd_hull(k0, k0 + nk, lev, p.s, &qlo, &qhi);
   for (int qb = (qlo / BM) * BM; qlo < qhi && qb < qhi; qb += BM) {
+    // warps leave a block's last phase 1 at different times (only __syncwarp
+    // follows it): the bounds of the next block wait for every reader
+    __syncthreads();
     for (int r = tid; r < BM; r += NT) {
       int lo[LV], hi[LV];
       const int q = qb + r;
