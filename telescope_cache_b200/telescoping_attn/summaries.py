@@ -42,9 +42,8 @@ class _QKWeights(torch.autograd.Function):
     the gradients torch autograd gives the reference's logsumexp."""
 
     @staticmethod
-    def forward(ctx, q, k, k_dtype):
+    def forward(ctx, q, k):
         ctx.save_for_backward(q, k)
-        ctx.k_dtype = k_dtype
         return _qk_weights(q, k)
 
     @staticmethod
@@ -57,7 +56,7 @@ class _QKWeights(torch.autograd.Function):
         _lib.launch("tc_qk_weights_bwd", q.device, B, N, Hq, Hkv, Dk, _lib.dtype_code(q.dtype),
                     _lib.ptr(q), _lib.ptr(k), _lib.dtype_code(g.dtype), _lib.ptr(g), _lib.ptr(dq),
                     _lib.ptr(dk), _lib.stream_of(q))
-        return dq, dk.to(ctx.k_dtype), None
+        return dq, dk
 
 
 def compute_summary_weights(q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
@@ -70,10 +69,10 @@ def compute_summary_weights(q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
     assert Dk == Dkk
     assert Hq % Hkv == 0
     _lib.require_cuda(q, k)
-    k_dtype = k.dtype
+    # k in q's type (the cast carries its own gradient back to k's type)
     q, k = _contig(q), _contig(k.to(q.dtype))
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad):
-        return _QKWeights.apply(q, k, k_dtype)
+        return _QKWeights.apply(q, k)
     return _qk_weights(q, k)
 
 
