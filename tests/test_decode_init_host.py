@@ -91,3 +91,27 @@ def test_mismatched_level_raises_before_launch(bad):
         wl[2] = torch.zeros(2, n >> 2, 3, 1)
     with pytest.raises(ValueError, match="shape"):
         T.init_decode_state(kl, vl, wl, fmap, cache)
+
+
+def test_conv_history_segments():
+    """The hand-off's conv history (last K-1 pre-conv rows, zero-padded on the
+    left) with segment ids: rows of an earlier packed example than the last
+    row's are zeroed; without ids, or with one example, it is the plain tail."""
+    import torch
+
+    from telescope_cache_b200.telescoping_attn.decode_state import _conv_history
+
+    x = torch.arange(2 * 6 * 3, dtype=torch.float32).reshape(2, 6, 3) + 1
+    seq = torch.tensor([[0, 0, 0, 1, 1, 1], [0, 0, 0, 0, 2, 2]])
+    h = _conv_history(x, 4, seq)
+    assert torch.equal(h[0], x[0, 3:])                       # the last example covers all K-1 rows
+    assert torch.equal(h[1, 0], torch.zeros(3)) and torch.equal(h[1, 1:], x[1, 4:])
+    assert torch.equal(_conv_history(x, 4), x[:, 3:])
+    assert torch.equal(_conv_history(x, 4, torch.zeros(2, 6, dtype=torch.long)), x[:, 3:])
+    # shorter prefill than K-1: left zero padding, then the segment rule
+    short = _conv_history(x[:, :2], 4, seq[:, :2])
+    assert short.shape == (2, 3, 3) and torch.equal(short[:, 0], torch.zeros(2, 3))
+    assert torch.equal(short[:, 1:], x[:, :2])
+    # a history is a copy: updating it leaves the prefill rows alone
+    h[0, 0, 0] = -1.0
+    assert x[0, 3, 0] != -1.0
