@@ -44,3 +44,17 @@ def test_rejected_arguments():
         MultiHeadAttention(32, 16, 16, 4, 2, position_mode="alibi")
     with pytest.raises(ValueError):
         ShortConv1d(8, 0)
+
+
+def test_rope_tables_are_kept_and_grown_by_doubling():
+    """Decode steps reuse one table (the rotated ring stays current); a longer
+    sequence doubles it, and the rows already there do not change."""
+    m = MultiHeadAttention(32, 16, 16, 4, 2, position_mode="rope")
+    cpu = torch.device("cpu")
+    c1, s1 = m._rope_tables(100, cpu)
+    c2, _ = m._rope_tables(60, cpu)
+    assert c2 is c1 and c1.shape == (100, 8)
+    c3, s3 = m._rope_tables(101, cpu)
+    assert c3.shape == (200, 8) and torch.equal(c3[:100], c1) and torch.equal(s3[:100], s1)
+    c4, _ = m._rope_tables(450, cpu)
+    assert c4.shape == (450, 8)
